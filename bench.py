@@ -1,0 +1,370 @@
+"""Benchmark of the B200 LCSA hot path (block selection + block-sparse attention), one JSON line on rank 0.
+
+Metric: block-sparse attention effective TFLOP/s — 4·128³ FLOP per kept (query block, key block,
+head) triple, over the whole path's device time (pooling + selection + attention) — plus ms per 30-layer chunk.
+Workload at N=1: config 3 (1920×1152 chunk: 12 heads, 135 × 405 blocks, R = 11, keep 30 %), a step = one chunk =
+30 layer calls, each on fresh seeded Q/K/V resident in HBM (371 MB per layer, larger than L2, so no flush is needed).
+N > 1 (torchrun, one process per GPU): independent config-3 streams, one per GPU (config 5's throughput variant);
+no data-path collective, weak scaling, time = max over ranks.
+
+--impl reference: the CPU baseline arm — the reference's Swift/MLX path cannot run off Apple hardware, so this times
+the CPU oracle (a C/OpenMP restatement of the reference's selection and block-masked attention) on all host threads,
+on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+
+def load_pkg():
+    from __graft_entry__ import _load_package
+    pkg = _load_package()
+    pkg.build()
+    import importlib
+    return pkg, importlib.import_module("fvsr_b200.configs")
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / "attn_bf16_config3_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_uuid: str | None):
+        self.proc = None
+        self.uuid = device_uuid
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.uuid:
+            cmd += ["-i", self.uuid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxs.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxs) if maxs else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# CPU baseline (oracle port, all host threads, bounded sample)
+# ---------------------------------------------------------------------------------------------------------------
+def cpu_baseline(cfg_id: int = 3, heads_sample: int = 12, seed: int = 3000):
+    import numpy as np
+    from oracle import oracle as orc
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import detrand
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[cfg_id]
+    g = cfg.geometry()
+    threads = os.cpu_count() or 1
+    orc.set_num_threads(threads)
+    c = g.channels
+    q = detrand.normal(seed, (g.nq * 128, c))
+    k = detrand.normal(seed + 1, (g.nk * 128, c))
+    v = detrand.normal(seed + 2, (g.nk * 128, c))
+    loc = orc.local_block_mask(g.bh, g.bw, g.local_range)
+    t0 = time.perf_counter()
+    pq, pk = orc.pool(q), orc.pool(k)
+    probs, mask, kidx, kcnt = orc.select(pq, pk, g.heads, g.q_slices, g.s, loc, g.topk)
+    t_sel = time.perf_counter() - t0
+    items = np.arange(heads_sample * g.nq, dtype=np.int32)           # every query block of the first heads
+    t0 = time.perf_counter()
+    orc.attention(q, k, v, kidx, kcnt, g.heads, items=items, fast=True)
+    t_att = time.perf_counter() - t0
+    kept = int(kcnt[:heads_sample].sum())
+    frac = heads_sample / g.heads
+    secs = t_sel * frac + t_att                                        # selection prorated to the sampled heads
+    flops = 4.0 * 128 ** 3 * kept
+    return {"value": flops / secs / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"config {cfg_id}, one layer: full pooling + selection (prorated to {heads_sample}/{g.heads} "
+                      f"heads) + fp32 attention over all query blocks of {heads_sample} head(s) ({kept} kept triples); "
+                      f"{secs:.2f} s", "seconds": secs, "kept_triples": kept}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    _, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[3]
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(3, seed=3000 + i)
+        if i >= args.warmup:
+            vals.append(r)
+    v = statistics.median(x["value"] for x in vals)
+    line = {
+        "impl": "reference", "metric": "block-sparse attn effective TFLOP/s (config 3, 1920x1152 chunk)", "value": v,
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.median(x["seconds"] for x in vals) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded normal, window order)",
+        "config": {"workload": cfg.name, "sample": vals[-1]["sample"]},
+        "cpu_baseline": {k: vals[-1][k] for k in ("kind", "cores", "sample")} | {"value": v, "unit": "TFLOP/s"},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own path is Swift/MLX on Apple GPUs (unavailable on this box); this arm is the CPU "
+                "oracle restating it",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[args.config]
+    g = cfg.geometry()
+    layers = args.layers
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+
+    # inputs: one fresh seeded (q, k, v) per layer, resident in HBM
+    inputs = [cfgs.synth_qkv(cfg, g, cfgs.seed_of(args.config, rank, l), device=dev) for l in range(layers)]
+    ws = pkg.make_workspace(g, dev)
+    kidx = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device=dev)
+    kcnt = torch.empty((g.heads, g.nq), dtype=torch.int32, device=dev)
+    outs = [torch.empty_like(inputs[0][0]) for _ in range(2)]
+    kept = []
+
+    import ctypes
+    L = pkg.lib()
+    p = g.params()
+
+    def layer_call(l, out):
+        """One layer through the C ABI: fvsr_lcsa_select (pool Q, pool K, scores + softmax, threshold + lists),
+        then fvsr_lcsa_attention."""
+        q, k, v = inputs[l]
+        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx), pkg._ptr(kcnt),
+                                      None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+        pkg._check(L.fvsr_lcsa_attention(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v), pkg._ptr(kidx),
+                                         pkg._ptr(kcnt), pkg._ptr(out), pkg._stream()))
+
+    def step():
+        for l in range(layers):
+            layer_call(l, outs[l & 1])
+
+    # kept triples per layer (deterministic given the inputs; read once, outside the timed region)
+    for l in range(layers):
+        layer_call(l, outs[0])
+        kept.append(int(kcnt.sum().item()))
+    flops_per_step = 4.0 * 128 ** 3 * sum(kept)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = Clocks(uuid)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    pkg.device_check()
+
+    # dominant kernel: the bf16 attention alone, CUDA events on the launching stream, over all layers
+    att_ms = []
+    for l in range(layers):
+        q, k, v = inputs[l]
+        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx), pkg._ptr(kcnt),
+                                      None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        pkg._check(L.fvsr_lcsa_attention(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v), pkg._ptr(kidx),
+                                         pkg._ptr(kcnt), pkg._ptr(outs[0]), pkg._stream()))
+        a1.record(stream)
+        a1.synchronize()
+        att_ms.append(a0.elapsed_time(a1))
+    att_avg = sum(att_ms) / len(att_ms)
+    att_tflops = 4.0 * 128 ** 3 * (sum(kept) / layers) / (att_avg * 1e-3) / 1e12
+    sel_ms = ms / layers - att_avg
+
+    # end to end through the C ABI with host buffers: per layer H2D of q/k/v from pinned memory, select + attention,
+    # D2H of the output; copies of layer l+1 overlap compute of layer l on a second stream
+    e2e = None
+    if args.e2e_steps > 0:
+        nbuf = 3
+        host = [tuple(t.cpu().pin_memory() for t in inputs[l]) for l in range(nbuf)]
+        dbuf = [tuple(torch.empty_like(t) for t in inputs[0]) for _ in range(2)]
+        hout = [torch.empty(inputs[0][0].shape, dtype=inputs[0][0].dtype, pin_memory=True) for _ in range(2)]
+        cp = torch.cuda.Stream(device=dev)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        h2d = sum(t.numel() * t.element_size() for t in host[0]) * layers
+        d2h = outs[0].numel() * outs[0].element_size() * layers
+
+        def e2e_step():
+            for l in range(layers):
+                b = l & 1
+                with torch.cuda.stream(cp):
+                    cp.wait_event(free[b])
+                    for dst, src in zip(dbuf[b], host[l % nbuf]):
+                        dst.copy_(src, non_blocking=True)
+                    ready[b].record(cp)
+                stream.wait_event(ready[b])
+                q, k, v = dbuf[b]
+                pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx),
+                                              pkg._ptr(kcnt), None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+                pkg._check(L.fvsr_lcsa_attention(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
+                                                 pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(outs[b]), pkg._stream()))
+                free[b].record(stream)
+                hout[b].copy_(outs[b], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        e2e_step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = f0.elapsed_time(f1) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * flops_per_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+
+    if rank == 0:
+        peak, hbm, peak_kind = peaks()
+        tr = profiled_traffic()
+        value = world * flops_per_step / (ms * 1e-3) / 1e12
+        line = {
+            "metric": "block-sparse attn effective TFLOP/s (+ ms per 30-layer chunk), config 3 1920x1152",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded normal Q/K/V per layer, window order, resident in HBM)",
+            "config": {"workload": f"config {args.config}: {cfg.name}", "layers_per_step": layers,
+                       "heads": g.heads, "q_blocks": g.nq, "k_blocks": g.nk, "topk": g.topk,
+                       "kept_triples_per_layer": sum(kept) / layers, "l2": "inputs > L2 (371 MB per layer), no flush",
+                       "parallelism": f"{world} independent streams" if world > 1 else "1 GPU"},
+            "ms_per_layer": ms / layers,
+            "breakdown_ms_per_layer": {"attention": att_avg, "pool+select": sel_ms},
+            "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
+                         "unit": "TFLOP/s", "frac": att_tflops / peak, "peak_kind": f"{peak_kind} bf16 burst",
+                         "traffic": (tr or {}).get("bytes_per_launch"),
+                         "traffic_source": (tr or {}).get("source")},
+            "clocks": clk,
+            "gpu_launches": 5 * layers * args.steps,
+            "e2e": e2e,
+        }
+        if not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline(args.config)
+                line["cpu_baseline"].pop("seconds", None)
+            except Exception as exc:  # the baseline is reported, never required
+                line["cpu_baseline"] = {"error": str(exc)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+/*
+ * fvsr_lcsa.h — C ABI of the B200 (sm_100a) LCSA hot path: FlashVSR's locality-constrained block-sparse
+ * self-attention (block selection + block-sparse flash attention over a streaming window KV cache).
+ *
+ * Drop-in boundary. The Swift DiT of xocialize/mlx-flashvsr-swift calls two functions per layer per chunk:
+ *   draftBlockMaskAndProbs(qW:kW:heads:qSlices:spatialBlocks:local:topk:)   Sources/FlashVSRMLX/DiT.swift:158-174
+ *   kernelBlockAttention(q:k:v:blockMask:heads:simdgroups:)                 Sources/FlashVSRMLX/SparseAttention.swift:169-187
+ * and keeps the window K/V cache in blockForward (DiT.swift:507-511, 532-538). The entry points below replace those
+ * with device-resident calls on plain pointers; a thin Swift shim binds them (the binding is shown in INTEGRATION.md).
+ *
+ * Tensor layout (identical to the Swift side): window-ordered tokens, row-major (L, H·128). Token t of window w is
+ * row w·128 + t; head h owns columns [h·128, h·128 + 128). Query block i = window i of the chunk; key block j =
+ * window j of (cache ⊕ current), oldest slice first. bf16 or fp32 storage (params.dtype).
+ *
+ * Conventions:
+ *   - All pointers are device pointers unless stated; the caller owns every buffer.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = the legacy default stream) and never
+ *     synchronises, except where noted.
+ *   - No call allocates device memory except fvsr_kv_cache_create. Scratch comes from a caller-provided workspace
+ *     whose size fvsr_lcsa_workspace_size reports.
+ *   - Errors are returned, never trapped: FVSR_EINVAL for bad shapes / NULL pointers (checked on the host before any
+ *     launch), FVSR_ECUDA for a failed launch, FVSR_ETIMEOUT when a device-side wait gave up (reported by
+ *     fvsr_device_check). fvsr_last_error() returns a message for the calling thread's last failure.
+ *   - Thread-safe across distinct streams and distinct cache handles; one cache handle is used by one stream.
+ */
+#ifndef FVSR_LCSA_H
+#define FVSR_LCSA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* fvsr_stream_t; /* a cudaStream_t */
+
+typedef enum fvsr_status {
+    FVSR_OK = 0,
+    FVSR_EINVAL = 1,      /* bad argument (shape, NULL pointer, misaligned pointer) */
+    FVSR_ECUDA = 2,       /* a CUDA runtime call or kernel launch failed */
+    FVSR_ETIMEOUT = 3,    /* a device-side wait hit its iteration limit and the kernel returned early */
+    FVSR_ENOMEM = 4,      /* workspace too small, or cache allocation failed */
+    FVSR_EUNSUPPORTED = 5 /* a size beyond the kernels' limits, or no sm_100 device */
+} fvsr_status;
+
+typedef enum fvsr_dtype { FVSR_F32 = 0, FVSR_BF16 = 1 } fvsr_dtype;
+
+/* One LCSA call's geometry. Mirrors the Swift StepGeometry fields the path reads (DiT.swift:473-485). */
+typedef struct fvsr_lcsa_params {
+    int32_t heads;       /* H — FlashVSR: 12 */
+    int32_t head_dim;    /* must be 128 (SparseAttention.swift:173) */
+    int32_t bh, bw;      /* spatial block grid of one temporal slice (latent h/8, w/8 on the patch grid); s = bh·bw */
+    int32_t q_slices;    /* temporal slices in the query chunk (StepGeometry.seqlen = f/2); Nq = q_slices·s */
+    int32_t kv_slices;   /* temporal slices of keys, cache ⊕ current; Nk = kv_slices·s */
+    int32_t local_range; /* R of localBlockMask (DiT.swift:130-145), ≥ 1 */
+    int32_t topk;        /* integer top-k (DiT.swift:482), ≥ 0; keeps p > the (min(n−1, topk)+1)-th largest */
+    int32_t dtype;       /* fvsr_dtype of q, k, v and out */
+} fvsr_lcsa_params;
+
+/* Library / error reporting. */
+int32_t fvsr_version(void);
+const char* fvsr_status_string(fvsr_status s);
+const char* fvsr_last_error(void);
+
+/* Synchronises `stream`, then reports (and clears) a device-side wait timeout recorded by any kernel of this library
+ * on the current device: FVSR_ETIMEOUT if one was recorded, else FVSR_OK. No reference counterpart (the reference's
+ * Metal kernel has no waits); this is the host side of the library's bounded device waits. */
+fvsr_status fvsr_device_check(fvsr_stream_t stream);
+
+/* Bytes of workspace that fvsr_lcsa_select, fvsr_lcsa_attention_mask and fvsr_lcsa_forward need for `p`
+ * (the maximum of the three). */
+fvsr_status fvsr_lcsa_workspace_size(const fvsr_lcsa_params* p, size_t* bytes);
+
+/* fp32 mean over each 128-token block: x (nblocks·128, H·128) in p->dtype → pooled (nblocks, H·128) fp32.
+ * Replaces qW.asType(.float32).mean(axis: 1) (DiT.swift:161-162). Summation order: four sequential partial sums over
+ * tokens [0,32) [32,64) [64,96) [96,128), combined (s0+s1)+(s2+s3), times 1/128. */
+fvsr_status fvsr_lcsa_pool(const fvsr_lcsa_params* p, const void* x, int64_t nblocks, float* pooled,
+                           fvsr_stream_t stream);
+
+/* Block selection — replaces draftBlockMaskAndProbs (DiT.swift:158-174).
+ *   q (Nq·128, H·128), k (Nk·128, H·128) in p->dtype, window order. If pooled_k is non-NULL it holds the pooled keys
+ *   (Nk, H·128) fp32 and k is not read (may be NULL) — the streaming cache keeps pooled keys per slice.
+ *   Outputs: kidx (H, Nq, Nk) int32 — the kept key blocks of each (head, query block) first, ascending, the rest −1;
+ *            kcnt (H, Nq) int32; mask (H, Nq, Nk) uint8 0/1 (optional, NULL to skip);
+ *            probs (H, Nq, Nk) fp32 softmaxed block probabilities (optional).
+ *   The top-k threshold is joint over each (head, query temporal slice) row, strict '>' (DiT.swift:169-173). */
+fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const void* k, const float* pooled_k,
+                             int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs, void* workspace,
+                             size_t workspace_bytes, fvsr_stream_t stream);
+
+/* Block-sparse attention over the kept pairs — replaces kernelBlockAttention (SparseAttention.swift:169-187) fed with
+ * index lists. q (Nq·128, H·128), k / v (Nk·128, H·128), out (Nq·128, H·128), all p->dtype; kidx / kcnt as produced by
+ * fvsr_lcsa_select. Scale 1/sqrt(128). A query block with kcnt = 0 writes zeros (SparseAttention.swift:47-53).
+ * bf16 runs the tcgen05/TMEM tensor-core kernel; fp32 runs an fp32 CUDA-core kernel. */
+fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                const int32_t* kidx, const int32_t* kcnt, void* out, fvsr_stream_t stream);
+
+/* kernelBlockAttention with the reference's own argument form (SparseAttention.swift:169-177): block_mask
+ * (H, Nq, Nk) fp32, kept where > 0.5. Builds the index lists in `workspace`, then runs fvsr_lcsa_attention. */
+fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                     const float* block_mask, void* out, void* workspace, size_t workspace_bytes,
+                                     fvsr_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------------------ */
+/* Streaming window KV cache — replaces the cacheK / cacheV arrays of blockForward (DiT.swift:507-511, 532-538).   */
+/* Keys/values live in slice pages of one device arena (one page = s·128 tokens × H·128), appended in place; the   */
+/* logical order (oldest first) is a page table, so eviction moves no data. Pooled keys are kept per page.         */
+/* ------------------------------------------------------------------------------------------------------------ */
+
+typedef struct fvsr_kv_cache fvsr_kv_cache;
+
+/* Allocates a cache for geometry p (heads, bh, bw, dtype are used) holding up to kv_len + max_new_slices pages.
+ * kv_len = the reference's kvLen = Int(kvRatio) (Pipeline.swift:129). Not a hot call: it is the one allocating entry. */
+fvsr_status fvsr_kv_cache_create(const fvsr_lcsa_params* p, int32_t kv_len, int32_t max_new_slices,
+                                 fvsr_kv_cache** cache);
+fvsr_status fvsr_kv_cache_destroy(fvsr_kv_cache* cache);
+/* Forget every slice (a new clip). Host-side only. */
+fvsr_status fvsr_kv_cache_reset(fvsr_kv_cache* cache);
+/* Number of slices currently held. */
+fvsr_status fvsr_kv_cache_slices(const fvsr_kv_cache* cache, int32_t* slices);
+/* Append new_slices slices of keys/values (new_slices·s·128, H·128) in p->dtype: copies them into free pages and
+ * pools the keys (the concat of DiT.swift:508-511). */
+fvsr_status fvsr_kv_cache_append(fvsr_kv_cache* cache, const void* k_new, const void* v_new, int32_t new_slices,
+                                 fvsr_stream_t stream);
+/* DiT.swift:532-538: if more than kv_len slices are held, drop the oldest one. Host-side only. */
+fvsr_status fvsr_kv_cache_trim(fvsr_kv_cache* cache);
+/* Copy the logical (cache order) keys and values into k_out / v_out (slices·s·128, H·128). For checks and export. */
+fvsr_status fvsr_kv_cache_gather(const fvsr_kv_cache* cache, void* k_out, void* v_out, fvsr_stream_t stream);
+/* Slot table for save/restore: pages[i] = arena page of logical slice i, for i < *slices (pages has room for
+ * kv_len + max_new_slices entries). */
+fvsr_status fvsr_kv_cache_state(const fvsr_kv_cache* cache, int32_t* pages, int32_t* slices);
+
+/* One layer of LCSA in streaming mode — the self-attention core of blockForward (DiT.swift:504-538):
+ * append (k_new, v_new) to the cache, select over cache ⊕ current with q, attend, then trim.
+ * p->q_slices gives the chunk's slices (k_new / v_new hold q_slices·s·128 rows); p->kv_slices is ignored (taken from
+ * the cache after the append). kidx / kcnt are optional outputs (NULL → kept in the workspace). */
+fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const void* k_new, const void* v_new,
+                              fvsr_kv_cache* cache, void* out, int32_t* kidx, int32_t* kcnt, void* workspace,
+                              size_t workspace_bytes, fvsr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FVSR_LCSA_H */

@@ -1,0 +1,352 @@
+"""B200-native LCSA hot path of FlashVSR — the host-side mirror of the reference's operator interface.
+
+The reference (xocialize/mlx-flashvsr-swift) exposes the path as Swift functions on MLXArrays:
+    draftBlockMaskAndProbs(qW:kW:heads:qSlices:spatialBlocks:local:topk:)   Sources/FlashVSRMLX/DiT.swift:158-174
+    kernelBlockAttention(q:k:v:blockMask:heads:simdgroups:)                 Sources/FlashVSRMLX/SparseAttention.swift:169-187
+    FlashVSRAttentionOps.kernel(q:k:v:blockMask:heads:)                     Sources/FlashVSRMLX/SparseAttention.swift:190-201
+    the window K/V cache of blockForward                                    Sources/FlashVSRMLX/DiT.swift:507-511, 532-538
+This module offers the same operations, with the same argument meaning, on CUDA torch tensors, by calling the C ABI of
+``include/fvsr_lcsa.h`` (``libfvsr_lcsa.so``, hand-written sm_100a kernels) through ctypes. torch is used only for
+device memory and the current stream. There is no fallback: if the library is missing, importing this package fails.
+
+Where the reference traps on a bad shape (``precondition``), these functions raise ``FVSRError`` carrying the C
+status and message.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libfvsr_lcsa.so"
+
+FVSR_OK, FVSR_EINVAL, FVSR_ECUDA, FVSR_ETIMEOUT, FVSR_ENOMEM, FVSR_EUNSUPPORTED = range(6)
+FVSR_F32, FVSR_BF16 = 0, 1
+
+EXPORTED = [
+    "fvsr_version", "fvsr_status_string", "fvsr_last_error", "fvsr_device_check", "fvsr_lcsa_workspace_size",
+    "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
+    "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
+    "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
+]
+
+
+class Params(ctypes.Structure):
+    """struct fvsr_lcsa_params."""
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("heads", "head_dim", "bh", "bw", "q_slices", "kv_slices", "local_range", "topk", "dtype")]
+
+
+class FVSRError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"fvsr status {status}: {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile libfvsr_lcsa.so in-tree (nvcc, sm_100a)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("fvsr_b200_build", PKG_DIR / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build(force=force)
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C ABI. Raises if the library has not been built — the CUDA path is the only path."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is not built; run build() (nvcc, sm_100a) first")
+    L = ctypes.CDLL(str(LIB_PATH))
+    P, I32, I64, SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+    PP = ctypes.POINTER(Params)
+    sigs = {
+        "fvsr_version": ([], I32),
+        "fvsr_status_string": ([ctypes.c_int], ctypes.c_char_p),
+        "fvsr_last_error": ([], ctypes.c_char_p),
+        "fvsr_device_check": ([P], ctypes.c_int),
+        "fvsr_lcsa_workspace_size": ([PP, ctypes.POINTER(SZ)], ctypes.c_int),
+        "fvsr_lcsa_pool": ([PP, P, I64, P, P], ctypes.c_int),
+        "fvsr_lcsa_select": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_attention": ([PP, P, P, P, P, P, P, P], ctypes.c_int),
+        "fvsr_lcsa_attention_mask": ([PP, P, P, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_kv_cache_create": ([PP, I32, I32, ctypes.POINTER(P)], ctypes.c_int),
+        "fvsr_kv_cache_destroy": ([P], ctypes.c_int),
+        "fvsr_kv_cache_reset": ([P], ctypes.c_int),
+        "fvsr_kv_cache_slices": ([P, ctypes.POINTER(I32)], ctypes.c_int),
+        "fvsr_kv_cache_append": ([P, P, P, I32, P], ctypes.c_int),
+        "fvsr_kv_cache_trim": ([P], ctypes.c_int),
+        "fvsr_kv_cache_gather": ([P, P, P, P], ctypes.c_int),
+        "fvsr_kv_cache_state": ([P, P, ctypes.POINTER(I32)], ctypes.c_int),
+        "fvsr_lcsa_forward": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def _check(status: int) -> None:
+    if status != FVSR_OK:
+        raise FVSRError(status, lib().fvsr_last_error().decode())
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Geometry (DiT.swift:473-485)
+# ---------------------------------------------------------------------------------------------------------------
+
+@dataclass
+class Geometry:
+    """One LCSA call's geometry: ``s = bh·bw`` spatial blocks per temporal slice, ``Nq = q_slices·s`` query blocks,
+    ``Nk = kv_slices·s`` key blocks (cache ⊕ current), locality range R and the integer top-k."""
+    heads: int
+    bh: int
+    bw: int
+    q_slices: int
+    kv_slices: int
+    local_range: int = 11
+    topk: int = 0
+    dtype: int = FVSR_BF16
+
+    @property
+    def s(self) -> int:
+        return self.bh * self.bw
+
+    @property
+    def nq(self) -> int:
+        return self.q_slices * self.s
+
+    @property
+    def nk(self) -> int:
+        return self.kv_slices * self.s
+
+    @property
+    def channels(self) -> int:
+        return self.heads * 128
+
+    def params(self) -> Params:
+        return Params(self.heads, 128, self.bh, self.bw, self.q_slices, self.kv_slices, self.local_range, self.topk,
+                      self.dtype)
+
+    def allowed_per_row(self) -> int:
+        """Locality-allowed (query block, key block) pairs in one (head, slice) selection row."""
+        half = self.local_range // 2
+        tot = 0
+        for qr in range(self.bh):
+            nr = sum(1 for kr in range(self.bh) if qr - half <= kr <= qr - half + self.local_range - 1)
+            for qc in range(self.bw):
+                nc = sum(1 for kc in range(self.bw) if qc - half <= kc <= qc - half + self.local_range - 1)
+                tot += nr * nc
+        return tot * self.kv_slices
+
+    @staticmethod
+    def topk_from_ratio(s: int, ratio: float) -> int:
+        """DiT.swift:482: topk = Int(Double(s·s)·topkRatio) − 1."""
+        return int(float(s * s) * ratio) - 1
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dtype_code(t) -> int:
+    torch = _torch()
+    if t.dtype == torch.bfloat16:
+        return FVSR_BF16
+    if t.dtype == torch.float32:
+        return FVSR_F32
+    raise FVSRError(FVSR_EINVAL, f"tensors must be bfloat16 or float32, got {t.dtype}")
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _rows(t):
+    """(1, L, C) or (L, C) → (L, C) view (the reference's batch-1 contract, SparseAttention.swift:173)."""
+    if t.dim() == 3:
+        if t.shape[0] != 1:
+            raise FVSRError(FVSR_EINVAL, "batch must be 1")
+        t = t[0]
+    if not t.is_cuda or not t.is_contiguous():
+        raise FVSRError(FVSR_EINVAL, "tensors must be contiguous CUDA tensors")
+    return t
+
+
+def workspace_size(geom: Geometry) -> int:
+    n = ctypes.c_size_t(0)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_workspace_size(ctypes.byref(p), ctypes.byref(n)))
+    return int(n.value)
+
+
+def make_workspace(geom: Geometry, device=None):
+    torch = _torch()
+    return torch.empty(workspace_size(geom), dtype=torch.uint8, device=device or "cuda")
+
+
+def pool(x, geom: Geometry, out=None, stream=None):
+    """fp32 block means (DiT.swift:161-162): x (N·128, H·128) → (N, H·128) fp32."""
+    torch = _torch()
+    x = _rows(x)
+    nblocks = x.shape[0] // 128
+    if out is None:
+        out = torch.empty((nblocks, x.shape[1]), dtype=torch.float32, device=x.device)
+    g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(x)})
+    p = g.params()
+    _check(lib().fvsr_lcsa_pool(ctypes.byref(p), _ptr(x), nblocks, _ptr(out), _stream(stream)))
+    return out
+
+
+def draft_block_mask_and_probs(qW, kW, geom: Geometry, pooled_k=None, want_mask: bool = True,
+                               want_probs: bool = True, workspace=None, stream=None):
+    """draftBlockMaskAndProbs (DiT.swift:158-174). qW (Nq·128, H·128), kW (Nk·128, H·128) window order.
+    Returns dict(mask (H,Nq,Nk) uint8, probs (H,Nq,Nk) f32, kidx (H,Nq,Nk) i32 kept-first ascending, kcnt (H,Nq))."""
+    torch = _torch()
+    q = _rows(qW)
+    k = None if kW is None else _rows(kW)
+    g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(q)})
+    dev = q.device
+    kidx = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device=dev)
+    kcnt = torch.empty((g.heads, g.nq), dtype=torch.int32, device=dev)
+    mask = torch.empty((g.heads, g.nq, g.nk), dtype=torch.uint8, device=dev) if want_mask else None
+    probs = torch.empty((g.heads, g.nq, g.nk), dtype=torch.float32, device=dev) if want_probs else None
+    ws = workspace if workspace is not None else make_workspace(g, dev)
+    p = g.params()
+    _check(lib().fvsr_lcsa_select(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(pooled_k), _ptr(kidx), _ptr(kcnt),
+                                  _ptr(mask), _ptr(probs), _ptr(ws), ws.numel(), _stream(stream)))
+    return {"mask": mask, "probs": probs, "kidx": kidx, "kcnt": kcnt}
+
+
+def block_sparse_attention(q, k, v, kidx, kcnt, geom: Geometry, out=None, stream=None):
+    """Attention over the kept blocks given index lists. q (Nq·128, H·128), k / v (Nk·128, H·128)."""
+    torch = _torch()
+    shape = q.shape
+    q2, k2, v2 = _rows(q), _rows(k), _rows(v)
+    g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(q2)})
+    if out is None:
+        out = torch.empty_like(q2)
+    p = g.params()
+    _check(lib().fvsr_lcsa_attention(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
+                                     _ptr(out), _stream(stream)))
+    return out.reshape(shape)
+
+
+def kernel_block_attention(q, k, v, block_mask, heads: int, workspace=None, stream=None):
+    """kernelBlockAttention(q:k:v:blockMask:heads:) (SparseAttention.swift:169-187). q (1, Lq, H·128), k / v
+    (1, Lk, H·128) window order, block_mask (H, Nq, Nk) 0/1 (kept where > 0.5). Returns (1, Lq, H·128)."""
+    torch = _torch()
+    shape = q.shape
+    q2, k2, v2 = _rows(q), _rows(k), _rows(v)
+    if q2.shape[1] != heads * 128:
+        raise FVSRError(FVSR_EINVAL, "kernel attention: batch 1, head dim 128")
+    nq, nk = block_mask.shape[1], block_mask.shape[2]
+    g = Geometry(heads=heads, bh=1, bw=1, q_slices=nq, kv_slices=nk, local_range=1, topk=0, dtype=_dtype_code(q2))
+    bm = block_mask.to(torch.float32).contiguous()
+    out = torch.empty_like(q2)
+    ws = workspace if workspace is not None else make_workspace(g, q2.device)
+    p = g.params()
+    _check(lib().fvsr_lcsa_attention_mask(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(bm), _ptr(out),
+                                          _ptr(ws), ws.numel(), _stream(stream)))
+    return out.reshape(shape)
+
+
+class FlashVSRAttentionOps:
+    """Public entry points of SparseAttention.swift:190-201. Only the kernel lane exists on B200: the dense and
+    gathered lanes are the reference's CPU / study paths, restated by the test oracle, not the product."""
+
+    @staticmethod
+    def kernel(q, k, v, block_mask, heads: int):
+        return kernel_block_attention(q, k, v, block_mask, heads)
+
+
+class KVCache:
+    """The window K/V cache of blockForward (DiT.swift:507-511, 532-538) as slice pages appended in place."""
+
+    def __init__(self, geom: Geometry, kv_len: int, max_new_slices: int):
+        self.geom = geom
+        self.kv_len = kv_len
+        self.capacity = kv_len + max_new_slices
+        h = ctypes.c_void_p()
+        p = geom.params()
+        _check(lib().fvsr_kv_cache_create(ctypes.byref(p), kv_len, max_new_slices, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            lib().fvsr_kv_cache_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        _check(lib().fvsr_kv_cache_reset(self.handle))
+
+    @property
+    def slices(self) -> int:
+        n = ctypes.c_int32(0)
+        _check(lib().fvsr_kv_cache_slices(self.handle, ctypes.byref(n)))
+        return int(n.value)
+
+    def append(self, k_new, v_new, new_slices: int, stream=None):
+        _check(lib().fvsr_kv_cache_append(self.handle, _ptr(_rows(k_new)), _ptr(_rows(v_new)), new_slices,
+                                          _stream(stream)))
+
+    def trim(self):
+        _check(lib().fvsr_kv_cache_trim(self.handle))
+
+    def state(self) -> list[int]:
+        n = ctypes.c_int32(0)
+        buf = (ctypes.c_int32 * self.capacity)()
+        _check(lib().fvsr_kv_cache_state(self.handle, buf, ctypes.byref(n)))
+        return list(buf[: n.value])
+
+    def gather(self, stream=None):
+        torch = _torch()
+        n = self.slices
+        rows = n * self.geom.s * 128
+        dt = torch.bfloat16 if self.geom.dtype == FVSR_BF16 else torch.float32
+        k = torch.empty((rows, self.geom.channels), dtype=dt, device="cuda")
+        v = torch.empty_like(k)
+        _check(lib().fvsr_kv_cache_gather(self.handle, _ptr(k), _ptr(v), _stream(stream)))
+        return k, v
+
+
+def lcsa_forward(q, k_new, v_new, cache: KVCache, geom: Geometry, out=None, kidx=None, kcnt=None, workspace=None,
+                 stream=None):
+    """One streaming layer (DiT.swift:504-538): append (k_new, v_new), select over cache ⊕ current, attend, trim.
+    geom.q_slices = the chunk's slices; geom.kv_slices is ignored (taken from the cache)."""
+    torch = _torch()
+    q2 = _rows(q)
+    if out is None:
+        out = torch.empty_like(q2)
+    full = Geometry(**{**geom.__dict__, "kv_slices": min(cache.slices + geom.q_slices, cache.capacity)})
+    ws = workspace if workspace is not None else make_workspace(full, q2.device)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_forward(ctypes.byref(p), _ptr(q2), _ptr(_rows(k_new)), _ptr(_rows(v_new)), cache.handle,
+                                   _ptr(out), _ptr(kidx), _ptr(kcnt), _ptr(ws), ws.numel(), _stream(stream)))
+    return out
+
+
+def device_check(stream=None) -> None:
+    """Synchronise and raise FVSRError(FVSR_ETIMEOUT) if a device-side wait of this library gave up."""
+    _check(lib().fvsr_device_check(_stream(stream)))

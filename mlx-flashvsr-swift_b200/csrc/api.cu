@@ -1,0 +1,417 @@
+// api.cu — the C ABI of include/fvsr_lcsa.h: host-side validation, workspace layout, the paged streaming KV cache
+// and the per-layer forward that chains append → select → attention → trim.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/fvsr_lcsa.h"
+#include "common.cuh"
+
+namespace fvsr {
+size_t select_scores_smem_bytes(int nk);
+size_t attn_bf16_smem_bytes(int nk);
+}  // namespace fvsr
+
+using namespace fvsr;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+fvsr_status fail(fvsr_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+
+fvsr_status cuda_fail(cudaError_t e, const char* what) {
+    return fail(FVSR_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define FVSR_CU(call, what)                          \
+    do {                                             \
+        cudaError_t _e = (call);                     \
+        if (_e != cudaSuccess) return cuda_fail(_e, what); \
+    } while (0)
+
+constexpr int kMaxNk = 2560;       // selection keeps one score row per query block in shared memory
+constexpr int kMaxHeads = 64;
+
+struct Dims {
+    int heads, s, nq, nk;
+    int64_t channels, elt;
+};
+
+fvsr_status check_params(const fvsr_lcsa_params* p, Dims* d, bool need_kv = true) {
+    if (!p) return fail(FVSR_EINVAL, "params is NULL");
+    if (p->heads < 1 || p->heads > kMaxHeads) return fail(FVSR_EINVAL, "heads must be in [1, %d], got %d", kMaxHeads, p->heads);
+    if (p->head_dim != 128) return fail(FVSR_EINVAL, "head_dim must be 128, got %d", p->head_dim);
+    if (p->bh < 1 || p->bw < 1) return fail(FVSR_EINVAL, "block grid must be positive, got %dx%d", p->bh, p->bw);
+    if (p->q_slices < 1) return fail(FVSR_EINVAL, "q_slices must be >= 1, got %d", p->q_slices);
+    if (need_kv && p->kv_slices < 1) return fail(FVSR_EINVAL, "kv_slices must be >= 1, got %d", p->kv_slices);
+    if (p->local_range < 1) return fail(FVSR_EINVAL, "local_range must be >= 1, got %d", p->local_range);
+    if (p->topk < 0) return fail(FVSR_EINVAL, "topk must be >= 0, got %d", p->topk);
+    if (p->dtype != FVSR_F32 && p->dtype != FVSR_BF16) return fail(FVSR_EINVAL, "dtype must be FVSR_F32 or FVSR_BF16");
+    d->heads = p->heads;
+    d->s = p->bh * p->bw;
+    d->nq = p->q_slices * d->s;
+    d->nk = need_kv ? p->kv_slices * d->s : 0;
+    d->channels = (int64_t)p->heads * 128;
+    d->elt = p->dtype == FVSR_BF16 ? 2 : 4;
+    if (d->nk > kMaxNk) return fail(FVSR_EUNSUPPORTED, "Nk = %d key blocks exceeds the supported %d", d->nk, kMaxNk);
+    if (d->nq > 65535 || (int64_t)d->heads * d->nq > (1ll << 30))
+        return fail(FVSR_EUNSUPPORTED, "Nq = %d query blocks is too large", d->nq);
+    return FVSR_OK;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Workspace {
+    float* pooled_q;
+    float* pooled_k;
+    float* probs;
+    int32_t* kidx;
+    int32_t* kcnt;
+    size_t bytes;
+};
+
+Workspace layout(const Dims& d, void* base) {
+    Workspace w{};
+    uint8_t* p = static_cast<uint8_t*>(base);
+    size_t off = 0;
+    auto take = [&](size_t n) {
+        uint8_t* r = p ? p + off : nullptr;
+        off += align_up(n);
+        return r;
+    };
+    w.pooled_q = reinterpret_cast<float*>(take((size_t)d.nq * d.channels * 4));
+    w.pooled_k = reinterpret_cast<float*>(take((size_t)d.nk * d.channels * 4));
+    w.probs = reinterpret_cast<float*>(take((size_t)d.heads * d.nq * d.nk * 4));
+    w.kidx = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * d.nk * 4));
+    w.kcnt = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * 4));
+    w.bytes = off;
+    return w;
+}
+
+// A contiguous K/V buffer: one page holding all nk blocks, so logical block j is physical block j.
+KvPages identity_pages(int nk) {
+    KvPages pg{};
+    pg.s = nk;
+    return pg;
+}
+
+// Checks once per device that it is an sm_100 part (the tcgen05 kernel's target).
+fvsr_status check_device_sm100() {
+    int dev = 0;
+    FVSR_CU(cudaGetDevice(&dev), "cudaGetDevice");
+    static std::mutex mu;
+    static std::vector<int> ok_cache(64, -1);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && ok_cache[dev] >= 0)
+        return ok_cache[dev] ? FVSR_OK : fail(FVSR_EUNSUPPORTED, "device %d is not sm_100", dev);
+    int major = 0, minor = 0;
+    FVSR_CU(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "cudaDeviceGetAttribute");
+    FVSR_CU(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev), "cudaDeviceGetAttribute");
+    const bool ok = major == 10 && minor == 0;
+    if (dev < 64) ok_cache[dev] = ok ? 1 : 0;
+    return ok ? FVSR_OK : fail(FVSR_EUNSUPPORTED, "device %d is sm_%d%d, the kernels need sm_100a", dev, major, minor);
+}
+
+fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* pooled_q, const float* pooled_k,
+                       const KvPages& pk_pages, int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs,
+                       cudaStream_t st) {
+    FVSR_CU(launch_select_scores(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range, probs, st),
+            "select scores launch");
+    FVSR_CU(launch_select_threshold(probs, d.heads, d.nq, d.nk, p->q_slices, p->topk, kidx, kcnt, mask, st),
+            "select threshold launch");
+    return FVSR_OK;
+}
+
+fvsr_status run_attention(const fvsr_lcsa_params* p, const Dims& d, const void* q, const void* k, const void* v,
+                          int64_t kv_rows, const KvPages& pages, const int32_t* kidx, const int32_t* kcnt, void* out,
+                          cudaStream_t st) {
+    fvsr_status s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    if (p->dtype == FVSR_BF16) {
+        FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, st), "bf16 attention launch");
+    } else {
+        FVSR_CU(launch_attn_f32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
+                                pages, d.heads, d.nq, d.nk, kidx, kcnt, static_cast<float*>(out), st),
+                "fp32 attention launch");
+    }
+    return FVSR_OK;
+}
+
+}  // namespace
+
+struct fvsr_kv_cache {
+    fvsr_lcsa_params p;
+    Dims d;
+    int kv_len, capacity;
+    std::vector<int32_t> pages;  // logical slice order, oldest first → arena page
+    void* k_arena = nullptr;
+    void* v_arena = nullptr;
+    float* pk_arena = nullptr;   // pooled keys, (capacity·s, H·128) fp32
+    int device = 0;
+    int64_t page_rows() const { return (int64_t)d.s * 128; }
+    int64_t page_bytes() const { return page_rows() * d.channels * d.elt; }
+};
+
+extern "C" {
+
+int32_t fvsr_version(void) { return 100; }
+
+const char* fvsr_status_string(fvsr_status s) {
+    switch (s) {
+        case FVSR_OK: return "ok";
+        case FVSR_EINVAL: return "invalid argument";
+        case FVSR_ECUDA: return "CUDA error";
+        case FVSR_ETIMEOUT: return "device wait timed out";
+        case FVSR_ENOMEM: return "out of memory / workspace too small";
+        case FVSR_EUNSUPPORTED: return "unsupported size or device";
+    }
+    return "unknown status";
+}
+
+const char* fvsr_last_error(void) { return g_last_error.c_str(); }
+
+fvsr_status fvsr_device_check(fvsr_stream_t stream) {
+    int flag = 0;
+    FVSR_CU(read_and_clear_device_error(&flag, reinterpret_cast<cudaStream_t>(stream)), "device check");
+    return flag ? fail(FVSR_ETIMEOUT, "a device-side wait hit its limit; the kernel returned early") : FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_workspace_size(const fvsr_lcsa_params* p, size_t* bytes) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!bytes) return fail(FVSR_EINVAL, "bytes is NULL");
+    *bytes = layout(d, nullptr).bytes;
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_pool(const fvsr_lcsa_params* p, const void* x, int64_t nblocks, float* pooled,
+                           fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d, false);
+    if (s != FVSR_OK) return s;
+    if (nblocks < 0 || nblocks > 65535) return fail(FVSR_EINVAL, "nblocks must be in [0, 65535], got %lld", (long long)nblocks);
+    if (nblocks > 0 && (!x || !pooled)) return fail(FVSR_EINVAL, "x and pooled must be non-NULL");
+    if (!aligned16(x) || !aligned16(pooled)) return fail(FVSR_EINVAL, "x and pooled must be 16-byte aligned");
+    FVSR_CU(launch_pool(x, p->dtype, nblocks, (int)d.channels, pooled, nullptr, reinterpret_cast<cudaStream_t>(stream)),
+            "pool launch");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const void* k, const float* pooled_k,
+                             int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs, void* workspace,
+                             size_t workspace_bytes, fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!q || (!k && !pooled_k) || !kidx || !kcnt) return fail(FVSR_EINVAL, "q, k (or pooled_k), kidx and kcnt are required");
+    if (!aligned16(q) || (k && !aligned16(k)) || (pooled_k && !aligned16(pooled_k)))
+        return fail(FVSR_EINVAL, "q, k and pooled_k must be 16-byte aligned");
+    Workspace w = layout(d, workspace);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    FVSR_CU(launch_pool(q, p->dtype, d.nq, (int)d.channels, w.pooled_q, nullptr, st), "pool q launch");
+    const float* pk = pooled_k;
+    if (!pk) {
+        FVSR_CU(launch_pool(k, p->dtype, d.nk, (int)d.channels, w.pooled_k, nullptr, st), "pool k launch");
+        pk = w.pooled_k;
+    }
+    return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, st);
+}
+
+fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                const int32_t* kidx, const int32_t* kcnt, void* out, fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!q || !k || !v || !kidx || !kcnt || !out) return fail(FVSR_EINVAL, "q, k, v, kidx, kcnt and out are required");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
+    return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                     const float* block_mask, void* out, void* workspace, size_t workspace_bytes,
+                                     fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!block_mask) return fail(FVSR_EINVAL, "block_mask is required");
+    Workspace w = layout(d, workspace);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    FVSR_CU(launch_mask_to_lists(block_mask, d.heads, d.nq, d.nk, w.kidx, w.kcnt, st), "mask to lists launch");
+    return fvsr_lcsa_attention(p, q, k, v, w.kidx, w.kcnt, out, stream);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// KV cache
+// ---------------------------------------------------------------------------------------------------------------
+
+fvsr_status fvsr_kv_cache_create(const fvsr_lcsa_params* p, int32_t kv_len, int32_t max_new_slices,
+                                 fvsr_kv_cache** cache) {
+    Dims d;
+    fvsr_status s = check_params(p, &d, false);
+    if (s != FVSR_OK) return s;
+    if (!cache) return fail(FVSR_EINVAL, "cache is NULL");
+    *cache = nullptr;
+    if (kv_len < 1 || max_new_slices < 1 || kv_len + max_new_slices > kMaxPages)
+        return fail(FVSR_EINVAL, "need kv_len >= 1, max_new_slices >= 1 and kv_len + max_new_slices <= %d", kMaxPages);
+    if ((int64_t)(kv_len + max_new_slices) * d.s > kMaxNk)
+        return fail(FVSR_EUNSUPPORTED, "cache of %d key blocks exceeds the supported %d", (kv_len + max_new_slices) * d.s, kMaxNk);
+    fvsr_kv_cache* c = new (std::nothrow) fvsr_kv_cache();
+    if (!c) return fail(FVSR_ENOMEM, "host allocation failed");
+    c->p = *p;
+    c->d = d;
+    c->kv_len = kv_len;
+    c->capacity = kv_len + max_new_slices;
+    cudaGetDevice(&c->device);
+    const size_t bytes = (size_t)c->capacity * c->page_bytes();
+    const size_t pbytes = (size_t)c->capacity * d.s * d.channels * 4;
+    if (cudaMalloc(&c->k_arena, bytes) != cudaSuccess || cudaMalloc(&c->v_arena, bytes) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&c->pk_arena), pbytes) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(c->k_arena);
+        cudaFree(c->v_arena);
+        cudaFree(c->pk_arena);
+        delete c;
+        return fail(FVSR_ENOMEM, "cache arena allocation of %zu bytes failed", 2 * bytes + pbytes);
+    }
+    *cache = c;
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_destroy(fvsr_kv_cache* c) {
+    if (!c) return FVSR_OK;
+    cudaFree(c->k_arena);
+    cudaFree(c->v_arena);
+    cudaFree(c->pk_arena);
+    delete c;
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_reset(fvsr_kv_cache* c) {
+    if (!c) return fail(FVSR_EINVAL, "cache is NULL");
+    c->pages.clear();
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_slices(const fvsr_kv_cache* c, int32_t* slices) {
+    if (!c || !slices) return fail(FVSR_EINVAL, "cache and slices must be non-NULL");
+    *slices = (int32_t)c->pages.size();
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_append(fvsr_kv_cache* c, const void* k_new, const void* v_new, int32_t new_slices,
+                                 fvsr_stream_t stream) {
+    if (!c) return fail(FVSR_EINVAL, "cache is NULL");
+    if (!k_new || !v_new) return fail(FVSR_EINVAL, "k_new and v_new are required");
+    if (!aligned16(k_new) || !aligned16(v_new)) return fail(FVSR_EINVAL, "k_new and v_new must be 16-byte aligned");
+    if (new_slices < 1 || (int)c->pages.size() + new_slices > c->capacity)
+        return fail(FVSR_EINVAL, "appending %d slices to %zu exceeds the capacity %d", new_slices, c->pages.size(), c->capacity);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    for (int t = 0; t < new_slices; ++t) {
+        int page = -1;
+        for (int cand = 0; cand < c->capacity && page < 0; ++cand) {
+            bool used = false;
+            for (int32_t u : c->pages) used |= (u == cand);
+            if (!used) page = cand;
+        }
+        const int64_t src_off = (int64_t)t * c->page_bytes();
+        uint8_t* kd = static_cast<uint8_t*>(c->k_arena) + (int64_t)page * c->page_bytes();
+        uint8_t* vd = static_cast<uint8_t*>(c->v_arena) + (int64_t)page * c->page_bytes();
+        FVSR_CU(launch_pool(static_cast<const uint8_t*>(k_new) + src_off, c->p.dtype, c->d.s, (int)c->d.channels,
+                            c->pk_arena + (int64_t)page * c->d.s * c->d.channels, kd, st),
+                "cache append (copy + pool keys)");
+        FVSR_CU(cudaMemcpyAsync(vd, static_cast<const uint8_t*>(v_new) + src_off, c->page_bytes(), cudaMemcpyDeviceToDevice, st),
+                "cache append (values)");
+        c->pages.push_back(page);
+    }
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_trim(fvsr_kv_cache* c) {
+    if (!c) return fail(FVSR_EINVAL, "cache is NULL");
+    if ((int)c->pages.size() > c->kv_len) c->pages.erase(c->pages.begin());
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_gather(const fvsr_kv_cache* c, void* k_out, void* v_out, fvsr_stream_t stream) {
+    if (!c) return fail(FVSR_EINVAL, "cache is NULL");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    for (size_t i = 0; i < c->pages.size(); ++i) {
+        const int64_t off = (int64_t)c->pages[i] * c->page_bytes();
+        if (k_out)
+            FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(k_out) + i * c->page_bytes(), static_cast<uint8_t*>(c->k_arena) + off,
+                                    c->page_bytes(), cudaMemcpyDeviceToDevice, st),
+                    "cache gather (keys)");
+        if (v_out)
+            FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(v_out) + i * c->page_bytes(), static_cast<uint8_t*>(c->v_arena) + off,
+                                    c->page_bytes(), cudaMemcpyDeviceToDevice, st),
+                    "cache gather (values)");
+    }
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_state(const fvsr_kv_cache* c, int32_t* pages, int32_t* slices) {
+    if (!c || !slices) return fail(FVSR_EINVAL, "cache and slices must be non-NULL");
+    *slices = (int32_t)c->pages.size();
+    if (pages)
+        for (size_t i = 0; i < c->pages.size(); ++i) pages[i] = c->pages[i];
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const void* k_new, const void* v_new,
+                              fvsr_kv_cache* cache, void* out, int32_t* kidx, int32_t* kcnt, void* workspace,
+                              size_t workspace_bytes, fvsr_stream_t stream) {
+    if (!cache) return fail(FVSR_EINVAL, "cache is NULL");
+    if (!p) return fail(FVSR_EINVAL, "params is NULL");
+    if (p->heads != cache->p.heads || p->bh != cache->p.bh || p->bw != cache->p.bw || p->dtype != cache->p.dtype)
+        return fail(FVSR_EINVAL, "params do not match the cache geometry");
+    if (!q || !out) return fail(FVSR_EINVAL, "q and out are required");
+    if (!aligned16(q) || !aligned16(out)) return fail(FVSR_EINVAL, "q and out must be 16-byte aligned");
+    fvsr_lcsa_params pp = *p;
+    pp.kv_slices = (int32_t)cache->pages.size() + p->q_slices;
+    Dims d;
+    fvsr_status s = check_params(&pp, &d);
+    if (s != FVSR_OK) return s;
+    Workspace w = layout(d, workspace);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    s = fvsr_kv_cache_append(cache, k_new, v_new, p->q_slices, stream);
+    if (s != FVSR_OK) return s;
+    KvPages pages{};
+    pages.s = d.s;
+    for (int i = 0; i < kMaxPages; ++i)
+        pages.page_block[i] = (i < (int)cache->pages.size() ? cache->pages[i] : 0) * d.s;
+    int32_t* li = kidx ? kidx : w.kidx;
+    int32_t* lc = kcnt ? kcnt : w.kcnt;
+    FVSR_CU(launch_pool(q, pp.dtype, d.nq, (int)d.channels, w.pooled_q, nullptr, st), "pool q launch");
+    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, st);
+    if (s != FVSR_OK) return s;
+    s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
+                      out, st);
+    if (s != FVSR_OK) return s;
+    return fvsr_kv_cache_trim(cache);
+}
+
+}  // extern "C"

@@ -1,0 +1,352 @@
+// attn_sm100.cu — bf16 block-sparse flash attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the Metal kernel of SparseAttention.swift:17-153 (one threadgroup per (query block, head), walking only the
+// selected key blocks by index with an fp32 online softmax; an empty query block writes zeros).
+//
+// One CTA per (head, query block) work item, ordered head-major so the CTAs in flight share one head's K/V in L2.
+// Warp roles (192 threads):
+//   warp 0      TMA producer: Q tile once, then K and V tiles of each kept key block into a 2-stage ring.
+//   warp 1      TMEM owner + single-thread MMA issuer: S_j = Q·K_jᵀ (SS-MMA, 128×128×128) one block ahead, then
+//               O += P_j·V_j (TS-MMA: P read from TMEM, V from shared memory as an MN-major operand).
+//   warps 2..5  softmax warpgroup: thread = query row = TMEM lane. Reads S_j from TMEM, online softmax in fp32
+//               (exp2 on the MUFU pipe), rescales O in TMEM when the row max moved, writes P_j (bf16) to TMEM,
+//               and finally normalises O and stores it.
+// TMEM (512 columns): O [0,128), S0 [128,256), S1 [256,384), P0 [384,448), P1 [448,512).
+// Shared memory: Q 32 KB + 2 × (K 32 KB + V 32 KB), each tile as two 128-row × 64-column boxes in the 128-byte
+// swizzled layout that TMA writes and the MMA descriptors read.
+// Every wait is bounded (4 s); on expiry the kernel raises a device timeout word that fvsr_device_check reports.
+#include <mutex>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace fvsr {
+
+__device__ int g_fvsr_timeout = 0;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kStages = 2;
+constexpr uint32_t kTileBytes = kBlock * kD * 2;  // 32 KB bf16 tile
+constexpr uint32_t kBoxBytes = kTileBytes / 2;    // one 128 × 64 box
+constexpr uint32_t kColO = 0, kColS0 = 128, kColP0 = 384;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+constexpr int kThreads = 192;
+
+constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, 0, 0);   // A = Q (K-major), B = K (K-major)
+constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);  // A = P (TMEM), B = V (MN-major)
+
+// Shared-memory map (offsets from a 1024-byte aligned base).
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kTileBytes;                          // stage s: kOffK + s·2·kTileBytes
+constexpr uint32_t kOffBar = kTileBytes * (1 + 2 * kStages);   // barriers
+constexpr int kBarQ = 0, kBarKF = 1, kBarVF = kBarKF + kStages, kBarKVE = kBarVF + kStages, kBarSF = kBarKVE + kStages,
+              kBarPF = kBarSF + 2, kBarO = kBarPF + 2, kNumBars = kBarO + 1;
+constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
+constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
+constexpr uint32_t kOffList = (kOffAbort + 4 + 15) & ~15u;
+
+struct AttnArgs {
+    const int32_t* kidx;
+    const int32_t* kcnt;
+    __nv_bfloat16* out;
+    int heads, nq, nk;
+    float scale_log2;
+    KvPages pages;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const int item = blockIdx.x;
+    const int h = item / a.nq, qb = item % a.nq;
+    const int64_t ld = (int64_t)a.heads * kD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int cnt = a.kcnt[item];
+    cnt = cnt < 0 ? 0 : (cnt > a.nk ? a.nk : cnt);
+
+    if (cnt == 0) {  // SparseAttention.swift:47-53: a query block that selected nothing writes zeros
+        for (int idx = threadIdx.x; idx < kBlock * 16; idx += kThreads) {
+            const int r = idx >> 4, c = idx & 15;
+            *reinterpret_cast<uint4*>(a.out + ((int64_t)qb * kBlock + r) * ld + h * kD + c * 8) = make_uint4(0, 0, 0, 0);
+        }
+        return;
+    }
+
+    volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(smem + kOffAbort);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
+    int32_t* s_list = reinterpret_cast<int32_t*>(smem + kOffList);
+    auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(kBarQ), 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(bar(kBarKF + s), 1);
+            mbar_init(bar(kBarVF + s), 1);
+            mbar_init(bar(kBarKVE + s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(kBarSF + b), 1);
+            mbar_init(bar(kBarPF + b), 128);
+        }
+        mbar_init(bar(kBarO), 1);
+        *abort_word = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
+    const int32_t* glist = a.kidx + (int64_t)item * a.nk;
+    for (int j = threadIdx.x; j < cnt; j += kThreads) {
+        int kb = glist[j];
+        kb = kb < 0 ? 0 : (kb >= a.nk ? a.nk - 1 : kb);
+        s_list[j] = kv_phys_block(a.pages, kb);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const int xq = h * kD;
+            mbar_expect_tx(bar(kBarQ), kTileBytes);
+            tma_load_2d(sbase + kOffQ, &tmQ, xq, qb * kBlock, bar(kBarQ));
+            tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, xq + 64, qb * kBlock, bar(kBarQ));
+            for (int j = 0; j < cnt; ++j) {
+                const int s = j % kStages;
+                if (j >= kStages &&
+                    !mbar_wait(bar(kBarKVE + s), (uint32_t)((j / kStages) - 1) & 1u, abort_word, &g_fvsr_timeout,
+                               kWaitLimitNs))
+                    break;
+                const int row = s_list[j] * kBlock;
+                const uint32_t dk = sbase + kOffK + (uint32_t)s * 2u * kTileBytes, dv = dk + kTileBytes;
+                mbar_expect_tx(bar(kBarKF + s), kTileBytes);
+                tma_load_2d(dk, &tmK, xq, row, bar(kBarKF + s));
+                tma_load_2d(dk + kBoxBytes, &tmK, xq + 64, row, bar(kBarKF + s));
+                mbar_expect_tx(bar(kBarVF + s), kTileBytes);
+                tma_load_2d(dv, &tmV, xq, row, bar(kBarVF + s));
+                tma_load_2d(dv + kBoxBytes, &tmV, xq + 64, row, bar(kBarVF + s));
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = mbar_wait(bar(kBarQ), 0, abort_word, &g_fvsr_timeout, kWaitLimitNs);
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kStages;
+                if (!mbar_wait(bar(kBarKF + s), (uint32_t)(j / kStages) & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs))
+                    return false;
+                tc_fence_after();
+                const uint32_t d = tmem + kColS0 + 128u * (uint32_t)(j & 1);
+                const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + (uint32_t)s * 2u * kTileBytes;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint32_t off = (uint32_t)(ks >> 2) * kBoxBytes + (uint32_t)(ks & 3) * 32u;
+                    mma_ss(d, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), kIdescS, ks > 0 ? 1u : 0u);
+                }
+                mma_commit(bar(kBarSF + (j & 1)));
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < cnt; ++j) {
+                if (j + 1 < cnt && !issue_s(j + 1)) break;
+                const int s = j % kStages;
+                if (!mbar_wait(bar(kBarVF + s), (uint32_t)(j / kStages) & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs))
+                    break;
+                if (!mbar_wait(bar(kBarPF + (j & 1)), (uint32_t)(j >> 1) & 1u, abort_word, &g_fvsr_timeout,
+                               kWaitLimitNs))
+                    break;
+                tc_fence_after();
+                const uint32_t va = sbase + kOffK + (uint32_t)s * 2u * kTileBytes + kTileBytes;
+                const uint32_t pa = tmem + kColP0 + 64u * (uint32_t)(j & 1);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                    mma_ts(tmem + kColO, pa + 8u * (uint32_t)ks, smem_desc(va + (uint32_t)ks * 2048u, kBoxBytes, 1024),
+                           kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+                mma_commit(bar(kBarKVE + s));
+                mma_commit(bar(kBarO));
+            }
+        }
+    } else {
+        // ---------------- softmax warpgroup ----------------
+        const int quarter = warp & 3;  // TMEM lanes [32·quarter, 32·quarter + 32) are this warp's
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        const float sl2 = a.scale_log2;
+        float m = -INFINITY, l = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < cnt; ++j) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarSF + (j & 1)), (uint32_t)(j >> 1) & 1u, abort_word,
+                                                    &g_fvsr_timeout, kWaitLimitNs))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sv[128];
+            const uint32_t scol = lane_base + kColS0 + 128u * (uint32_t)(j & 1);
+            tmem_ld32(scol, sv);
+            tmem_ld32(scol + 32, sv + 32);
+            tmem_ld32(scol + 64, sv + 64);
+            tmem_ld32(scol + 96, sv + 96);
+            tmem_ld_wait(sv);
+            tmem_ld_wait(sv + 32);
+            tmem_ld_wait(sv + 64);
+            tmem_ld_wait(sv + 96);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+            const float m_new = fmaxf(m, mx * sl2);
+            const float neg = -m_new;
+            uint32_t pk[64];
+            float rs = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, neg));
+                const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, neg));
+                rs += p0 + p1;
+                pk[c] = pack_bf16x2(p0, p1);
+            }
+            const float alpha = ex2_approx(m - m_new);
+            l = l * alpha + rs;
+            m = m_new;
+            if (j > 0) {
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarO), (uint32_t)(j - 1) & 1u, abort_word, &g_fvsr_timeout,
+                                                        kWaitLimitNs))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t ov[32];
+                        tmem_ld32(lane_base + kColO + 32u * c, ov);
+                        tmem_ld_wait(ov);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st32(lane_base + kColO + 32u * c, ov);
+                    }
+                }
+            }
+            const uint32_t pcol = lane_base + kColP0 + 64u * (uint32_t)(j & 1);
+            tmem_st32(pcol, pk);
+            tmem_st32(pcol + 32, pk + 32);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(bar(kBarPF + (j & 1)));
+        }
+        if (ok && __all_sync(0xffffffffu,
+                             mbar_wait(bar(kBarO), (uint32_t)(cnt - 1) & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs))) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+            __nv_bfloat16* orow = a.out + ((int64_t)qb * kBlock + r) * ld + h * kD;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t ov[32];
+                tmem_ld32(lane_base + kColO + 32u * c, ov);
+                tmem_ld_wait(ov);
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    w[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv, __uint_as_float(ov[2 * i + 1]) * inv);
+                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D map over a (rows, channels) bf16 matrix, box = 128 rows × 64 channels, 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t channels) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)channels * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t attn_bf16_smem_bytes(int nk) { return 1024 + kOffList + sizeof(int32_t) * (size_t)nk; }
+
+cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
+                             int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
+                             cudaStream_t st) {
+    CUtensorMap mq, mk, mv;
+    const int64_t channels = (int64_t)heads * kD;
+    if (!make_map(&mq, q, (int64_t)nq * kBlock, channels) || !make_map(&mk, k, kv_rows, channels) ||
+        !make_map(&mv, v, kv_rows, channels))
+        return cudaErrorInvalidValue;
+    const size_t smem = attn_bf16_smem_bytes(nk);
+    cudaError_t e = cudaFuncSetAttribute(attn_bf16_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    AttnArgs a;
+    a.kidx = kidx;
+    a.kcnt = kcnt;
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.heads = heads;
+    a.nq = nq;
+    a.nk = nk;
+    a.scale_log2 = (1.0f / sqrtf((float)kD)) * 1.4426950408889634f;
+    a.pages = pages;
+    attn_bf16_sm100_kernel<<<heads * nq, kThreads, smem, st>>>(mq, mk, mv, a);
+    return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st) {
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return e;
+    int v = 0;
+    e = cudaMemcpyFromSymbol(&v, g_fvsr_timeout, sizeof(int));
+    if (e != cudaSuccess) return e;
+    if (v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_fvsr_timeout, &zero, sizeof(int));
+    }
+    *flag = v;
+    return e;
+}
+
+}  // namespace fvsr

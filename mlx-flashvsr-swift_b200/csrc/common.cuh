@@ -1,0 +1,44 @@
+// common.cuh — shared definitions of the sm_100a LCSA kernels (internal; the public surface is include/fvsr_lcsa.h).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fvsr {
+
+constexpr int kBlock = 128;  // tokens per window / block (DiT.swift:113-118)
+constexpr int kD = 128;      // head dim (SparseAttention.swift:173)
+constexpr int kMaxPages = 32;
+
+// Logical key block j lives at physical block page_block[j / s] + j % s of the K/V arena (a contiguous K/V buffer is
+// the identity table). Used by the attention and selection kernels to read the paged streaming cache in place.
+struct KvPages {
+    int32_t page_block[kMaxPages];
+    int32_t s;  // blocks per page (spatial blocks per temporal slice)
+};
+
+__host__ __device__ inline int32_t kv_phys_block(const KvPages& pg, int32_t j) {
+    return pg.page_block[j / pg.s] + j % pg.s;
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+// ---- launchers (each returns the launch's cudaError_t) ----
+cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
+                        cudaStream_t st);
+cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
+                                 int bh, int bw, int local_range, float* probs, cudaStream_t st);
+cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
+                                    int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st);
+cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
+                                 cudaStream_t st);
+cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
+                            int nk, const int32_t* kidx, const int32_t* kcnt, float* out, cudaStream_t st);
+cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
+                             int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
+                             cudaStream_t st);
+// Reads and clears the device-side timeout word of the current device (1 if a wait gave up since the last read).
+cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st);
+
+}  // namespace fvsr

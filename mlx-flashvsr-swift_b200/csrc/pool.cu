@@ -1,0 +1,84 @@
+// pool.cu — fp32 block means of window-ordered tokens (DiT.swift:161-162), optionally fused with the in-place copy
+// of the same rows into a KV-cache page (the cache append of DiT.swift:508-511 reads each key row once).
+//
+// HBM-bound: algorithmic bytes = nblocks·128·C·elt read (+ the same written when copying) + nblocks·C·4 written.
+// Layout: one CTA covers one 128-token block × 512 channels; 4 token groups × 64 channel lanes, 8 channels per lane
+// (one 128-bit load per token for bf16), so a warp reads 512 contiguous bytes of a token row per load.
+#include "common.cuh"
+
+namespace fvsr {
+
+namespace {
+
+constexpr int kPoolLanes = 64;               // channel lanes per CTA
+constexpr int kPoolChannels = kPoolLanes * 8;  // 512 channels per CTA
+
+template <int DT>
+__global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, int channels,
+                                                   float* __restrict__ out, void* __restrict__ copy_dst) {
+    __shared__ float part[4][kPoolChannels];
+    const int lane = threadIdx.x & (kPoolLanes - 1);
+    const int g = threadIdx.x / kPoolLanes;  // token group: tokens [32g, 32g + 32)
+    const int c0 = blockIdx.x * kPoolChannels + lane * 8;
+    const int64_t b = blockIdx.y;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    if (c0 < channels) {
+#pragma unroll 4
+        for (int t = 32 * g; t < 32 * g + 32; ++t) {
+            const int64_t off = (b * kBlock + t) * (int64_t)channels + c0;
+            if (DT == 1) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
+                if (copy_dst) *reinterpret_cast<uint4*>(static_cast<uint16_t*>(copy_dst) + off) = v;
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[2 * i] = __fadd_rn(acc[2 * i], bf16_bits_to_float(w[i] & 0xFFFFu));
+                    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_bits_to_float(w[i] >> 16));
+                }
+            } else {
+                const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
+                const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
+                if (copy_dst) {
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(copy_dst) + off);
+                    dst[0] = v0;
+                    dst[1] = v1;
+                }
+                const float w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], w[i]);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) part[g][lane * 8 + i] = acc[i];
+    __syncthreads();
+    if (g == 0 && c0 < channels) {
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = lane * 8 + i;
+            const float s = __fadd_rn(__fadd_rn(part[0][c], part[1][c]), __fadd_rn(part[2][c], part[3][c]));
+            r[i] = __fmul_rn(s, 0.0078125f);
+        }
+        float4* o = reinterpret_cast<float4*>(out + b * channels + c0);
+        o[0] = make_float4(r[0], r[1], r[2], r[3]);
+        o[1] = make_float4(r[4], r[5], r[6], r[7]);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
+                        cudaStream_t st) {
+    if (nblocks == 0) return cudaSuccess;
+    dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)nblocks);
+    if (dtype == 1)
+        pool_kernel<1><<<grid, 256, 0, st>>>(x, channels, out, copy_dst);
+    else
+        pool_kernel<0><<<grid, 256, 0, st>>>(x, channels, out, copy_dst);
+    return cudaGetLastError();
+}
+
+}  // namespace fvsr

@@ -1,0 +1,97 @@
+"""CPU tests of the C ABI: the library loads, exports every entry point include/fvsr_lcsa.h declares, and rejects bad
+arguments on the host before touching a device. No compute call needs a GPU here."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols() -> list[str]:
+    text = (ROOT / "include" / "fvsr_lcsa.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fvsr_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    syms = declared_symbols()
+    for must in ("fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_forward", "fvsr_kv_cache_append",
+                 "fvsr_lcsa_workspace_size"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol(fvsr):
+    L = fvsr.lib()
+    missing = [s for s in declared_symbols() if not hasattr(L, s)]
+    assert not missing, missing
+    assert sorted(fvsr.EXPORTED) == declared_symbols()
+
+
+def test_version_and_status_strings(fvsr):
+    L = fvsr.lib()
+    assert L.fvsr_version() >= 100
+    assert L.fvsr_status_string(fvsr.FVSR_OK) == b"ok"
+    assert b"timed out" in L.fvsr_status_string(fvsr.FVSR_ETIMEOUT)
+
+
+def test_workspace_size_matches_layout(fvsr):
+    g = fvsr.Geometry(heads=12, bh=9, bw=15, q_slices=1, kv_slices=3, local_range=11, topk=8384)
+    n = fvsr.workspace_size(g)
+    a = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    c = 12 * 128
+    want = a(g.nq * c * 4) + a(g.nk * c * 4) + a(12 * g.nq * g.nk * 4) * 2 + a(12 * g.nq * 4)
+    assert n == want
+
+
+@pytest.mark.parametrize("field,value,status", [
+    ("heads", 0, 1), ("head_dim", 64, 1), ("bh", 0, 1), ("q_slices", 0, 1), ("kv_slices", 0, 1),
+    ("local_range", 0, 1), ("topk", -1, 1), ("dtype", 7, 1), ("kv_slices", 100, 5),
+])
+def test_bad_params_rejected_on_host(fvsr, field, value, status):
+    g = fvsr.Geometry(heads=12, bh=6, bw=10, q_slices=1, kv_slices=3, local_range=11, topk=10)
+    p = g.params()
+    setattr(p, field, value)
+    n = ctypes.c_size_t(0)
+    assert fvsr.lib().fvsr_lcsa_workspace_size(ctypes.byref(p), ctypes.byref(n)) == status
+    assert fvsr.lib().fvsr_last_error()
+
+
+def test_null_pointers_rejected_before_any_launch(fvsr):
+    L = fvsr.lib()
+    g = fvsr.Geometry(heads=2, bh=2, bw=2, q_slices=1, kv_slices=2, local_range=3, topk=3)
+    p = g.params()
+    assert L.fvsr_lcsa_select(ctypes.byref(p), None, None, None, None, None, None, None, None, 0, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_lcsa_attention(ctypes.byref(p), None, None, None, None, None, None, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_lcsa_pool(None, None, 0, None, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_kv_cache_trim(None) == fvsr.FVSR_EINVAL
+    h = ctypes.c_void_p()
+    assert L.fvsr_kv_cache_create(ctypes.byref(p), 0, 1, ctypes.byref(h)) == fvsr.FVSR_EINVAL
+    assert L.fvsr_kv_cache_create(ctypes.byref(p), 30, 5, ctypes.byref(h)) == fvsr.FVSR_EINVAL
+    assert L.fvsr_kv_cache_destroy(None) == fvsr.FVSR_OK
+
+
+def test_misaligned_pointer_rejected(fvsr):
+    L = fvsr.lib()
+    g = fvsr.Geometry(heads=2, bh=2, bw=2, q_slices=1, kv_slices=2, local_range=3, topk=3)
+    p = g.params()
+    bad = ctypes.c_void_p(0x1000 + 4)
+    ok = ctypes.c_void_p(0x1000)
+    assert L.fvsr_lcsa_attention(ctypes.byref(p), bad, ok, ok, ok, ok, ok, None) == fvsr.FVSR_EINVAL
+    assert b"aligned" in L.fvsr_last_error()
+
+
+def test_topk_formula_and_allowed_counts(fvsr):
+    """DiT.swift:482 and the per-row allowed counts the configs translate their keep fractions with."""
+    assert fvsr.Geometry.topk_from_ratio(60, 2.0) == 7199
+    counts = {2: 8640, 3: 27945, 5: 58140}
+    import importlib
+    cfgs = importlib.import_module("fvsr_b200.configs").CONFIGS
+    for c, want in counts.items():
+        assert cfgs[c].geometry().allowed_per_row() == want
+    assert cfgs[3].geometry().topk == 8384
+    assert cfgs[5].geometry().topk == 14535
+    assert cfgs[1].geometry().topk == 96

@@ -1,0 +1,175 @@
+"""CPU tests of the oracle: the reference's known-answer tests, its own attention oracle's outputs (golden fixtures),
+and the fixed-order arithmetic the GPU kernels must reproduce. Citations are relative to the reference tree."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import detrand
+from make_golden import ATTN_CASES, SELECT_CASES, attn_inputs, local_mask, select_inputs
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+# --- Tests/FlashVSRMLXTests/FlashVSRStructureTests.swift:34-44 -------------------------------------------------
+def test_window_partition_round_trip_and_order(orc):
+    f, h, w, c = 4, 16, 24, 3
+    x = np.arange(f * h * w * c, dtype=np.float32).reshape(1, f, h, w, c)
+    p = orc.window_partition(x)
+    assert p.shape == ((f // 2) * (h // 8) * (w // 8), 128, c)
+    win = (1 * (h // 8) + 1) * (w // 8) + 2
+    tok = (1 * 8 + 3) * 8 + 5
+    np.testing.assert_array_equal(p[win, tok], x[0, 3, 11, 21])
+    r = orc.window_reverse(p, 1, f, h, w)
+    np.testing.assert_array_equal(r.reshape(x.shape), x)
+
+
+# --- FlashVSRStructureTests.swift:46-58 ------------------------------------------------------------------------
+@pytest.mark.parametrize("bh,bw,r", [(3, 4, 11), (6, 10, 3), (5, 5, 4)])
+def test_local_block_mask_matches_definition(orc, bh, bw, r):
+    m = orc.local_block_mask(bh, bw, r)
+    for q in range(bh * bw):
+        for k in range(bh * bw):
+            qr, qc, kr, kc = q // bw, q % bw, k // bw, k % bw
+            lo = lambda v: v - r // 2  # noqa: E731
+            want = lo(qr) <= kr <= lo(qr) + r - 1 and lo(qc) <= kc <= lo(qc) + r - 1
+            assert m[q, k] == want
+    np.testing.assert_array_equal(m, local_mask(bh, bw, r))
+
+
+def test_local_block_mask_range_covering_grid_is_dense(orc):
+    assert orc.local_block_mask(3, 4, 11).all()
+
+
+# --- FlashVSRStructureTests.swift:60-75 ------------------------------------------------------------------------
+def test_draft_mask_keeps_strictly_above_threshold(orc):
+    q = np.ones((2 * 128, 128), np.float32)
+    k = np.zeros((2 * 128, 128), np.float32)
+    k[:128] = 2.0                                       # key block 0 scores higher than block 1
+    local = np.ones((2, 2), bool)
+    _, m, _, kcnt = orc.draft_block_mask_and_probs(q, k, heads=1, q_slices=1, s=2, local=local, topk=1)
+    assert m.sum() == 0                                 # threshold = 2nd largest = p0 → nothing strictly above
+    _, m0, kidx, kcnt = orc.draft_block_mask_and_probs(q, k, heads=1, q_slices=1, s=2, local=local, topk=2)
+    np.testing.assert_array_equal(m0.reshape(-1).astype(np.float32), [1, 0, 1, 0])
+    np.testing.assert_array_equal(kcnt, [[1, 1]])
+    np.testing.assert_array_equal(kidx[0, :, 0], [0, 0])
+
+
+def test_topk_larger_than_row_keeps_all_but_minimum(orc):
+    """k = min(n − 1, topk) (DiT.swift:171): a huge topk thresholds at the smallest entry."""
+    q = detrand.normal(5, (2 * 128, 128))
+    k = detrand.normal(6, (4 * 128, 128))
+    probs, m, _, _ = orc.draft_block_mask_and_probs(q, k, heads=1, q_slices=1, s=2, local=np.ones((2, 2), bool),
+                                                    topk=10 ** 6)
+    assert m.sum() == probs.size - (probs == probs.min()).sum()
+
+
+# --- DiT.swift:478-485 -----------------------------------------------------------------------------------------
+def test_geometry_topk(orc):
+    assert orc.geometry_topk(60, 2.0) == 7199
+    assert orc.geometry_topk(135, 2.0 * 768 * 1280 / (1152 * 1920)) == int(135 * 135 * (2.0 * 768 * 1280 / (1152 * 1920))) - 1
+    assert orc.geometry_topk(8, 0.5) == 31
+
+
+# --- the softmax exponential shared with the GPU ---------------------------------------------------------------
+def test_exp_accuracy(orc):
+    xs = np.concatenate([np.linspace(-103.9, 0.0, 20001), -np.logspace(-8, 1, 2001), [0.0, -1e-30, 88.0, 1.0]])
+    xs = xs.astype(np.float32)
+    got = np.array([orc.fvsr_exp(x) for x in xs], np.float32)
+    want = np.exp(xs.astype(np.float64))
+    normal = want >= np.finfo(np.float32).tiny
+    ulp = np.spacing(want[normal].astype(np.float32)).astype(np.float64)
+    err_ulp = np.abs(got[normal].astype(np.float64) - want[normal]) / ulp
+    assert err_ulp.max() <= 1.0, err_ulp.max()
+    sub = ~normal
+    assert np.all(np.abs(got[sub].astype(np.float64) - want[sub]) <= 2 ** -149)
+    assert orc.fvsr_exp(float("-inf")) == 0.0
+    assert orc.fvsr_exp(-200.0) == 0.0
+
+
+# --- pooling order ---------------------------------------------------------------------------------------------
+def test_pool_fixed_order(orc):
+    x = detrand.normal(7, (3 * 128, 40), bf16_exact=False)
+    got = orc.pool(x)
+    want = np.empty((3, 40), np.float32)
+    for b in range(3):
+        for c in range(40):
+            parts = []
+            for g in range(4):
+                acc = np.float32(0)
+                for t in range(32 * g, 32 * g + 32):
+                    acc = np.float32(acc + x[b * 128 + t, c])
+                parts.append(acc)
+            want[b, c] = np.float32(np.float32(parts[0] + parts[1]) + np.float32(parts[2] + parts[3])) * np.float32(1 / 128)
+    np.testing.assert_array_equal(got, want)
+    xb = orc.f32_to_bf16_bits(x)
+    np.testing.assert_allclose(orc.pool(xb), orc.bf16_bits_to_f32(xb).reshape(3, 128, 40).mean(1), rtol=0, atol=1e-6)
+
+
+# --- attention against the reference's own oracle (golden fixtures) --------------------------------------------
+@pytest.mark.parametrize("case", ATTN_CASES, ids=[c[0] for c in ATTN_CASES])
+def test_attention_matches_reference_oracle(orc, case):
+    name, heads, nq, nk, density, seed, empty = case
+    g = np.load(GOLDEN / f"{name}.npz")
+    q, k, v, mask = attn_inputs(heads, nq, nk, density, seed, empty)
+    np.testing.assert_array_equal(g["mask"], mask.astype(np.uint8))
+    kidx, kcnt = orc.mask_to_lists(mask)
+    assert kcnt[empty[0], empty[1]] == 0
+    out = orc.attention(q, k, v, kidx, kcnt, heads)
+    cmp = orc.compare(out, g["out"])
+    assert cmp["rel"] < 2e-6, cmp                      # reference oracle is fp32 SDPA; ours accumulates in fp64
+    e = empty[1] * 128
+    assert not out[e:e + 128, empty[0] * 128:(empty[0] + 1) * 128].any()
+    fast = orc.attention(q, k, v, kidx, kcnt, heads, fast=True)
+    assert orc.compare(fast, g["out"])["rel"] < 5e-6
+
+
+def test_attention_items_subset(orc):
+    name, heads, nq, nk, density, seed, empty = ATTN_CASES[0]
+    q, k, v, mask = attn_inputs(heads, nq, nk, density, seed, empty)
+    kidx, kcnt = orc.mask_to_lists(mask)
+    full = orc.attention(q, k, v, kidx, kcnt, heads)
+    items = [1 * nq + 2, 0 * nq + 0]
+    part = orc.attention(q, k, v, kidx, kcnt, heads, items=items)
+    for w in items:
+        h, qb = divmod(w, nq)
+        sl = (slice(qb * 128, qb * 128 + 128), slice(h * 128, h * 128 + 128))
+        np.testing.assert_array_equal(part[sl], full[sl])
+
+
+def test_attention_bf16_inputs_match_fp32_of_same_values(orc):
+    name, heads, nq, nk, density, seed, empty = ATTN_CASES[1]
+    q, k, v, mask = attn_inputs(heads, nq, nk, density, seed, empty)      # bf16-representable values
+    kidx, kcnt = orc.mask_to_lists(mask)
+    a = orc.attention(q, k, v, kidx, kcnt, heads)
+    b = orc.attention(*(orc.f32_to_bf16_bits(t) for t in (q, k, v)), kidx, kcnt, heads)
+    np.testing.assert_array_equal(a, b)
+
+
+# --- selection against the float64 line-by-line evaluation -----------------------------------------------------
+@pytest.mark.parametrize("case", SELECT_CASES, ids=[c[0] for c in SELECT_CASES])
+def test_select_matches_f64_evaluation(orc, case):
+    name, heads, bh, bw, qs, kvs, r, keep, seed = case
+    g = np.load(GOLDEN / f"{name}.npz")
+    topk = int(g["meta"][6])
+    q, k = select_inputs(heads, bh, bw, qs, kvs, seed)
+    probs, m, kidx, kcnt = orc.draft_block_mask_and_probs(q, k, heads, qs, bh * bw, local_mask(bh, bw, r), topk)
+    rep = orc.mask_flip_report(m, g["mask"].astype(bool), probs, qs)
+    assert rep["flips"] == 0, rep
+    np.testing.assert_allclose(probs, g["probs"], rtol=2e-5, atol=1e-9)
+    assert int(kcnt.sum()) == int(g["mask"].sum()) == topk * heads * qs
+    for h in range(heads):
+        for i in range(probs.shape[1]):
+            sel = np.nonzero(m[h, i])[0]
+            np.testing.assert_array_equal(kidx[h, i, :len(sel)], sel)
+            assert (kidx[h, i, len(sel):] == -1).all()
+
+
+def test_select_bad_shapes_rejected(orc):
+    pq = np.zeros((6, 128), np.float32)
+    with pytest.raises(ValueError):
+        orc.select(pq, np.zeros((7, 128), np.float32), 1, 1, 6, np.ones((6, 6), bool), 3)   # Nk not a multiple of s
+    with pytest.raises(ValueError):
+        orc.select(pq, np.zeros((12, 128), np.float32), 1, 1, 6, np.ones((6, 6), bool), -1)  # negative topk
