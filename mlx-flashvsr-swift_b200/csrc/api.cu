@@ -11,11 +11,6 @@
 #include "../../include/fvsr_lcsa.h"
 #include "common.cuh"
 
-namespace fvsr {
-size_t select_scores_smem_bytes(int nk);
-size_t attn_bf16_smem_bytes(int nk);
-}  // namespace fvsr
-
 using namespace fvsr;
 
 namespace {
@@ -46,7 +41,7 @@ constexpr int kMaxNk = 2560;       // selection keeps one score row per query bl
 constexpr int kMaxHeads = 64;
 
 struct Dims {
-    int heads, s, nq, nk;
+    int heads, s, nq, nk, q_slices;
     int64_t channels, elt;
 };
 
@@ -63,6 +58,7 @@ fvsr_status check_params(const fvsr_lcsa_params* p, Dims* d, bool need_kv = true
     d->heads = p->heads;
     d->s = p->bh * p->bw;
     d->nq = p->q_slices * d->s;
+    d->q_slices = p->q_slices;
     d->nk = need_kv ? p->kv_slices * d->s : 0;
     d->channels = (int64_t)p->heads * 128;
     d->elt = p->dtype == FVSR_BF16 ? 2 : 4;
@@ -82,6 +78,7 @@ struct Workspace {
     float* probs;
     int32_t* kidx;
     int32_t* kcnt;
+    uint32_t* hist;
     size_t bytes;
 };
 
@@ -99,6 +96,7 @@ Workspace layout(const Dims& d, void* base) {
     w.probs = reinterpret_cast<float*>(take((size_t)d.heads * d.nq * d.nk * 4));
     w.kidx = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * d.nk * 4));
     w.kcnt = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * 4));
+    w.hist = reinterpret_cast<uint32_t*>(take(select_hist_bytes(d.heads, d.q_slices)));
     w.bytes = off;
     return w;
 }
@@ -129,10 +127,11 @@ fvsr_status check_device_sm100() {
 
 fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* pooled_q, const float* pooled_k,
                        const KvPages& pk_pages, int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs,
-                       cudaStream_t st) {
-    FVSR_CU(launch_select_scores(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range, probs, st),
+                       uint32_t* hist, cudaStream_t st) {
+    FVSR_CU(launch_select_scores(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range,
+                                 p->q_slices, probs, hist, st),
             "select scores launch");
-    FVSR_CU(launch_select_threshold(probs, d.heads, d.nq, d.nk, p->q_slices, p->topk, kidx, kcnt, mask, st),
+    FVSR_CU(launch_select_threshold(probs, d.heads, d.nq, d.nk, p->q_slices, p->topk, hist, kidx, kcnt, mask, st),
             "select threshold launch");
     return FVSR_OK;
 }
@@ -232,7 +231,7 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
         FVSR_CU(launch_pool(k, p->dtype, d.nk, (int)d.channels, w.pooled_k, nullptr, st), "pool k launch");
         pk = w.pooled_k;
     }
-    return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, st);
+    return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, w.hist, st);
 }
 
 fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
@@ -406,7 +405,7 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     int32_t* li = kidx ? kidx : w.kidx;
     int32_t* lc = kcnt ? kcnt : w.kcnt;
     FVSR_CU(launch_pool(q, pp.dtype, d.nq, (int)d.channels, w.pooled_q, nullptr, st), "pool q launch");
-    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, st);
+    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, st);
     if (s != FVSR_OK) return s;
     s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
                       out, st);

@@ -5,14 +5,15 @@
 //
 // One CTA per (head, query block) work item, ordered head-major so the CTAs in flight share one head's K/V in L2.
 // Warp roles (192 threads):
-//   warp 0      TMA producer: Q tile once, then K and V tiles of each kept key block into a 2-stage ring.
-//   warp 1      TMEM owner + single-thread MMA issuer: S_j = Q·K_jᵀ (SS-MMA, 128×128×128) one block ahead, then
-//               O += P_j·V_j (TS-MMA: P read from TMEM, V from shared memory as an MN-major operand).
+//   warp 0      TMA producer: Q tile once, then the K and V tiles of each kept key block into a 2-slot K ring
+//               (a slot frees when its S MMA completes) and a 3-slot V ring (freed when its PV MMA completes).
+//   warp 1      TMEM owner + single-thread MMA issuer: S_{j+1} = Q·K_{j+1}ᵀ (SS-MMA, 128×128×128) is issued ahead
+//               of O += P_j·V_j (TS-MMA: P read from TMEM, V from shared memory as an MN-major operand).
 //   warps 2..5  softmax warpgroup: thread = query row = TMEM lane. Reads S_j from TMEM, online softmax in fp32
-//               (exp2 on the MUFU pipe), rescales O in TMEM when the row max moved, writes P_j (bf16) to TMEM,
-//               and finally normalises O and stores it.
+//               (exp2 on the MUFU pipe), rescales O in TMEM only when a row maximum grew by more than 2^8 (lazy
+//               rescaling), writes P_j (bf16) to TMEM, and finally normalises O and stores it.
 // TMEM (512 columns): O [0,128), S0 [128,256), S1 [256,384), P0 [384,448), P1 [448,512).
-// Shared memory: Q 32 KB + 2 × (K 32 KB + V 32 KB), each tile as two 128-row × 64-column boxes in the 128-byte
+// Shared memory: Q 32 KB + K 2 × 32 KB + V 3 × 32 KB, each tile as two 128-row × 64-column boxes in the 128-byte
 // swizzled layout that TMA writes and the MMA descriptors read.
 // Every wait is bounded (4 s); on expiry the kernel raises a device timeout word that fvsr_device_check reports.
 #include <mutex>
@@ -28,23 +29,28 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 2;
+constexpr int kKSlots = 2;                        // K ring: a slot frees as soon as S_j = Q·K_jᵀ has completed
+constexpr int kVSlots = 3;                        // V ring: a slot frees when O += P_j·V_j has completed
 constexpr uint32_t kTileBytes = kBlock * kD * 2;  // 32 KB bf16 tile
 constexpr uint32_t kBoxBytes = kTileBytes / 2;    // one 128 × 64 box
 constexpr uint32_t kColO = 0, kColS0 = 128, kColP0 = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr int kThreads = 192;
+// Lazy rescaling: a row's running maximum (log2 units) is only raised — and O rescaled — when the block maximum
+// exceeds it by more than this; otherwise P entries may reach 2^8, which bf16 P and fp32 O/l carry exactly as well.
+constexpr float kRescaleThreshold = 8.0f;
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, 0, 0);   // A = Q (K-major), B = K (K-major)
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);  // A = P (TMEM), B = V (MN-major)
 
 // Shared-memory map (offsets from a 1024-byte aligned base).
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kTileBytes;                          // stage s: kOffK + s·2·kTileBytes
-constexpr uint32_t kOffBar = kTileBytes * (1 + 2 * kStages);   // barriers
-constexpr int kBarQ = 0, kBarKF = 1, kBarVF = kBarKF + kStages, kBarKVE = kBarVF + kStages, kBarSF = kBarKVE + kStages,
-              kBarPF = kBarSF + 2, kBarO = kBarPF + 2, kNumBars = kBarO + 1;
+constexpr uint32_t kOffK = kTileBytes;                          // K slot i at kOffK + i·kTileBytes
+constexpr uint32_t kOffV = kOffK + kKSlots * kTileBytes;        // V slot i at kOffV + i·kTileBytes
+constexpr uint32_t kOffBar = kOffV + kVSlots * kTileBytes;      // barriers
+constexpr int kBarQ = 0, kBarKF = 1, kBarKE = kBarKF + kKSlots, kBarVF = kBarKE + kKSlots, kBarVE = kBarVF + kVSlots,
+              kBarSF = kBarVE + kVSlots, kBarPF = kBarSF + 2, kBarPV = kBarPF + 2, kNumBars = kBarPV + 2;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffList = (kOffAbort + 4 + 15) & ~15u;
@@ -83,19 +89,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
     int32_t* s_list = reinterpret_cast<int32_t*>(smem + kOffList);
     auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+    auto wait = [&](int b, uint32_t parity) { return mbar_wait(bar(b), parity & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs); };
 
     if (threadIdx.x == 0) {
         mbar_init(bar(kBarQ), 1);
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar(kBarKF + s), 1);
-            mbar_init(bar(kBarVF + s), 1);
-            mbar_init(bar(kBarKVE + s), 1);
+        for (int i = 0; i < kKSlots; ++i) {
+            mbar_init(bar(kBarKF + i), 1);
+            mbar_init(bar(kBarKE + i), 1);
+        }
+        for (int i = 0; i < kVSlots; ++i) {
+            mbar_init(bar(kBarVF + i), 1);
+            mbar_init(bar(kBarVE + i), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar(kBarSF + b), 1);
             mbar_init(bar(kBarPF + b), 128);
+            mbar_init(bar(kBarPV + b), 1);
         }
-        mbar_init(bar(kBarO), 1);
         *abort_word = 0;
         fence_mbar_init();
     }
@@ -120,78 +130,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer: Q, then K_j and V_j in the order the MMA issuer consumes them ----------------
         if (lane == 0) {
             const int xq = h * kD;
             mbar_expect_tx(bar(kBarQ), kTileBytes);
             tma_load_2d(sbase + kOffQ, &tmQ, xq, qb * kBlock, bar(kBarQ));
             tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, xq + 64, qb * kBlock, bar(kBarQ));
             for (int j = 0; j < cnt; ++j) {
-                const int s = j % kStages;
-                if (j >= kStages &&
-                    !mbar_wait(bar(kBarKVE + s), (uint32_t)((j / kStages) - 1) & 1u, abort_word, &g_fvsr_timeout,
-                               kWaitLimitNs))
-                    break;
                 const int row = s_list[j] * kBlock;
-                const uint32_t dk = sbase + kOffK + (uint32_t)s * 2u * kTileBytes, dv = dk + kTileBytes;
-                mbar_expect_tx(bar(kBarKF + s), kTileBytes);
-                tma_load_2d(dk, &tmK, xq, row, bar(kBarKF + s));
-                tma_load_2d(dk + kBoxBytes, &tmK, xq + 64, row, bar(kBarKF + s));
-                mbar_expect_tx(bar(kBarVF + s), kTileBytes);
-                tma_load_2d(dv, &tmV, xq, row, bar(kBarVF + s));
-                tma_load_2d(dv + kBoxBytes, &tmV, xq + 64, row, bar(kBarVF + s));
+                const int ks = j % kKSlots, vs = j % kVSlots;
+                if (j >= kKSlots && !wait(kBarKE + ks, (uint32_t)(j / kKSlots - 1))) break;
+                const uint32_t dk = sbase + kOffK + (uint32_t)ks * kTileBytes;
+                mbar_expect_tx(bar(kBarKF + ks), kTileBytes);
+                tma_load_2d(dk, &tmK, xq, row, bar(kBarKF + ks));
+                tma_load_2d(dk + kBoxBytes, &tmK, xq + 64, row, bar(kBarKF + ks));
+                if (j >= kVSlots && !wait(kBarVE + vs, (uint32_t)(j / kVSlots - 1))) break;
+                const uint32_t dv = sbase + kOffV + (uint32_t)vs * kTileBytes;
+                mbar_expect_tx(bar(kBarVF + vs), kTileBytes);
+                tma_load_2d(dv, &tmV, xq, row, bar(kBarVF + vs));
+                tma_load_2d(dv + kBoxBytes, &tmV, xq + 64, row, bar(kBarVF + vs));
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer (one thread): S_{j+1} ahead of O += P_j·V_j ----------------
         if (lane == 0) {
-            bool ok = mbar_wait(bar(kBarQ), 0, abort_word, &g_fvsr_timeout, kWaitLimitNs);
+            bool ok = wait(kBarQ, 0);
             auto issue_s = [&](int j) -> bool {
-                const int s = j % kStages;
-                if (!mbar_wait(bar(kBarKF + s), (uint32_t)(j / kStages) & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs))
-                    return false;
+                const int ks = j % kKSlots;
+                if (!wait(kBarKF + ks, (uint32_t)(j / kKSlots))) return false;
                 tc_fence_after();
                 const uint32_t d = tmem + kColS0 + 128u * (uint32_t)(j & 1);
-                const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + (uint32_t)s * 2u * kTileBytes;
+                const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + (uint32_t)ks * kTileBytes;
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const uint32_t off = (uint32_t)(ks >> 2) * kBoxBytes + (uint32_t)(ks & 3) * 32u;
-                    mma_ss(d, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), kIdescS, ks > 0 ? 1u : 0u);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (uint32_t)(kk >> 2) * kBoxBytes + (uint32_t)(kk & 3) * 32u;
+                    mma_ss(d, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
                 }
+                mma_commit(bar(kBarKE + ks));
                 mma_commit(bar(kBarSF + (j & 1)));
                 return true;
             };
             if (ok) ok = issue_s(0);
             for (int j = 0; ok && j < cnt; ++j) {
                 if (j + 1 < cnt && !issue_s(j + 1)) break;
-                const int s = j % kStages;
-                if (!mbar_wait(bar(kBarVF + s), (uint32_t)(j / kStages) & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs))
-                    break;
-                if (!mbar_wait(bar(kBarPF + (j & 1)), (uint32_t)(j >> 1) & 1u, abort_word, &g_fvsr_timeout,
-                               kWaitLimitNs))
-                    break;
+                const int vs = j % kVSlots;
+                if (!wait(kBarVF + vs, (uint32_t)(j / kVSlots))) break;
+                if (!wait(kBarPF + (j & 1), (uint32_t)(j >> 1))) break;
                 tc_fence_after();
-                const uint32_t va = sbase + kOffK + (uint32_t)s * 2u * kTileBytes + kTileBytes;
+                const uint32_t va = sbase + kOffV + (uint32_t)vs * kTileBytes;
                 const uint32_t pa = tmem + kColP0 + 64u * (uint32_t)(j & 1);
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                    mma_ts(tmem + kColO, pa + 8u * (uint32_t)ks, smem_desc(va + (uint32_t)ks * 2048u, kBoxBytes, 1024),
-                           kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
-                mma_commit(bar(kBarKVE + s));
-                mma_commit(bar(kBarO));
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_ts(tmem + kColO, pa + 8u * (uint32_t)kk, smem_desc(va + (uint32_t)kk * 2048u, kBoxBytes, 1024),
+                           kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(bar(kBarVE + vs));
+                mma_commit(bar(kBarPV + (j & 1)));
             }
         }
     } else {
-        // ---------------- softmax warpgroup ----------------
+        // ---------------- softmax warpgroup: thread = query row = TMEM lane ----------------
         const int quarter = warp & 3;  // TMEM lanes [32·quarter, 32·quarter + 32) are this warp's
         const int r = quarter * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
         const float sl2 = a.scale_log2;
         float m = -INFINITY, l = 0.0f;
         bool ok = true;
+        auto wait_warp = [&](int b, uint32_t parity) { return __all_sync(0xffffffffu, wait(b, parity)); };
         for (int j = 0; j < cnt; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarSF + (j & 1)), (uint32_t)(j >> 1) & 1u, abort_word,
-                                                    &g_fvsr_timeout, kWaitLimitNs))) {
+            if (!wait_warp(kBarSF + (j & 1), (uint32_t)(j >> 1))) {
                 ok = false;
                 break;
             }
@@ -206,41 +212,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_wait(sv + 32);
             tmem_ld_wait(sv + 64);
             tmem_ld_wait(sv + 96);
-            float mx = -INFINITY;
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
-            const float m_new = fmaxf(m, mx * sl2);
+            for (int c = 0; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sv[c]));
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+            const bool need = mx > m + kRescaleThreshold;  // always true on the first block (m = −inf)
+            const float m_new = need ? fmaxf(m, mx) : m;
+            const float alpha = need ? ex2_approx(m - m_new) : 1.0f;
             const float neg = -m_new;
             uint32_t pk[64];
-            float rs = 0.0f;
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < 64; ++c) {
                 const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, neg));
                 const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, neg));
-                rs += p0 + p1;
+                rs4[c & 3] += p0 + p1;
                 pk[c] = pack_bf16x2(p0, p1);
             }
-            const float alpha = ex2_approx(m - m_new);
-            l = l * alpha + rs;
+            l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
             m = m_new;
-            if (j > 0) {
-                if (!__all_sync(0xffffffffu, mbar_wait(bar(kBarO), (uint32_t)(j - 1) & 1u, abort_word, &g_fvsr_timeout,
-                                                        kWaitLimitNs))) {
+            if (j > 0 && __any_sync(0xffffffffu, need)) {
+                // O holds Σ_{i<j} P_i·V_i once PV_{j−1} has completed; rescale it in TMEM
+                if (!wait_warp(kBarPV + ((j - 1) & 1), (uint32_t)((j - 1) >> 1))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t ov[32];
-                        tmem_ld32(lane_base + kColO + 32u * c, ov);
-                        tmem_ld_wait(ov);
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t ov[32];
+                    tmem_ld32(lane_base + kColO + 32u * c, ov);
+                    tmem_ld_wait(ov);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st32(lane_base + kColO + 32u * c, ov);
-                    }
+                    for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                    tmem_st32(lane_base + kColO + 32u * c, ov);
                 }
+            }
+            if (j >= 2 && !wait_warp(kBarPV + (j & 1), (uint32_t)((j - 2) >> 1))) {  // PV_{j−2} read P[j&1]
+                ok = false;
+                break;
             }
             const uint32_t pcol = lane_base + kColP0 + 64u * (uint32_t)(j & 1);
             tmem_st32(pcol, pk);
@@ -249,8 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(bar(kBarPF + (j & 1)));
         }
-        if (ok && __all_sync(0xffffffffu,
-                             mbar_wait(bar(kBarO), (uint32_t)(cnt - 1) & 1u, abort_word, &g_fvsr_timeout, kWaitLimitNs))) {
+        if (ok && wait_warp(kBarPV + ((cnt - 1) & 1), (uint32_t)((cnt - 1) >> 1))) {
             tc_fence_after();
             const float inv = 1.0f / l;
             __nv_bfloat16* orow = a.out + ((int64_t)qb * kBlock + r) * ld + h * kD;

@@ -28,9 +28,13 @@ __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __
 cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
                         cudaStream_t st);
 cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
-                                 int bh, int bw, int local_range, float* probs, cudaStream_t st);
+                                 int bh, int bw, int local_range, int q_slices, float* probs, uint32_t* hist,
+                                 cudaStream_t st);
 cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
-                                    int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st);
+                                    uint32_t* hist, int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st);
+size_t select_scores_smem_bytes(int nk);
+size_t select_hist_bytes(int heads, int q_slices);
+size_t attn_bf16_smem_bytes(int nk);
 cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
                                  cudaStream_t st);
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
