@@ -332,7 +332,7 @@ def run_ours(args):
                          "traffic": (tr or {}).get("bytes_per_launch"),
                          "traffic_source": (tr or {}).get("source")},
             "clocks": clk,
-            "gpu_launches": 5 * layers * args.steps,
+            "gpu_launches": 7 * layers * args.steps,  # per layer: pool, scores, softmax, 2 histogram passes, finish, attention
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:

@@ -129,7 +129,7 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
                        const KvPages& pk_pages, int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs,
                        uint32_t* hist, cudaStream_t st) {
     FVSR_CU(launch_select_scores(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range,
-                                 p->q_slices, probs, hist, st),
+                                 p->q_slices, p->topk, probs, hist, st),
             "select scores launch");
     FVSR_CU(launch_select_threshold(probs, d.heads, d.nq, d.nk, p->q_slices, p->topk, hist, kidx, kcnt, mask, st),
             "select threshold launch");
@@ -225,12 +225,10 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
     if (!workspace || workspace_bytes < w.bytes)
         return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    FVSR_CU(launch_pool(q, p->dtype, d.nq, (int)d.channels, w.pooled_q, nullptr, st), "pool q launch");
-    const float* pk = pooled_k;
-    if (!pk) {
-        FVSR_CU(launch_pool(k, p->dtype, d.nk, (int)d.channels, w.pooled_k, nullptr, st), "pool k launch");
-        pk = w.pooled_k;
-    }
+    const float* pk = pooled_k ? pooled_k : w.pooled_k;
+    FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, pooled_k ? nullptr : k, pooled_k ? 0 : d.nk, w.pooled_k, p->dtype,
+                         (int)d.channels, st),
+            "pool launch");
     return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, w.hist, st);
 }
 

@@ -4,16 +4,20 @@
 // selected key blocks by index with an fp32 online softmax; an empty query block writes zeros).
 //
 // One CTA per (head, query block) work item, ordered head-major so the CTAs in flight share one head's K/V in L2.
-// Warp roles (192 threads):
-//   warp 0      TMA producer: Q tile once, then the K and V tiles of each kept key block into a 2-slot K ring
-//               (a slot frees when its S MMA completes) and a 3-slot V ring (freed when its PV MMA completes).
-//   warp 1      TMEM owner + single-thread MMA issuer: S_{j+1} = Q·K_{j+1}ᵀ (SS-MMA, 128×128×128) is issued ahead
-//               of O += P_j·V_j (TS-MMA: P read from TMEM, V from shared memory as an MN-major operand).
-//   warps 2..5  softmax warpgroup: thread = query row = TMEM lane. Reads S_j from TMEM, online softmax in fp32
-//               (exp2 on the MUFU pipe), rescales O in TMEM only when a row maximum grew by more than 2^8 (lazy
-//               rescaling), writes P_j (bf16) to TMEM, and finally normalises O and stores it.
-// TMEM (512 columns): O [0,128), S0 [128,256), S1 [256,384), P0 [384,448), P1 [448,512).
-// Shared memory: Q 32 KB + K 2 × 32 KB + V 3 × 32 KB, each tile as two 128-row × 64-column boxes in the 128-byte
+// Warp roles (320 threads):
+//   warp 0      TMA producer: the Q tile, then the K and V tiles of each kept key block into a 3-slot K ring (a slot
+//               frees when its S MMA completes) and a 2-slot V ring (freed when its PV MMA completes).
+//   warp 1      TMEM owner + single-thread MMA issuer: S_j = Q·K_jᵀ (SS-MMA, 128×128×128) is issued two blocks
+//               ahead of O += P_j·V_j (TS-MMA: P read from TMEM, V from shared memory as an MN-major operand), so two
+//               S tiles are queued on the tensor core while the softmax of block j is in flight.
+//   warps 2..9  softmax, two sets of four warps (one warp per TMEM lane quarter each): set 0 takes the even key
+//               blocks, set 1 the odd ones, so two blocks are in flight on every SM sub-partition. Thread = query row
+//               = TMEM lane. Per block: row maximum from S_j, the running maximum handed over from the other set
+//               (raised, and O rescaled in TMEM, only when it grew by more than 2^8 — lazy rescaling), exp2 on the
+//               MUFU pipe, P_j (bf16) written over the first half of S_j's TMEM columns. Each set keeps its own
+//               partial row sum; at the end the two are combined and O is normalised and stored.
+// TMEM (512 columns): O [0,128), S0/P0 [128,256), S1/P1 [256,384), S2/P2 [384,512).
+// Shared memory: Q 32 KB + K 3 × 32 KB + V 2 × 32 KB, each tile as two 128-row × 64-column boxes in the 128-byte
 // swizzled layout that TMA writes and the MMA descriptors read.
 // Every wait is bounded (4 s); on expiry the kernel raises a device timeout word that fvsr_device_check reports.
 #include <mutex>
@@ -29,20 +33,23 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kKSlots = 2;                        // K ring: a slot frees as soon as S_j = Q·K_jᵀ has completed
-constexpr int kVSlots = 3;                        // V ring: a slot frees when O += P_j·V_j has completed
+constexpr int kKSlots = 3;                        // K ring: a slot frees as soon as S_j = Q·K_jᵀ has completed
+constexpr int kVSlots = 2;                        // V ring: a slot frees when O += P_j·V_j has completed
+constexpr int kSBufs = 3;                         // S/P buffers in TMEM: S_{j+1} and S_{j+2} queue behind PV_j
 constexpr uint32_t kTileBytes = kBlock * kD * 2;  // 32 KB bf16 tile
 constexpr uint32_t kBoxBytes = kTileBytes / 2;    // one 128 × 64 box
-constexpr uint32_t kColO = 0, kColS0 = 128, kColP0 = 384;
+// TMEM columns: O (fp32 128) then three S buffers (fp32 128 each); P_j (bf16 pairs) overwrites the first 64
+// columns of its own S buffer once its row maximum is known.
+constexpr uint32_t kColO = 0, kColS0 = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 2 role warps + 2 softmax sets of 4 warps
 // Lazy rescaling: a row's running maximum (log2 units) is only raised — and O rescaled — when the block maximum
 // exceeds it by more than this; otherwise P entries may reach 2^8, which bf16 P and fp32 O/l carry exactly as well.
 constexpr float kRescaleThreshold = 8.0f;
 
-constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, 0, 0);   // A = Q (K-major), B = K (K-major)
-constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);  // A = P (TMEM), B = V (MN-major)
+constexpr uint32_t kIdescS = idesc_bf16_f32(128, 128, 0, 0);   // A = Q, B = K (both K-major shared memory)
+constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, 0, 1);  // A = P (TMEM), B = V (MN-major shared memory)
 
 // Shared-memory map (offsets from a 1024-byte aligned base).
 constexpr uint32_t kOffQ = 0;
@@ -50,10 +57,13 @@ constexpr uint32_t kOffK = kTileBytes;                          // K slot i at k
 constexpr uint32_t kOffV = kOffK + kKSlots * kTileBytes;        // V slot i at kOffV + i·kTileBytes
 constexpr uint32_t kOffBar = kOffV + kVSlots * kTileBytes;      // barriers
 constexpr int kBarQ = 0, kBarKF = 1, kBarKE = kBarKF + kKSlots, kBarVF = kBarKE + kKSlots, kBarVE = kBarVF + kVSlots,
-              kBarSF = kBarVE + kVSlots, kBarPF = kBarSF + 2, kBarPV = kBarPF + 2, kNumBars = kBarPV + 2;
+              kBarSF = kBarVE + kVSlots, kBarPF = kBarSF + kSBufs, kBarPV = kBarPF + kSBufs, kBarM = kBarPV + 2,
+              kBarFin = kBarM + 2, kNumBars = kBarFin + 1;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-constexpr uint32_t kOffList = (kOffAbort + 4 + 15) & ~15u;
+constexpr uint32_t kOffM = (kOffAbort + 4 + 15) & ~15u;         // running max handoff: [2 parities][128] f32
+constexpr uint32_t kOffFin = kOffM + 2 * 128 * 4;               // final (l, m_ref) of each set: [2][2][128] f32
+constexpr uint32_t kOffList = kOffFin + 2 * 2 * 128 * 4;
 
 struct AttnArgs {
     const int32_t* kidx;
@@ -101,11 +111,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(kBarVF + i), 1);
             mbar_init(bar(kBarVE + i), 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kSBufs; ++b) {
             mbar_init(bar(kBarSF + b), 1);
             mbar_init(bar(kBarPF + b), 128);
-            mbar_init(bar(kBarPV + b), 1);
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(kBarPV + b), 1);
+            mbar_init(bar(kBarM + b), 128);
+        }
+        mbar_init(bar(kBarFin), 256);
         *abort_word = 0;
         fence_mbar_init();
     }
@@ -130,36 +144,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer: Q, then K_j and V_j in the order the MMA issuer consumes them ----------------
+        // ---------------- TMA producer: Q, then K and V in the order the MMA issuer consumes them ----------------
         if (lane == 0) {
-            const int xq = h * kD;
+            const int x0 = h * kD;
             mbar_expect_tx(bar(kBarQ), kTileBytes);
-            tma_load_2d(sbase + kOffQ, &tmQ, xq, qb * kBlock, bar(kBarQ));
-            tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, xq + 64, qb * kBlock, bar(kBarQ));
-            for (int j = 0; j < cnt; ++j) {
-                const int row = s_list[j] * kBlock;
-                const int ks = j % kKSlots, vs = j % kVSlots;
-                if (j >= kKSlots && !wait(kBarKE + ks, (uint32_t)(j / kKSlots - 1))) break;
+            tma_load_2d(sbase + kOffQ, &tmQ, x0, qb * kBlock, bar(kBarQ));
+            tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, x0 + 64, qb * kBlock, bar(kBarQ));
+            auto load_k = [&](int j) -> bool {
+                const int ks = j % kKSlots;
+                if (j >= kKSlots && !wait(kBarKE + ks, (uint32_t)(j / kKSlots - 1))) return false;
                 const uint32_t dk = sbase + kOffK + (uint32_t)ks * kTileBytes;
                 mbar_expect_tx(bar(kBarKF + ks), kTileBytes);
-                tma_load_2d(dk, &tmK, xq, row, bar(kBarKF + ks));
-                tma_load_2d(dk + kBoxBytes, &tmK, xq + 64, row, bar(kBarKF + ks));
-                if (j >= kVSlots && !wait(kBarVE + vs, (uint32_t)(j / kVSlots - 1))) break;
+                tma_load_2d(dk, &tmK, x0, s_list[j] * kBlock, bar(kBarKF + ks));
+                tma_load_2d(dk + kBoxBytes, &tmK, x0 + 64, s_list[j] * kBlock, bar(kBarKF + ks));
+                return true;
+            };
+            auto load_v = [&](int j) -> bool {
+                const int vs = j % kVSlots;
+                if (j >= kVSlots && !wait(kBarVE + vs, (uint32_t)(j / kVSlots - 1))) return false;
                 const uint32_t dv = sbase + kOffV + (uint32_t)vs * kTileBytes;
                 mbar_expect_tx(bar(kBarVF + vs), kTileBytes);
-                tma_load_2d(dv, &tmV, xq, row, bar(kBarVF + vs));
-                tma_load_2d(dv + kBoxBytes, &tmV, xq + 64, row, bar(kBarVF + vs));
-            }
+                tma_load_2d(dv, &tmV, x0, s_list[j] * kBlock, bar(kBarVF + vs));
+                tma_load_2d(dv + kBoxBytes, &tmV, x0 + 64, s_list[j] * kBlock, bar(kBarVF + vs));
+                return true;
+            };
+            bool ok = load_k(0) && (cnt < 2 || load_k(1));
+            for (int j = 0; ok && j < cnt; ++j) ok = load_v(j) && (j + 2 >= cnt || load_k(j + 2));
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (one thread): S_{j+1} ahead of O += P_j·V_j ----------------
+        // ---------------- MMA issuer (one thread): S_{j+2} and S_{j+1} queued ahead of O += P_j·V_j ----------------
         if (lane == 0) {
             bool ok = wait(kBarQ, 0);
             auto issue_s = [&](int j) -> bool {
                 const int ks = j % kKSlots;
                 if (!wait(kBarKF + ks, (uint32_t)(j / kKSlots))) return false;
                 tc_fence_after();
-                const uint32_t d = tmem + kColS0 + 128u * (uint32_t)(j & 1);
+                const uint32_t d = tmem + kColS0 + 128u * (uint32_t)(j % kSBufs);
                 const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + (uint32_t)ks * kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
@@ -167,18 +187,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_ss(d, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(bar(kBarKE + ks));
-                mma_commit(bar(kBarSF + (j & 1)));
+                mma_commit(bar(kBarSF + j % kSBufs));
                 return true;
             };
-            if (ok) ok = issue_s(0);
+            if (ok) ok = issue_s(0) && (cnt < 2 || issue_s(1));
             for (int j = 0; ok && j < cnt; ++j) {
-                if (j + 1 < cnt && !issue_s(j + 1)) break;
+                // S_{j+2} lands in the buffer that held P_{j−1}; PV_{j−1} was issued before it, and tcgen05 MMAs of
+                // one thread execute in issue order
+                if (j + 2 < cnt && !issue_s(j + 2)) break;
                 const int vs = j % kVSlots;
                 if (!wait(kBarVF + vs, (uint32_t)(j / kVSlots))) break;
-                if (!wait(kBarPF + (j & 1), (uint32_t)(j >> 1))) break;
+                if (!wait(kBarPF + j % kSBufs, (uint32_t)(j / kSBufs))) break;
                 tc_fence_after();
                 const uint32_t va = sbase + kOffV + (uint32_t)vs * kTileBytes;
-                const uint32_t pa = tmem + kColP0 + 64u * (uint32_t)(j & 1);
+                const uint32_t pa = tmem + kColS0 + 128u * (uint32_t)(j % kSBufs);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_ts(tmem + kColO, pa + 8u * (uint32_t)kk, smem_desc(va + (uint32_t)kk * 2048u, kBoxBytes, 1024),
@@ -188,26 +210,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- softmax warpgroup: thread = query row = TMEM lane ----------------
+        // ---------------- softmax: set `st` handles blocks j ≡ st (mod 2), thread = query row ----------------
+        const int st = (warp - 2) >> 2;
         const int quarter = warp & 3;  // TMEM lanes [32·quarter, 32·quarter + 32) are this warp's
         const int r = quarter * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        float* m_x = reinterpret_cast<float*>(smem + kOffM);
+        float* fin = reinterpret_cast<float*>(smem + kOffFin);
         const float sl2 = a.scale_log2;
-        float m = -INFINITY, l = 0.0f;
+        float l = 0.0f, mref = -INFINITY;  // this set's partial row sum and the maximum it is relative to
         bool ok = true;
         auto wait_warp = [&](int b, uint32_t parity) { return __all_sync(0xffffffffu, wait(b, parity)); };
-        for (int j = 0; j < cnt; ++j) {
-            if (!wait_warp(kBarSF + (j & 1), (uint32_t)(j >> 1))) {
+        for (int j = st; j < cnt; j += 2) {
+            if (!wait_warp(kBarSF + j % kSBufs, (uint32_t)(j / kSBufs))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
+            const uint32_t sbuf = lane_base + kColS0 + 128u * (uint32_t)(j % kSBufs);
             uint32_t sv[128];
-            const uint32_t scol = lane_base + kColS0 + 128u * (uint32_t)(j & 1);
-            tmem_ld32(scol, sv);
-            tmem_ld32(scol + 32, sv + 32);
-            tmem_ld32(scol + 64, sv + 64);
-            tmem_ld32(scol + 96, sv + 96);
+            tmem_ld32(sbuf, sv);
+            tmem_ld32(sbuf + 32, sv + 32);
+            tmem_ld32(sbuf + 64, sv + 64);
+            tmem_ld32(sbuf + 96, sv + 96);
             tmem_ld_wait(sv);
             tmem_ld_wait(sv + 32);
             tmem_ld_wait(sv + 64);
@@ -216,28 +241,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sv[c]));
             const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-            const bool need = mx > m + kRescaleThreshold;  // always true on the first block (m = −inf)
-            const float m_new = need ? fmaxf(m, mx) : m;
-            const float alpha = need ? ex2_approx(m - m_new) : 1.0f;
-            const float neg = -m_new;
-            uint32_t pk[64];
-            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, neg));
-                const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, neg));
-                rs4[c & 3] += p0 + p1;
-                pk[c] = pack_bf16x2(p0, p1);
+            // running maximum after block j−1 comes from the other set (block j−1 is theirs)
+            float m_prev = -INFINITY;
+            if (j > 0) {
+                if (!wait_warp(kBarM + ((j - 1) & 1), (uint32_t)((j - 1) >> 1))) {
+                    ok = false;
+                    break;
+                }
+                m_prev = m_x[((j - 1) & 1) * 128 + r];
             }
-            l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
-            m = m_new;
+            const bool need = mx > m_prev + kRescaleThreshold;  // always true on block 0 (m_prev = −inf)
+            const float m_j = need ? fmaxf(m_prev, mx) : m_prev;
+            m_x[(j & 1) * 128 + r] = m_j;
+            mbar_arrive(bar(kBarM + (j & 1)));  // published before the exponentials so block j+1 can start
             if (j > 0 && __any_sync(0xffffffffu, need)) {
-                // O holds Σ_{i<j} P_i·V_i once PV_{j−1} has completed; rescale it in TMEM
+                // O holds Σ_{i<j} P_i·V_i relative to m_prev once PV_{j−1} has completed; bring it to m_j
                 if (!wait_warp(kBarPV + ((j - 1) & 1), (uint32_t)((j - 1) >> 1))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const float alpha = need ? ex2_approx(m_prev - m_j) : 1.0f;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t ov[32];
@@ -248,25 +272,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(lane_base + kColO + 32u * c, ov);
                 }
             }
-            if (j >= 2 && !wait_warp(kBarPV + (j & 1), (uint32_t)((j - 2) >> 1))) {  // PV_{j−2} read P[j&1]
-                ok = false;
-                break;
+            const float neg = -m_j;
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {  // 64 key columns → 32 packed P columns per store
+                uint32_t pk[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(sv[64 * h2 + 2 * c]), sl2, neg));
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(sv[64 * h2 + 2 * c + 1]), sl2, neg));
+                    rs4[c & 3] += p0 + p1;
+                    pk[c] = pack_bf16x2(p0, p1);
+                }
+                tmem_st32(sbuf + 32u * (uint32_t)h2, pk);
             }
-            const uint32_t pcol = lane_base + kColP0 + 64u * (uint32_t)(j & 1);
-            tmem_st32(pcol, pk);
-            tmem_st32(pcol + 32, pk + 32);
+            if (m_j != mref) {  // bring this set's partial sum to the current maximum
+                l *= ex2_approx(mref - m_j);
+                mref = m_j;
+            }
+            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(bar(kBarPF + (j & 1)));
+            mbar_arrive(bar(kBarPF + j % kSBufs));
         }
+        // the row sum: both sets' partial sums brought to the final maximum (the larger m_ref), added in set order
+        fin[(st * 2) * 128 + r] = l;
+        fin[(st * 2 + 1) * 128 + r] = mref;
+        mbar_arrive(bar(kBarFin));
+        if (ok) ok = wait_warp(kBarFin, 0);
         if (ok && wait_warp(kBarPV + ((cnt - 1) & 1), (uint32_t)((cnt - 1) >> 1))) {
             tc_fence_after();
-            const float inv = 1.0f / l;
-            __nv_bfloat16* orow = a.out + ((int64_t)qb * kBlock + r) * ld + h * kD;
+            const float l0 = fin[r], m0 = fin[128 + r], l1 = fin[256 + r], m1 = fin[384 + r];
+            const float mf = fmaxf(m0, m1);
+            const float l_row = l0 * ex2_approx(m0 - mf) + l1 * ex2_approx(m1 - mf);
+            const float inv = 1.0f / l_row;
+            __nv_bfloat16* orow = a.out + ((int64_t)qb * kBlock + r) * ld + h * kD + 64 * st;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t ov[32];
-                tmem_ld32(lane_base + kColO + 32u * c, ov);
+                tmem_ld32(lane_base + kColO + 64u * (uint32_t)st + 32u * c, ov);
                 tmem_ld_wait(ov);
                 uint32_t w[16];
 #pragma unroll

@@ -27,8 +27,11 @@ __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __
 // ---- launchers (each returns the launch's cudaError_t) ----
 cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
                         cudaStream_t st);
+// Pools two tensors (n1 and n2 blocks) in one launch.
+cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,
+                         float* out2, int dtype, int channels, cudaStream_t st);
 cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
-                                 int bh, int bw, int local_range, int q_slices, float* probs, uint32_t* hist,
+                                 int bh, int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist,
                                  cudaStream_t st);
 cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
                                     uint32_t* hist, int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st);

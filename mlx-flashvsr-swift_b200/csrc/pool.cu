@@ -13,41 +13,69 @@ namespace {
 constexpr int kPoolLanes = 64;               // channel lanes per CTA
 constexpr int kPoolChannels = kPoolLanes * 8;  // 512 channels per CTA
 
+// Blocks [0, n1) pool x into out (and copy to copy_dst); blocks [n1, gridDim.y) pool x2 into out2, so the query and
+// key pools of one selection share a launch.
 template <int DT>
-__global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, int channels,
-                                                   float* __restrict__ out, void* __restrict__ copy_dst) {
+__global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, int channels, float* __restrict__ out,
+                                                   void* __restrict__ copy_dst, int n1, const void* __restrict__ x2,
+                                                   float* __restrict__ out2) {
     __shared__ float part[4][kPoolChannels];
     const int lane = threadIdx.x & (kPoolLanes - 1);
     const int g = threadIdx.x / kPoolLanes;  // token group: tokens [32g, 32g + 32)
     const int c0 = blockIdx.x * kPoolChannels + lane * 8;
-    const int64_t b = blockIdx.y;
+    int64_t b = blockIdx.y;
+    if (b >= n1) {
+        b -= n1;
+        x = x2;
+        out = out2;
+        copy_dst = nullptr;
+    }
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
     if (c0 < channels) {
-#pragma unroll 4
-        for (int t = 32 * g; t < 32 * g + 32; ++t) {
-            const int64_t off = (b * kBlock + t) * (int64_t)channels + c0;
+        // 8 tokens per batch: all 8 loads are issued before their sums (which stay in token order)
+        for (int t0 = 32 * g; t0 < 32 * g + 32; t0 += 8) {
             if (DT == 1) {
-                const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
-                if (copy_dst) *reinterpret_cast<uint4*>(static_cast<uint16_t*>(copy_dst) + off) = v;
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                uint4 v[8];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[2 * i] = __fadd_rn(acc[2 * i], bf16_bits_to_float(w[i] & 0xFFFFu));
-                    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_bits_to_float(w[i] >> 16));
+                for (int u = 0; u < 8; ++u)
+                    v[u] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) +
+                                                               (b * kBlock + t0 + u) * (int64_t)channels + c0));
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (copy_dst)
+                        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(copy_dst) +
+                                                  (b * kBlock + t0 + u) * (int64_t)channels + c0) = v[u];
+                    const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[2 * i] = __fadd_rn(acc[2 * i], bf16_bits_to_float(w[i] & 0xFFFFu));
+                        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_bits_to_float(w[i] >> 16));
+                    }
                 }
             } else {
-                const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
-                const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-                if (copy_dst) {
-                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(copy_dst) + off);
-                    dst[0] = v0;
-                    dst[1] = v1;
-                }
-                const float w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                float4 v[8][2];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], w[i]);
+                for (int u = 0; u < 8; ++u) {
+                    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) +
+                                                                        (b * kBlock + t0 + u) * (int64_t)channels + c0);
+                    v[u][0] = __ldg(src);
+                    v[u][1] = __ldg(src + 1);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (copy_dst) {
+                        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(copy_dst) +
+                                                                (b * kBlock + t0 + u) * (int64_t)channels + c0);
+                        dst[0] = v[u][0];
+                        dst[1] = v[u][1];
+                    }
+                    const float w[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                                        v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], w[i]);
+                }
             }
         }
     }
@@ -72,12 +100,17 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
 
 cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
                         cudaStream_t st) {
-    if (nblocks == 0) return cudaSuccess;
-    dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)nblocks);
+    return launch_pool2(x, nblocks, out, copy_dst, nullptr, 0, nullptr, dtype, channels, st);
+}
+
+cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,
+                         float* out2, int dtype, int channels, cudaStream_t st) {
+    if (n1 + n2 == 0) return cudaSuccess;
+    dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)(n1 + n2));
     if (dtype == 1)
-        pool_kernel<1><<<grid, 256, 0, st>>>(x, channels, out, copy_dst);
+        pool_kernel<1><<<grid, 256, 0, st>>>(x1, channels, out1, copy_dst, (int)n1, x2, out2);
     else
-        pool_kernel<0><<<grid, 256, 0, st>>>(x, channels, out, copy_dst);
+        pool_kernel<0><<<grid, 256, 0, st>>>(x1, channels, out1, copy_dst, (int)n1, x2, out2);
     return cudaGetLastError();
 }
 

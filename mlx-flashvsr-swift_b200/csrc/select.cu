@@ -1,9 +1,11 @@
 // select.cu — LCSA block selection (draftBlockMaskAndProbs, DiT.swift:158-174) on pooled fp32 Q/K.
 //
 // Kernels (in launch order):
-//   select_scores_kernel    per (head, 8 query blocks): block scores pq·pk / sqrt(d) (fixed-order fmaf dot), the
-//                           spatial locality mask (DiT.swift:130-145, computed from (bh, bw, R) instead of a table),
-//                           the softmax over key blocks → probs (H, Nq, Nk), and pass 1 of the radix select.
+//   select_scores_kernel    block scores pq·pk / sqrt(d) (fixed-order fmaf dot over 128 dims) with the spatial locality
+//                           mask (DiT.swift:130-145, computed from (bh, bw, R) instead of a table; −inf outside),
+//                           one 32 × 64 (query block × key block) tile per CTA → scores (H, Nq, Nk).
+//   select_softmax_kernel   one warp per (head, query block) row: softmax over key blocks, in place → probs, and
+//                           pass 1 of the radix select's histogram.
 //   select_hist_kernel ×2   passes 2 and 3 of an MSB-first radix select (11 + 11 + 10 bits of the fp32 patterns —
 //                           probabilities are ≥ 0, so unsigned order = float order; no sort) that finds, per
 //                           (head, query slice) row of n = (Nq/q_slices)·Nk entries, the exact
@@ -23,22 +25,22 @@ namespace fvsr {
 
 namespace {
 
-constexpr int kQR = 8;    // query blocks per CTA (one per warp)
-constexpr int kKT = 64;   // key blocks per staged tile
-constexpr int kKS = 132;  // padded fp32 row stride of the staged key tile (conflict-free float4 reads)
+constexpr int kTI = 64;   // query blocks per score tile
+constexpr int kTJ = 64;   // key blocks per score tile
+constexpr int kPS = 132;  // padded fp32 row stride of the staged pooled rows
+constexpr int kSoftRows = 8;  // (head, query block) rows per softmax CTA, one per warp
 
 __device__ __forceinline__ float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
 
-// e^x: the softmax exponential of the selection (see the file comment for the method).
+// e^x: the softmax exponential of the selection (see the file comment for the method). Branch-free: the special
+// cases are selected at the end, so a warp never diverges on it.
 __device__ __forceinline__ float fvsr_exp(float x) {
-    if (x != x) return x;
-    if (x < -104.0f) return 0.0f;
-    if (x > 88.72f) return INFINITY;
     const float log2e = 1.44269502925872802734375f;
     const float ln2_hi = 0.693145751953125f;
     const float ln2_lo = 1.428606765330187045e-06f;
-    const float n = rintf(__fmul_rn(x, log2e));
-    float r = __fmaf_rn(-n, ln2_hi, x);
+    const float xc = fminf(fmaxf(x, -104.0f), 88.72f);  // keeps n in range; the out-of-range results are selected below
+    const float n = rintf(__fmul_rn(xc, log2e));
+    float r = __fmaf_rn(-n, ln2_hi, xc);
     r = __fmaf_rn(-n, ln2_lo, r);
     float p = 1.0f / 5040.0f;
     p = __fmaf_rn(p, r, 1.0f / 720.0f);
@@ -49,20 +51,29 @@ __device__ __forceinline__ float fvsr_exp(float x) {
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
     const int ni = (int)n;
-    if (ni >= -126) {
-        if (ni > 127) return INFINITY;
-        return __fmul_rn(p, pow2i(ni));
-    }
-    return __fmul_rn(__fmul_rn(p, pow2i(ni + 64)), pow2i(-64));
+    // 2^n as one multiply for −126 ≤ n ≤ 127, else (p·2^(n+64))·2^−64 or (p·2^(n−1))·2 — the second factor is 1 in
+    // the common case, which leaves the product unchanged
+    const bool lo = ni < -126, hi = ni > 127;
+    const int e1 = lo ? ni + 64 : (hi ? ni - 1 : ni);
+    const float s2 = lo ? pow2i(-64) : (hi ? 2.0f : 1.0f);
+    float y = __fmul_rn(__fmul_rn(p, pow2i(e1)), s2);
+    y = x < -104.0f ? 0.0f : y;
+    y = x > 88.72f ? INFINITY : y;
+    return x != x ? x : y;
 }
 
 // Exact k-th largest by a 3-pass MSB-first radix select on the fp32 bit patterns (probabilities are ≥ 0, so the
 // unsigned order of the bits is the float order): pass 1 bins bits [31:21] (2048 bins), pass 2 bits [20:10] (2048),
 // pass 3 bits [9:0] (1024). Each pass only counts the entries whose higher bits equal the bins chosen so far.
 constexpr int kBins1 = 2048, kBins2 = 2048, kBins3 = 1024;
-constexpr int kHistPerRow = kBins1 + kBins2 + kBins3;
-constexpr int kHistChunk = 8192;  // entries of one selection row per histogram CTA
-constexpr int kFinishRows = 8;    // query blocks compacted per finishing CTA
+// Per-row workspace words: the three histograms, then completion counters and the radix state after each pass.
+// The last CTA of a pass (threadfence-and-count, no waiting) turns that pass's histogram into the next state.
+constexpr int kOffCounter = kBins1 + kBins2 + kBins3;  // 3 counters (pass 1 counts per head, in the head's first row)
+constexpr int kOffState = kOffCounter + 4;             // state after pass p at kOffState + 3·(p−1): prefix, mask, rank
+constexpr int kHistPerRow = kOffState + 12;
+constexpr int kHistPer = 16;                  // entries per thread per histogram CTA
+constexpr int kHistChunk = 256 * kHistPer;    // entries of one selection row per histogram CTA
+constexpr int kFinishRows = 8;                // query blocks compacted per finishing CTA
 
 // Warp-aggregated shared-memory histogram increment (bins repeat heavily: probabilities share exponents).
 __device__ __forceinline__ void hist_add(uint32_t* h, uint32_t key, bool valid) {
@@ -81,8 +92,12 @@ __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uin
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int per = nbins / 256;
     const int top = nbins - 1 - per * tid;  // this thread covers bins top, top−1, …, top−per+1
+    uint32_t c[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = i < per ? __ldcg(hist + top - i) : 0u;
     uint32_t local = 0;
-    for (int i = 0; i < per; ++i) local += hist[top - i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) local += c[i];
     uint32_t incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -101,13 +116,12 @@ __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uin
     if (rank >= excl && rank < excl + local) {
         uint32_t cum = excl;
         for (int i = 0; i < per; ++i) {
-            const uint32_t c = hist[top - i];
-            if (rank < cum + c) {
+            if (rank < cum + c[i]) {
                 s_bin = (uint32_t)(top - i);
                 s_rank = rank - cum;
                 break;
             }
-            cum += c;
+            cum += c[i];
         }
     }
     __syncthreads();
@@ -116,134 +130,204 @@ __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uin
     __syncthreads();
 }
 
-// Row state after `passes` completed passes: the fixed high bits (prefix under pmask) and the remaining rank.
-__device__ void row_state(const uint32_t* __restrict__ hrow, int passes, uint32_t rank0, uint32_t* prefix,
-                          uint32_t* pmask, uint32_t* rank) {
-    uint32_t b, r = rank0, pre = 0, msk = 0;
-    if (passes >= 1) {
-        block_find_bin(hrow, kBins1, r, &b, &r);
-        pre = b << 21;
-        msk = 0xFFE00000u;
+// Called by the last CTA of pass `pass` for row `hrow`: folds that pass's histogram into the radix state.
+__device__ void advance_state(uint32_t* __restrict__ hrow, int pass, uint32_t rank0) {
+    uint32_t prefix = 0, pmask = 0, rank = rank0;
+    if (pass > 1) {
+        const uint32_t* st = hrow + kOffState + 3 * (pass - 2);
+        prefix = __ldcg(st);
+        pmask = __ldcg(st + 1);
+        rank = __ldcg(st + 2);
     }
-    if (passes >= 2) {
-        block_find_bin(hrow + kBins1, kBins2, r, &b, &r);
-        pre |= b << 10;
-        msk |= 0x001FFC00u;
+    const int off = pass == 1 ? 0 : (pass == 2 ? kBins1 : kBins1 + kBins2);
+    const int nb = pass == 3 ? kBins3 : kBins1;
+    uint32_t b;
+    block_find_bin(hrow + off, nb, rank, &b, &rank);
+    if (pass == 1) {
+        prefix = b << 21;
+        pmask = 0xFFE00000u;
+    } else if (pass == 2) {
+        prefix |= b << 10;
+        pmask |= 0x001FFC00u;
+    } else {
+        prefix |= b;
+        pmask = 0xFFFFFFFFu;
     }
-    if (passes >= 3) {
-        block_find_bin(hrow + kBins1 + kBins2, kBins3, r, &b, &r);
-        pre |= b;
-        msk = 0xFFFFFFFFu;
+    if (threadIdx.x == 0) {
+        uint32_t* st = hrow + kOffState + 3 * (pass - 1);
+        st[0] = prefix;
+        st[1] = pmask;
+        st[2] = rank;
     }
-    *prefix = pre;
-    *pmask = msk;
-    *rank = r;
 }
 
+// True in every thread of the CTA that completes `counter` (threadfence reduction: each CTA publishes its histogram
+// atomics, fences, then counts itself; the CTA that sees total − 1 runs after all others' atomics are visible).
+__device__ bool last_cta(uint32_t* counter, uint32_t total) {
+    __shared__ uint32_t s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == total - 1 ? 1u : 0u;
+    __syncthreads();
+    const bool last = s_last != 0;
+    if (last) __threadfence();
+    return last;
+}
+
+__device__ __forceinline__ uint32_t row_rank0(int64_t n, int topk) {
+    return (uint32_t)((int64_t)topk < n - 1 ? (int64_t)topk : n - 1);
+}
+
+// Score tile: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 4 micro-tile of rows
+// 4·ty + a and keys tx + 16·u, each score a sequential fmaf chain over e = 0..127.
 __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restrict__ pq, const float* __restrict__ pk,
                                                             KvPages pages, int heads, int nq, int nk, int bh, int bw,
-                                                            int local_range, int q_slices, float sqrt_d,
-                                                            float* __restrict__ probs, uint32_t* __restrict__ hist) {
-    extern __shared__ float4 sm4[];
-    uint32_t* shist = reinterpret_cast<uint32_t*>(sm4);  // [2][kBins1] pass-1 histograms of the CTA's first 2 slices
-    float* sq = reinterpret_cast<float*>(shist + 2 * kBins1);  // [kQR][128]
-    float* sk = sq + kQR * kD;                                  // [kKT][kKS]
-    float* ss = sk + kKT * kKS;                                 // [kQR][nk]
-    const int h = blockIdx.y;
-    const int i0 = blockIdx.x * kQR;
+                                                            int local_range, float sqrt_d, float* __restrict__ scores) {
+    extern __shared__ float4 score_smem[];
+    float* sq = reinterpret_cast<float*>(score_smem);  // [kTI][kPS]
+    float* sk = sq + kTI * kPS;                         // [kTJ][kPS]
+    const int h = blockIdx.z;
+    const int i0 = blockIdx.y * kTI, j0 = blockIdx.x * kTJ;
     const int64_t ld = (int64_t)heads * kD;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int s = bh * bw, half = local_range / 2;
-    const int nqs = nq / q_slices;
-    const int slice0 = i0 / nqs;
-
-    for (int i = tid; i < 2 * kBins1; i += 256) shist[i] = 0;
-    for (int idx = tid; idx < kQR * 32; idx += 256) {
+    const int tid = threadIdx.x;
+    for (int idx = tid; idx < kTI * 32; idx += 256) {
         const int r = idx >> 5, e4 = idx & 31;
         const int i = i0 + r;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < nq) v = __ldg(reinterpret_cast<const float4*>(pq + i * ld + h * kD) + e4);
-        reinterpret_cast<float4*>(sq)[idx] = v;
+        *reinterpret_cast<float4*>(sq + r * kPS + e4 * 4) = v;
     }
-    const int r0 = warp;  // one query block per warp
-    const int i_0 = i0 + r0;
-    const int qi = i_0 % s, qr_ = qi / bw, qc_ = qi % bw;
-
-    for (int jt = 0; jt < nk; jt += kKT) {
-        __syncthreads();
-        for (int idx = tid; idx < kKT * 32; idx += 256) {
-            const int kr = idx >> 5, e4 = idx & 31;
-            const int j = jt + kr;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (j < nk) v = __ldg(reinterpret_cast<const float4*>(pk + (int64_t)kv_phys_block(pages, j) * ld + h * kD) + e4);
-            *reinterpret_cast<float4*>(sk + kr * kKS + e4 * 4) = v;
-        }
-        __syncthreads();
-        if (i_0 >= nq) continue;
-        const float4* q0 = reinterpret_cast<const float4*>(sq + r0 * kD);
-        const float4* k0 = reinterpret_cast<const float4*>(sk + lane * kKS);
-        const float4* k1 = reinterpret_cast<const float4*>(sk + (lane + 32) * kKS);
-        float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll 8
-        for (int e4 = 0; e4 < 32; ++e4) {
-            const float4 x = q0[e4], y0 = k0[e4], y1 = k1[e4];
-            a0 = __fmaf_rn(x.x, y0.x, a0);
-            a0 = __fmaf_rn(x.y, y0.y, a0);
-            a0 = __fmaf_rn(x.z, y0.z, a0);
-            a0 = __fmaf_rn(x.w, y0.w, a0);
-            a1 = __fmaf_rn(x.x, y1.x, a1);
-            a1 = __fmaf_rn(x.y, y1.y, a1);
-            a1 = __fmaf_rn(x.z, y1.z, a1);
-            a1 = __fmaf_rn(x.w, y1.w, a1);
-        }
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            const int j = jt + lane + 32 * cc;
-            if (j >= nk) continue;
-            const int kj = j % s, kr_ = kj / bw, kc_ = kj % bw;
-            const bool allowed = kr_ >= qr_ - half && kr_ <= qr_ - half + local_range - 1 && kc_ >= qc_ - half &&
-                                 kc_ <= qc_ - half + local_range - 1;
-            ss[r0 * nk + j] = allowed ? __fdiv_rn(cc ? a1 : a0, sqrt_d) : -INFINITY;
-        }
+    for (int idx = tid; idx < kTJ * 32; idx += 256) {
+        const int r = idx >> 5, e4 = idx & 31;
+        const int j = j0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < nk) v = __ldg(reinterpret_cast<const float4*>(pk + (int64_t)kv_phys_block(pages, j) * ld + h * kD) + e4);
+        *reinterpret_cast<float4*>(sk + r * kPS + e4 * 4) = v;
     }
     __syncthreads();
-    if (i_0 < nq) {  // warp-uniform
-        float* row = ss + r0 * nk;
+    const int ty = tid >> 4, tx = tid & 15;
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[a][u] = 0.0f;
+#pragma unroll 2
+    for (int e4 = 0; e4 < 32; ++e4) {
+        float4 x[4], y[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) x[a] = reinterpret_cast<const float4*>(sq + (4 * ty + a) * kPS)[e4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) y[u] = reinterpret_cast<const float4*>(sk + (tx + 16 * u) * kPS)[e4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                acc[a][u] = __fmaf_rn(x[a].x, y[u].x, acc[a][u]);
+                acc[a][u] = __fmaf_rn(x[a].y, y[u].y, acc[a][u]);
+                acc[a][u] = __fmaf_rn(x[a].z, y[u].z, acc[a][u]);
+                acc[a][u] = __fmaf_rn(x[a].w, y[u].w, acc[a][u]);
+            }
+    }
+    const int s = bh * bw, half = local_range / 2;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int i = i0 + 4 * ty + a;
+        if (i >= nq) continue;
+        const int qi = i % s, qr = qi / bw, qc = qi % bw;
+        float* out = scores + ((int64_t)h * nq + i) * nk;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = j0 + tx + 16 * u;
+            if (j >= nk) continue;
+            const int kj = j % s, kr = kj / bw, kc = kj % bw;
+            const bool allowed = kr >= qr - half && kr <= qr - half + local_range - 1 && kc >= qc - half &&
+                                 kc <= qc - half + local_range - 1;
+            out[j] = allowed ? __fdiv_rn(acc[a][u], sqrt_d) : -INFINITY;
+        }
+    }
+}
+
+// Softmax over the key blocks of one (head, query block) row per warp, in place (scores → probs), plus the pass-1
+// histogram of each (head, query slice) row. A CTA's rows lie in at most two slices whenever Nq/q_slices ≥ 8; rows
+// of any further slice go straight to global atomics.
+__global__ void __launch_bounds__(256) select_softmax_kernel(float* __restrict__ probs, int nq, int nk, int q_slices,
+                                                             int topk, uint32_t* __restrict__ hist) {
+    __shared__ uint32_t shist[2][kBins1];
+    const int h = blockIdx.y;
+    const int i0 = blockIdx.x * kSoftRows;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nqs = nq / q_slices;
+    const int slice0 = i0 / nqs;
+    for (int i = tid; i < 2 * kBins1; i += 256) (&shist[0][0])[i] = 0;
+    __syncthreads();
+    const int i = i0 + warp;
+    if (i < nq) {  // warp-uniform
+        float* row = probs + ((int64_t)h * nq + i) * nk;
         float m = -INFINITY;
-        for (int j = lane; j < nk; j += 32) m = fmaxf(m, row[j]);
+        for (int jb = 0; jb < nk; jb += 256) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                v[u] = j < nk ? row[j] : -INFINITY;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) m = fmaxf(m, v[u]);
+        }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float part = 0.0f;
-        for (int j = lane; j < nk; j += 32) {
-            const float e = fvsr_exp(__fsub_rn(row[j], m));
-            row[j] = e;
-            part = __fadd_rn(part, e);
+        for (int jb = 0; jb < nk; jb += 256) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                v[u] = j < nk ? row[j] : -INFINITY;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                const float e = fvsr_exp(__fsub_rn(v[u], m));
+                if (j < nk) {
+                    row[j] = e;
+                    part = __fadd_rn(part, e);
+                }
+            }
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
-        float* out = probs + ((int64_t)h * nq + i_0) * nk;
-        const int sl = i_0 / nqs, local = sl - slice0;
+        const int sl = i / nqs, local = sl - slice0;
         uint32_t* gh = hist + (int64_t)(h * q_slices + sl) * kHistPerRow;
-        for (int j0 = 0; j0 < nk; j0 += 32) {
-            const int j = j0 + lane;
-            float p = 0.0f;
-            if (j < nk) {
-                p = __fdiv_rn(row[j], part);
-                out[j] = p;
+        for (int jb = 0; jb < nk; jb += 256) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                v[u] = j < nk ? row[j] : 0.0f;
             }
-            const uint32_t bin = __float_as_uint(p) >> 21;
-            if (local < 2)
-                hist_add(shist + local * kBins1, bin, j < nk);
-            else if (j < nk)
-                atomicAdd(gh + bin, 1u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                const float p = v[u] == 0.0f ? 0.0f : __fdiv_rn(v[u], part);  // 0 / sum = +0 exactly
+                if (j < nk) row[j] = p;
+                const uint32_t bin = __float_as_uint(p) >> 21;
+                if (local < 2)
+                    hist_add(&shist[local][0], bin, j < nk);
+                else if (j < nk)
+                    atomicAdd(gh + bin, 1u);
+            }
         }
     }
     __syncthreads();
-    for (int i = tid; i < 2 * kBins1; i += 256) {
-        const uint32_t c = shist[i];
-        const int sl = slice0 + i / kBins1;
-        if (c && sl < q_slices) atomicAdd(hist + (int64_t)(h * q_slices + sl) * kHistPerRow + (i % kBins1), c);
+    for (int x = tid; x < 2 * kBins1; x += 256) {
+        const uint32_t c = (&shist[0][0])[x];
+        const int sl = slice0 + x / kBins1;
+        if (c && sl < q_slices) atomicAdd(hist + (int64_t)(h * q_slices + sl) * kHistPerRow + (x % kBins1), c);
     }
+    uint32_t* head0 = hist + (int64_t)(h * q_slices) * kHistPerRow;
+    if (last_cta(head0 + kOffCounter, gridDim.x))
+        for (int t = 0; t < q_slices; ++t)
+            advance_state(hist + (int64_t)(h * q_slices + t) * kHistPerRow, 1, row_rank0((int64_t)nqs * nk, topk));
 }
 
 // Passes 2 and 3 of the radix select: one CTA per kHistChunk entries of one (head, query slice) row.
@@ -254,24 +338,25 @@ __global__ void __launch_bounds__(256) select_hist_kernel(const float* __restric
     const int h = row / q_slices, t = row % q_slices;
     const int nqs = nq / q_slices;
     const int64_t n = (int64_t)nqs * nk;
-    const uint32_t rank0 = (uint32_t)((int64_t)topk < n - 1 ? (int64_t)topk : n - 1);
     uint32_t* hrow = hist + (int64_t)row * kHistPerRow;
     const int tid = threadIdx.x;
-    for (int i = tid; i < kBins2; i += 256) sh[i] = 0;
-    uint32_t prefix, pmask, rank;
-    row_state(hrow, pass - 1, rank0, &prefix, &pmask, &rank);  // also synchronises the block
     const float* base = probs + ((int64_t)h * nq + (int64_t)t * nqs) * nk;
     const int64_t e0 = (int64_t)blockIdx.x * kHistChunk;
-    const int64_t e1 = e0 + kHistChunk < n ? e0 + kHistChunk : n;
-    for (int64_t b = e0 + (tid & ~31); b < e1; b += 256) {
-        const int64_t idx = b + (tid & 31);
-        uint32_t u = 0;
-        bool valid = idx < e1;
-        if (valid) {
-            u = __float_as_uint(base[idx]);
-            valid = (u & pmask) == prefix;
-        }
-        const uint32_t bin = pass == 2 ? (u >> 10) & (kBins2 - 1) : u & (kBins3 - 1);
+    uint32_t u[kHistPer];
+#pragma unroll
+    for (int k = 0; k < kHistPer; ++k) {
+        const int64_t idx = e0 + tid + 256 * k;
+        u[k] = idx < n ? __float_as_uint(base[idx]) : 0xFFFFFFFFu;
+    }
+    for (int i = tid; i < kBins2; i += 256) sh[i] = 0;
+    const uint32_t* st = hrow + kOffState + 3 * (pass - 2);
+    const uint32_t prefix = __ldcg(st), pmask = __ldcg(st + 1);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kHistPer; ++k) {
+        const int64_t idx = e0 + tid + 256 * k;
+        const bool valid = idx < n && (u[k] & pmask) == prefix;
+        const uint32_t bin = pass == 2 ? (u[k] >> 10) & (kBins2 - 1) : u[k] & (kBins3 - 1);
         hist_add(sh, bin, valid);
     }
     __syncthreads();
@@ -279,6 +364,7 @@ __global__ void __launch_bounds__(256) select_hist_kernel(const float* __restric
     const int nb = pass == 2 ? kBins2 : kBins3;
     for (int i = tid; i < nb; i += 256)
         if (sh[i]) atomicAdd(gh + i, sh[i]);
+    if (last_cta(hrow + kOffCounter + pass - 1, gridDim.x)) advance_state(hrow, pass, row_rank0(n, topk));
 }
 
 // Threshold = the exact (min(n−1, topk)+1)-th largest of the row; compaction of p > threshold into ascending kidx
@@ -290,11 +376,7 @@ __global__ void __launch_bounds__(256) select_finish_kernel(const float* __restr
     const int row = blockIdx.y;
     const int h = row / q_slices, t = row % q_slices;
     const int nqs = nq / q_slices;
-    const int64_t n = (int64_t)nqs * nk;
-    const uint32_t rank0 = (uint32_t)((int64_t)topk < n - 1 ? (int64_t)topk : n - 1);
-    uint32_t prefix, pmask, rank;
-    row_state(hist + (int64_t)row * kHistPerRow, 3, rank0, &prefix, &pmask, &rank);
-    const float thr = __uint_as_float(prefix);
+    const float thr = __uint_as_float(__ldcg(hist + (int64_t)row * kHistPerRow + kOffState + 6));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ii = blockIdx.x * kFinishRows + warp;
     if (ii >= nqs) return;
@@ -302,13 +384,22 @@ __global__ void __launch_bounds__(256) select_finish_kernel(const float* __restr
     const float* p = probs + qrow * nk;
     int32_t* lst = kidx + qrow * nk;
     int cnt = 0;
-    for (int j0 = 0; j0 < nk; j0 += 32) {
-        const int j = j0 + lane;
-        const bool keep = j < nk && p[j] > thr;
-        const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-        if (keep) lst[cnt + __popc(bal & ((1u << lane) - 1u))] = j;
-        if (mask && j < nk) mask[qrow * nk + j] = keep ? 1 : 0;
-        cnt += __popc(bal);
+    for (int jb = 0; jb < nk; jb += 256) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = jb + 32 * u + lane;
+            v[u] = j < nk ? p[j] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = jb + 32 * u + lane;
+            const bool keep = j < nk && v[u] > thr;
+            const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+            if (keep) lst[cnt + __popc(bal & ((1u << lane) - 1u))] = j;
+            if (mask && j < nk) mask[qrow * nk + j] = keep ? 1 : 0;
+            cnt += __popc(bal);
+        }
     }
     for (int j = cnt + lane; j < nk; j += 32) lst[j] = -1;
     if (lane == 0) kcnt[qrow] = cnt;
@@ -334,24 +425,25 @@ __global__ void __launch_bounds__(256) mask_to_lists_kernel(const float* __restr
 
 }  // namespace
 
-size_t select_scores_smem_bytes(int nk) {
-    return sizeof(uint32_t) * 2 * kBins1 + sizeof(float) * ((size_t)kQR * kD + (size_t)kKT * kKS + (size_t)kQR * nk);
-}
+size_t select_scores_smem_bytes(int) { return sizeof(float) * (size_t)(kTI + kTJ) * kPS; }
 
 size_t select_hist_bytes(int heads, int q_slices) { return sizeof(uint32_t) * (size_t)heads * q_slices * kHistPerRow; }
 
 cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
-                                 int bh, int bw, int local_range, int q_slices, float* probs, uint32_t* hist,
+                                 int bh, int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist,
                                  cudaStream_t st) {
-    const size_t smem = select_scores_smem_bytes(nk);
-    cudaError_t e = cudaFuncSetAttribute(select_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaMemsetAsync(hist, 0, select_hist_bytes(heads, q_slices), st);
     if (e != cudaSuccess) return e;
-    e = cudaMemsetAsync(hist, 0, select_hist_bytes(heads, q_slices), st);
+    const int smem = (int)select_scores_smem_bytes(nk);
+    e = cudaFuncSetAttribute(select_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const float sqrt_d = sqrtf((float)kD);
-    dim3 grid((nq + kQR - 1) / kQR, heads);
-    select_scores_kernel<<<grid, 256, smem, st>>>(pq, pk, pk_pages, heads, nq, nk, bh, bw, local_range, q_slices, sqrt_d,
-                                                  probs, hist);
+    dim3 grid((nk + kTJ - 1) / kTJ, (nq + kTI - 1) / kTI, heads);
+    select_scores_kernel<<<grid, 256, smem, st>>>(pq, pk, pk_pages, heads, nq, nk, bh, bw, local_range, sqrt_d, probs);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 sgrid((nq + kSoftRows - 1) / kSoftRows, heads);
+    select_softmax_kernel<<<sgrid, 256, 0, st>>>(probs, nq, nk, q_slices, topk, hist);
     return cudaGetLastError();
 }
 

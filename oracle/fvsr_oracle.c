@@ -48,8 +48,8 @@ static inline float orc_pow2i(int n) {          /* 2^n for n in [-126, 127], bui
 
 /* e^x in fp32. Range reduction: n = rint(x·log2 e), r = x − n·ln2 with ln 2 split into a 24-bit-exact high part
  * (0x3f317200) and a low correction, both applied by fmaf. e^r by the Taylor series Σ r^k/k!, k ≤ 7 (|r| ≤ 0.347,
- * truncation < 6e-9 relative). Scaling by 2^n is one IEEE multiply for n ≥ −126 and two (the first exact) below it,
- * so subnormal results round exactly once. */
+ * truncation < 6e-9 relative). Scaling by 2^n is one IEEE multiply for −126 ≤ n ≤ 127 and two (the first exact)
+ * outside that range, so subnormal results round exactly once and e^x just below the overflow bound stays finite. */
 float fvsr_exp(float x) {
     if (x != x) return x;
     if (x < -104.0f) return 0.0f;                 /* below half the smallest subnormal */
@@ -69,10 +69,8 @@ float fvsr_exp(float x) {
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
     int ni = (int)n;
-    if (ni >= -126) {
-        if (ni > 127) return INFINITY;
-        return p * orc_pow2i(ni);
-    }
+    if (ni > 127) return (p * orc_pow2i(ni - 1)) * 2.0f;
+    if (ni >= -126) return p * orc_pow2i(ni);
     return (p * orc_pow2i(ni + 64)) * orc_pow2i(-64);
 }
 
