@@ -89,6 +89,22 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
                              int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs, void* workspace,
                              size_t workspace_bytes, fvsr_stream_t stream);
 
+/* Size of the fixed scratch array behind fvsr_lcsa_select_noalloc (device memory held by every GPU that loads the
+ * library, for the life of the process). */
+#define FVSR_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/* fvsr_lcsa_select without a workspace: for callers that cannot allocate device memory — an engine that owns every
+ * buffer under a fixed budget, or a real-time thread that must not take an allocation's device-wide synchronisation.
+ * Same arguments and results as fvsr_lcsa_select, except that probs is required (an output, as in the reference) and
+ * the scratch (pooled queries/keys, selection histograms) comes from one fixed FVSR_NOALLOC_SCRATCH_BYTES array
+ * inside the library. Calls needing more scratch than that fail with FVSR_EUNSUPPORTED; nothing is allocated.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress) with that device current, so make
+ * that first call before any stream capture. All calls on a device share the array and it keeps the last call's
+ * contents (what must start at zero is cleared by each call); calls that overlap on the GPU race, so order them on
+ * one stream. No counterpart in the reference: it is an addition for hosts without an allocator. */
+fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const void* q, const void* k, const float* pooled_k,
+                                     int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs, fvsr_stream_t stream);
+
 /* Block-sparse attention over the kept pairs — replaces kernelBlockAttention (SparseAttention.swift:169-187) fed with
  * index lists. q (Nq·128, H·128), k / v (Nk·128, H·128), out (Nq·128, H·128), all p->dtype; kidx / kcnt as produced by
  * fvsr_lcsa_select. Scale 1/sqrt(128). A query block with kcnt = 0 writes zeros (SparseAttention.swift:47-53).

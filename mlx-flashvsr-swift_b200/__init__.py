@@ -29,6 +29,7 @@ EXPORTED = [
     "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
+    "fvsr_lcsa_select_noalloc",
 ]
 
 
@@ -85,6 +86,7 @@ def lib() -> ctypes.CDLL:
         "fvsr_kv_cache_gather": ([P, P, P, P], ctypes.c_int),
         "fvsr_kv_cache_state": ([P, P, ctypes.POINTER(I32)], ctypes.c_int),
         "fvsr_lcsa_forward": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_select_noalloc": ([PP, P, P, P, P, P, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)

@@ -11,11 +11,21 @@
 #include "../../include/fvsr_lcsa.h"
 #include "common.cuh"
 
+namespace fvsr {
+void set_last_error(const char* msg);
+}
+
 using namespace fvsr;
 
 namespace {
 
 thread_local std::string g_last_error;
+
+}  // namespace
+
+void fvsr::set_last_error(const char* msg) { g_last_error = msg; }
+
+namespace {
 
 fvsr_status fail(fvsr_status s, const char* fmt, ...) {
     char buf[512];
