@@ -6,7 +6,8 @@
 // One CTA per (head, query block) work item, ordered head-major so the CTAs in flight share one head's K/V in L2.
 // Warp roles (320 threads):
 //   warp 0      TMA producer: the Q tile, then the K and V tiles of each kept key block into a 3-slot K ring (a slot
-//               frees when its S MMA completes) and a 2-slot V ring (freed when its PV MMA completes).
+//               frees when its S MMA completes) and a 2-slot V ring (freed when its PV MMA completes); the releases
+//               reuse the S-full and PV-done barriers, so each key block costs two tcgen05.commit.
 //   warp 1      TMEM owner + single-thread MMA issuer: S_j = Q·K_jᵀ (SS-MMA, 128×128×128) is issued two blocks
 //               ahead of O += P_j·V_j (TS-MMA: P read from TMEM, V from shared memory as an MN-major operand), so two
 //               S tiles are queued on the tensor core while the softmax of block j is in flight.
@@ -56,9 +57,13 @@ constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kTileBytes;                          // K slot i at kOffK + i·kTileBytes
 constexpr uint32_t kOffV = kOffK + kKSlots * kTileBytes;        // V slot i at kOffV + i·kTileBytes
 constexpr uint32_t kOffBar = kOffV + kVSlots * kTileBytes;      // barriers
-constexpr int kBarQ = 0, kBarKF = 1, kBarKE = kBarKF + kKSlots, kBarVF = kBarKE + kKSlots, kBarVE = kBarVF + kVSlots,
-              kBarSF = kBarVE + kVSlots, kBarPF = kBarSF + kSBufs, kBarPV = kBarPF + kSBufs, kBarM = kBarPV + 2,
-              kBarFin = kBarM + 2, kNumBars = kBarFin + 1;
+// A K slot frees when its S MMA completes and a V slot when its PV MMA completes, which the S-full and PV-done
+// barriers already signal, so the producer waits on those (K slot j%3 ↔ S buffer j%3, V slot j%2 ↔ PV barrier j%2):
+// two tcgen05.commit per key block instead of four. Neither barrier can run a phase ahead of the producer's wait,
+// because the next completion on it needs the tile the producer has not loaded yet.
+static_assert(kKSlots == kSBufs && kVSlots == 2, "ring slots are released through the S and PV barriers");
+constexpr int kBarQ = 0, kBarKF = 1, kBarVF = kBarKF + kKSlots, kBarSF = kBarVF + kVSlots, kBarPF = kBarSF + kSBufs,
+              kBarPV = kBarPF + kSBufs, kBarM = kBarPV + 2, kBarFin = kBarM + 2, kNumBars = kBarFin + 1;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffM = (kOffAbort + 4 + 15) & ~15u;         // running max handoff: [2 parities][128] f32
@@ -103,14 +108,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(bar(kBarQ), 1);
-        for (int i = 0; i < kKSlots; ++i) {
-            mbar_init(bar(kBarKF + i), 1);
-            mbar_init(bar(kBarKE + i), 1);
-        }
-        for (int i = 0; i < kVSlots; ++i) {
-            mbar_init(bar(kBarVF + i), 1);
-            mbar_init(bar(kBarVE + i), 1);
-        }
+        for (int i = 0; i < kKSlots; ++i) mbar_init(bar(kBarKF + i), 1);
+        for (int i = 0; i < kVSlots; ++i) mbar_init(bar(kBarVF + i), 1);
         for (int b = 0; b < kSBufs; ++b) {
             mbar_init(bar(kBarSF + b), 1);
             mbar_init(bar(kBarPF + b), 128);
@@ -152,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, x0 + 64, qb * kBlock, bar(kBarQ));
             auto load_k = [&](int j) -> bool {
                 const int ks = j % kKSlots;
-                if (j >= kKSlots && !wait(kBarKE + ks, (uint32_t)(j / kKSlots - 1))) return false;
+                if (j >= kKSlots && !wait(kBarSF + ks, (uint32_t)(j / kKSlots - 1))) return false;  // S_{j−3} done
                 const uint32_t dk = sbase + kOffK + (uint32_t)ks * kTileBytes;
                 mbar_expect_tx(bar(kBarKF + ks), kTileBytes);
                 tma_load_2d(dk, &tmK, x0, s_list[j] * kBlock, bar(kBarKF + ks));
@@ -161,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             };
             auto load_v = [&](int j) -> bool {
                 const int vs = j % kVSlots;
-                if (j >= kVSlots && !wait(kBarVE + vs, (uint32_t)(j / kVSlots - 1))) return false;
+                if (j >= kVSlots && !wait(kBarPV + vs, (uint32_t)(j / kVSlots - 1))) return false;  // PV_{j−2} done
                 const uint32_t dv = sbase + kOffV + (uint32_t)vs * kTileBytes;
                 mbar_expect_tx(bar(kBarVF + vs), kTileBytes);
                 tma_load_2d(dv, &tmV, x0, s_list[j] * kBlock, bar(kBarVF + vs));
@@ -186,7 +185,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t off = (uint32_t)(kk >> 2) * kBoxBytes + (uint32_t)(kk & 3) * 32u;
                     mma_ss(d, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(bar(kBarKE + ks));
                 mma_commit(bar(kBarSF + j % kSBufs));
                 return true;
             };
@@ -205,7 +203,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < 8; ++kk)
                     mma_ts(tmem + kColO, pa + 8u * (uint32_t)kk, smem_desc(va + (uint32_t)kk * 2048u, kBoxBytes, 1024),
                            kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(bar(kBarVE + vs));
                 mma_commit(bar(kBarPV + (j & 1)));
             }
         }
