@@ -45,6 +45,7 @@ constexpr uint32_t kColO = 0, kColS0 = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr int kThreads = 320;  // 2 role warps + 2 softmax sets of 4 warps
+
 // Lazy rescaling: a row's running maximum (log2 units) is only raised — and O rescaled — when the block maximum
 // exceeds it by more than this; otherwise P entries may reach 2^8, which bf16 P and fp32 O/l carry exactly as well.
 constexpr float kRescaleThreshold = 8.0f;
@@ -179,11 +180,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait(kBarKF + ks, (uint32_t)(j / kKSlots))) return false;
                 tc_fence_after();
                 const uint32_t d = tmem + kColS0 + 128u * (uint32_t)(j % kSBufs);
-                const uint32_t qa = sbase + kOffQ, ka = sbase + kOffK + (uint32_t)ks * kTileBytes;
+                // descriptors advance by byte offset >> 4 in their start-address field (no carry: smem < 256 KB)
+                const uint64_t qd = smem_desc(sbase + kOffQ, 16, 1024);
+                const uint64_t kd = smem_desc(sbase + kOffK + (uint32_t)ks * kTileBytes, 16, 1024);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (uint32_t)(kk >> 2) * kBoxBytes + (uint32_t)(kk & 3) * 32u;
-                    mma_ss(d, smem_desc(qa + off, 16, 1024), smem_desc(ka + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+                    const uint32_t off = ((uint32_t)(kk >> 2) * kBoxBytes + (uint32_t)(kk & 3) * 32u) >> 4;
+                    mma_ss(d, qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(bar(kBarSF + j % kSBufs));
                 return true;
@@ -197,12 +200,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait(kBarVF + vs, (uint32_t)(j / kVSlots))) break;
                 if (!wait(kBarPF + j % kSBufs, (uint32_t)(j / kSBufs))) break;
                 tc_fence_after();
-                const uint32_t va = sbase + kOffV + (uint32_t)vs * kTileBytes;
+                const uint64_t vd = smem_desc(sbase + kOffV + (uint32_t)vs * kTileBytes, kBoxBytes, 1024);
                 const uint32_t pa = tmem + kColS0 + 128u * (uint32_t)(j % kSBufs);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_ts(tmem + kColO, pa + 8u * (uint32_t)kk, smem_desc(va + (uint32_t)kk * 2048u, kBoxBytes, 1024),
-                           kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_ts(tmem + kColO, pa + 8u * (uint32_t)kk, vd + (uint64_t)(kk * (2048 >> 4)), kIdescPV,
+                           (j > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(bar(kBarPV + (j & 1)));
             }
         }
