@@ -220,6 +220,16 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    run_step = step
+    if not args.no_graph:
+        # the 30 layer calls of a step (7 kernels + 1 memset each) replayed as one CUDA graph: the C ABI calls make no
+        # host synchronisation and no allocation, so they capture as they are
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        torch.cuda.synchronize()
+        run_step = graph.replay
     if world > 1:
         dist.barrier()
     uuid = None
@@ -233,7 +243,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        run_step()
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -324,6 +334,7 @@ def run_ours(args):
             "config": {"workload": f"config {args.config}: {cfg.name}", "layers_per_step": layers,
                        "heads": g.heads, "q_blocks": g.nq, "k_blocks": g.nk, "topk": g.topk,
                        "kept_triples_per_layer": sum(kept) / layers, "l2": "inputs > L2 (371 MB per layer), no flush",
+                       "launch": "eager" if args.no_graph else "CUDA graph of one step",
                        "parallelism": f"{world} independent streams" if world > 1 else "1 GPU"},
             "ms_per_layer": ms / layers,
             "breakdown_ms_per_layer": {"attention": att_avg, "pool+select": sel_ms},
@@ -357,6 +368,7 @@ def main():
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one instead of a CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

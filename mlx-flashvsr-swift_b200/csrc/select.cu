@@ -28,7 +28,7 @@ namespace {
 constexpr int kTI = 64;   // query blocks per score tile
 constexpr int kTJ = 64;   // key blocks per score tile
 constexpr int kPS = 132;  // padded fp32 row stride of the staged pooled rows
-constexpr int kSoftRows = 8;  // (head, query block) rows per softmax CTA, one per warp
+constexpr int kSoftRows = 4;  // (head, query block) rows per softmax CTA, one per warp
 
 __device__ __forceinline__ float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
 
@@ -84,20 +84,22 @@ __device__ __forceinline__ void hist_add(uint32_t* h, uint32_t key, bool valid) 
 }
 
 // Finds, among `nbins` histogram bins scanned from the highest, the bin holding the entry of descending rank `rank`
-// (0 = largest). All 256 threads of the block call it; the result is returned to every thread.
+// (0 = largest). All threads of the block call it (128 to 1024 threads, nbins / blockDim ≤ 16); the result is
+// returned to every thread.
 __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uint32_t rank, uint32_t* out_bin,
                                uint32_t* out_rank) {
-    __shared__ uint32_t warp_sums[8];
+    __shared__ uint32_t warp_sums[32];
     __shared__ uint32_t s_bin, s_rank;
+    const int nt = blockDim.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = nbins / 256;
+    const int per = nbins / nt;
     const int top = nbins - 1 - per * tid;  // this thread covers bins top, top−1, …, top−per+1
-    uint32_t c[8];
+    uint32_t c[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) c[i] = i < per ? __ldcg(hist + top - i) : 0u;
+    for (int i = 0; i < 16; ++i) c[i] = i < per ? __ldcg(hist + top - i) : 0u;
     uint32_t local = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) local += c[i];
+    for (int i = 0; i < 16; ++i) local += c[i];
     uint32_t incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -228,20 +230,32 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
                 acc[a][u] = __fmaf_rn(x[a].w, y[u].w, acc[a][u]);
             }
     }
+    // locality window of each of the 4 rows and grid position of each of the 4 keys, computed once
     const int s = bh * bw, half = local_range / 2;
+    int lo_r[4], lo_c[4], kr[4], kc[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int qi = (i0 + 4 * ty + a) % s;
+        lo_r[a] = qi / bw - half;
+        lo_c[a] = qi % bw - half;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int kj = (j0 + tx + 16 * u) % s;
+        kr[u] = kj / bw;
+        kc[u] = kj % bw;
+    }
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
         const int i = i0 + 4 * ty + a;
         if (i >= nq) continue;
-        const int qi = i % s, qr = qi / bw, qc = qi % bw;
         float* out = scores + ((int64_t)h * nq + i) * nk;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int j = j0 + tx + 16 * u;
             if (j >= nk) continue;
-            const int kj = j % s, kr = kj / bw, kc = kj % bw;
-            const bool allowed = kr >= qr - half && kr <= qr - half + local_range - 1 && kc >= qc - half &&
-                                 kc <= qc - half + local_range - 1;
+            const bool allowed = kr[u] >= lo_r[a] && kr[u] <= lo_r[a] + local_range - 1 && kc[u] >= lo_c[a] &&
+                                 kc[u] <= lo_c[a] + local_range - 1;
             out[j] = allowed ? __fdiv_rn(acc[a][u], sqrt_d) : -INFINITY;
         }
     }
@@ -250,7 +264,8 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
 // Softmax over the key blocks of one (head, query block) row per warp, in place (scores → probs), plus the pass-1
 // histogram of each (head, query slice) row. A CTA's rows lie in at most two slices whenever Nq/q_slices ≥ 8; rows
 // of any further slice go straight to global atomics.
-__global__ void __launch_bounds__(256) select_softmax_kernel(float* __restrict__ probs, int nq, int nk, int q_slices,
+__global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* __restrict__ probs, int nq, int nk,
+                                                                       int q_slices,
                                                              int topk, uint32_t* __restrict__ hist) {
     __shared__ uint32_t shist[2][kBins1];
     const int h = blockIdx.y;
@@ -258,7 +273,7 @@ __global__ void __launch_bounds__(256) select_softmax_kernel(float* __restrict__
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nqs = nq / q_slices;
     const int slice0 = i0 / nqs;
-    for (int i = tid; i < 2 * kBins1; i += 256) (&shist[0][0])[i] = 0;
+    for (int i = tid; i < 2 * kBins1; i += kSoftRows * 32) (&shist[0][0])[i] = 0;
     __syncthreads();
     const int i = i0 + warp;
     if (i < nq) {  // warp-uniform
@@ -319,7 +334,7 @@ __global__ void __launch_bounds__(256) select_softmax_kernel(float* __restrict__
         }
     }
     __syncthreads();
-    for (int x = tid; x < 2 * kBins1; x += 256) {
+    for (int x = tid; x < 2 * kBins1; x += kSoftRows * 32) {
         const uint32_t c = (&shist[0][0])[x];
         const int sl = slice0 + x / kBins1;
         if (c && sl < q_slices) atomicAdd(hist + (int64_t)(h * q_slices + sl) * kHistPerRow + (x % kBins1), c);
@@ -443,7 +458,7 @@ cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 sgrid((nq + kSoftRows - 1) / kSoftRows, heads);
-    select_softmax_kernel<<<sgrid, 256, 0, st>>>(probs, nq, nk, q_slices, topk, hist);
+    select_softmax_kernel<<<sgrid, kSoftRows * 32, 0, st>>>(probs, nq, nk, q_slices, topk, hist);
     return cudaGetLastError();
 }
 
