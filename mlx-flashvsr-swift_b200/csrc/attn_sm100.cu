@@ -254,8 +254,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float m_j = need ? fmaxf(m_prev, mx) : m_prev;
             m_x[(j & 1) * 128 + r] = m_j;
             mbar_arrive(bar(kBarM + (j & 1)));  // published before the exponentials so block j+1 can start
+            const float neg = -m_j;
+            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {  // 32 key columns → 16 packed P columns per store
+                uint32_t pk[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(sv[32 * q4 + 2 * c]), sl2, neg));
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(sv[32 * q4 + 2 * c + 1]), sl2, neg));
+                    rs4[c & 3] += p0 + p1;
+                    pk[c] = pack_bf16x2(p0, p1);
+                }
+                tmem_st16(sbuf + 16u * (uint32_t)q4, pk);
+            }
+            if (m_j != mref) {  // bring this set's partial sum to the current maximum
+                l *= ex2_approx(mref - m_j);
+                mref = m_j;
+            }
+            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             if (j > 0 && __any_sync(0xffffffffu, need)) {
-                // O holds Σ_{i<j} P_i·V_i relative to m_prev once PV_{j−1} has completed; bring it to m_j
+                // after the P stores (S_j's registers are free by now): O holds Σ_{i<j} P_i·V_i relative to
+                // m_prev once PV_{j−1} has completed; bring it to m_j
                 if (!wait_warp(kBarPV + ((j - 1) & 1), (uint32_t)((j - 1) >> 1))) {
                     ok = false;
                     break;
@@ -272,25 +292,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(lane_base + kColO + 32u * c, ov);
                 }
             }
-            const float neg = -m_j;
-            float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {  // 64 key columns → 32 packed P columns per store
-                uint32_t pk[32];
-#pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const float p0 = ex2_approx(fmaf(__uint_as_float(sv[64 * h2 + 2 * c]), sl2, neg));
-                    const float p1 = ex2_approx(fmaf(__uint_as_float(sv[64 * h2 + 2 * c + 1]), sl2, neg));
-                    rs4[c & 3] += p0 + p1;
-                    pk[c] = pack_bf16x2(p0, p1);
-                }
-                tmem_st32(sbuf + 32u * (uint32_t)h2, pk);
-            }
-            if (m_j != mref) {  // bring this set's partial sum to the current maximum
-                l *= ex2_approx(mref - m_j);
-                mref = m_j;
-            }
-            l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(bar(kBarPF + j % kSBufs));
