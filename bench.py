@@ -5,7 +5,8 @@ head) triple, over the whole path's device time (pooling + selection + attention
 Workload at N=1: config 3 (1920×1152 chunk: 12 heads, 135 × 405 blocks, R = 11, keep 30 %), a step = one chunk =
 30 layer calls, each on fresh seeded Q/K/V resident in HBM (371 MB per layer, larger than L2, so no flush is needed).
 N > 1 (torchrun, one process per GPU): independent config-3 streams, one per GPU (config 5's throughput variant);
-no data-path collective, weak scaling, time = max over ranks.
+no data-path collective, weak scaling, time = max over ranks. --config 5 (or --shard) instead splits one config's
+(head, query block) items across the ranks: strong scaling, still no data-path collective (heads are independent).
 
 --impl reference: the CPU baseline arm — the reference's Swift/MLX path cannot run off Apple hardware, so this times
 the CPU oracle (a C/OpenMP restatement of the reference's selection and block-masked attention) on all host threads,
@@ -185,37 +186,71 @@ def run_ours(args):
     layers = args.layers
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream()
+    shard = args.shard if args.shard is not None else args.config == 5
+
+    if shard:
+        # the config's (head, query block) items split across ranks (strong scaling, no data-path collective: LCSA
+        # heads are independent, so each rank holds the Q/K/V of the heads its items touch, as a tensor-parallel
+        # QKV projection leaves them); inputs are seeded per head, so the ranks together solve the one-GPU problem
+        sh = pkg.shard_items(g.heads, g.nq, world, rank)
+        g_loc = pkg.Geometry(**{**g.__dict__, "heads": max(sh.heads, 1)})
+        item_begin, item_count = sh.local_range(g.nq) if sh.heads > 0 else (0, 0)
+
+        def make_inputs(l):
+            parts = [cfgs.synth_qkv(cfg, pkg.Geometry(**{**g.__dict__, "heads": 1}),
+                                    cfgs.seed_of(args.config, 0, l) * 64 + h, device=dev)
+                     for h in range(sh.head_lo, max(sh.head_hi, sh.head_lo) + 1)]
+            return tuple(torch.cat([pt[i] for pt in parts], dim=1).contiguous() for i in range(3))
+    else:
+        g_loc = g
+        item_begin, item_count = 0, g.heads * g.nq
+
+        def make_inputs(l):
+            return cfgs.synth_qkv(cfg, g, cfgs.seed_of(args.config, rank, l), device=dev)
 
     # inputs: one fresh seeded (q, k, v) per layer, resident in HBM
-    inputs = [cfgs.synth_qkv(cfg, g, cfgs.seed_of(args.config, rank, l), device=dev) for l in range(layers)]
-    ws = pkg.make_workspace(g, dev)
-    kidx = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device=dev)
-    kcnt = torch.empty((g.heads, g.nq), dtype=torch.int32, device=dev)
+    inputs = [make_inputs(l) for l in range(layers)]
+    ws = pkg.make_workspace(g_loc, dev)
+    kidx = torch.empty((g_loc.heads, g_loc.nq, g_loc.nk), dtype=torch.int32, device=dev)
+    kcnt = torch.empty((g_loc.heads, g_loc.nq), dtype=torch.int32, device=dev)
     outs = [torch.empty_like(inputs[0][0]) for _ in range(2)]
     kept = []
 
     import ctypes
     L = pkg.lib()
-    p = g.params()
+    p = g_loc.params()
+
+    def select_call(q, k):
+        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx), pkg._ptr(kcnt),
+                                      None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+
+    def attention_call(q, k, v, out):
+        pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
+                                               pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(out), item_begin, item_count,
+                                               pkg._stream()))
 
     def layer_call(l, out):
         """One layer through the C ABI: fvsr_lcsa_select (pool Q, pool K, scores + softmax, threshold + lists),
-        then fvsr_lcsa_attention."""
+        then the attention over this rank's work items."""
         q, k, v = inputs[l]
-        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx), pkg._ptr(kcnt),
-                                      None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
-        pkg._check(L.fvsr_lcsa_attention(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v), pkg._ptr(kidx),
-                                         pkg._ptr(kcnt), pkg._ptr(out), pkg._stream()))
+        select_call(q, k)
+        attention_call(q, k, v, out)
 
     def step():
         for l in range(layers):
             layer_call(l, outs[l & 1])
 
-    # kept triples per layer (deterministic given the inputs; read once, outside the timed region)
+    # kept triples per layer of this rank's items (deterministic given the inputs; read once, outside the timed region)
     for l in range(layers):
         layer_call(l, outs[0])
-        kept.append(int(kcnt.sum().item()))
+        kept.append(int(kcnt.view(-1)[item_begin:item_begin + item_count].sum().item()))
     flops_per_step = 4.0 * 128 ** 3 * sum(kept)
+    total_kept = sum(kept)
+    if world > 1:
+        t = torch.tensor([float(total_kept)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_kept = int(t.item())
+    flops_all_ranks = 4.0 * 128 ** 3 * total_kept
 
     for _ in range(args.warmup):
         step()
@@ -258,12 +293,10 @@ def run_ours(args):
     att_ms = []
     for l in range(layers):
         q, k, v = inputs[l]
-        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx), pkg._ptr(kcnt),
-                                      None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+        select_call(q, k)
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record(stream)
-        pkg._check(L.fvsr_lcsa_attention(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v), pkg._ptr(kidx),
-                                         pkg._ptr(kcnt), pkg._ptr(outs[0]), pkg._stream()))
+        attention_call(q, k, v, outs[0])
         a1.record(stream)
         a1.synchronize()
         att_ms.append(a0.elapsed_time(a1))
@@ -295,10 +328,8 @@ def run_ours(args):
                     ready[b].record(cp)
                 stream.wait_event(ready[b])
                 q, k, v = dbuf[b]
-                pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx),
-                                              pkg._ptr(kcnt), None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
-                pkg._check(L.fvsr_lcsa_attention(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
-                                                 pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(outs[b]), pkg._stream()))
+                select_call(q, k)
+                attention_call(q, k, v, outs[b])
                 free[b].record(stream)
                 hout[b].copy_(outs[b], non_blocking=True)
             torch.cuda.current_stream().synchronize()
@@ -319,23 +350,25 @@ def run_ours(args):
             t = torch.tensor([e2e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
-        e2e = {"value": world * flops_per_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        e2e = {"value": flops_all_ranks / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
 
     if rank == 0:
         peak, hbm, peak_kind = peaks()
         tr = profiled_traffic()
-        value = world * flops_per_step / (ms * 1e-3) / 1e12
+        value = flops_all_ranks / (ms * 1e-3) / 1e12
         line = {
-            "metric": "block-sparse attn effective TFLOP/s (+ ms per 30-layer chunk), config 3 1920x1152",
+            "metric": f"block-sparse attn effective TFLOP/s (+ ms per 30-layer chunk), config {args.config}",
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if shard else "weak",
+            "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "bf16" else "f32",
             "data": "synthetic (seeded normal Q/K/V per layer, window order, resident in HBM)",
             "config": {"workload": f"config {args.config}: {cfg.name}", "layers_per_step": layers,
                        "heads": g.heads, "q_blocks": g.nq, "k_blocks": g.nk, "topk": g.topk,
-                       "kept_triples_per_layer": sum(kept) / layers, "l2": "inputs > L2 (371 MB per layer), no flush",
+                       "kept_triples_per_layer": total_kept / layers, "l2": "inputs > L2 (371 MB per layer), no flush",
                        "launch": "eager" if args.no_graph else "CUDA graph of one step",
-                       "parallelism": f"{world} independent streams" if world > 1 else "1 GPU"},
+                       "parallelism": (f"{world} GPUs, (head, query block) items sharded, no collective" if shard
+                                       else (f"{world} independent streams" if world > 1 else "1 GPU"))},
             "ms_per_layer": ms / layers,
             "breakdown_ms_per_layer": {"attention": att_avg, "pool+select": sel_ms},
             "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
@@ -369,6 +402,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one instead of a CUDA graph")
+    ap.add_argument("--shard", dest="shard", action="store_true", default=None,
+                    help="split the config's (head, query block) items across the ranks (default for config 5)")
+    ap.add_argument("--replicas", dest="shard", action="store_false",
+                    help="one independent copy of the config per rank (default except for config 5)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -112,6 +112,14 @@ fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const void* q, c
 fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
                                 const int32_t* kidx, const int32_t* kcnt, void* out, fvsr_stream_t stream);
 
+/* fvsr_lcsa_attention restricted to the work items [item_begin, item_begin + item_count), item = h·Nq + qb
+ * (head-major): the query-block sharding unit when one (head, query block) space is split across GPUs. Rows of
+ * `out` outside the range are not written. The reference has no multi-device path; its per-item semantics are
+ * SparseAttention.swift:17-153 (one threadgroup per (query block, head)). */
+fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                      const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
+                                      int32_t item_count, fvsr_stream_t stream);
+
 /* kernelBlockAttention with the reference's own argument form (SparseAttention.swift:169-177): block_mask
  * (H, Nq, Nk) fp32, kept where > 0.5. Builds the index lists in `workspace`, then runs fvsr_lcsa_attention. */
 fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,

@@ -29,7 +29,7 @@ EXPORTED = [
     "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
-    "fvsr_lcsa_select_noalloc",
+    "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range",
 ]
 
 
@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         "fvsr_kv_cache_state": ([P, P, ctypes.POINTER(I32)], ctypes.c_int),
         "fvsr_lcsa_forward": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_lcsa_select_noalloc": ([PP, P, P, P, P, P, P, P, P], ctypes.c_int),
+        "fvsr_lcsa_attention_range": ([PP, P, P, P, P, P, P, I32, I32, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -247,6 +248,46 @@ def block_sparse_attention(q, k, v, kidx, kcnt, geom: Geometry, out=None, stream
     _check(lib().fvsr_lcsa_attention(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
                                      _ptr(out), _stream(stream)))
     return out.reshape(shape)
+
+
+def block_sparse_attention_range(q, k, v, kidx, kcnt, geom: Geometry, item_begin: int, item_count: int, out,
+                                 stream=None):
+    """block_sparse_attention for work items [item_begin, item_begin + item_count) only (item = h·Nq + qb)."""
+    q2, k2, v2, o2 = _rows(q), _rows(k), _rows(v), _rows(out)
+    g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(q2)})
+    p = g.params()
+    _check(lib().fvsr_lcsa_attention_range(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
+                                           _ptr(o2), int(item_begin), int(item_count), _stream(stream)))
+    return out
+
+
+@dataclass
+class Shard:
+    """One rank's share of a (head, query block) item space split across GPUs: global items [begin, end), the heads
+    they touch [head_lo, head_hi], and the range relative to those heads (what the rank's local tensors index)."""
+    begin: int
+    end: int
+    head_lo: int
+    head_hi: int
+
+    @property
+    def heads(self) -> int:
+        return self.head_hi - self.head_lo + 1
+
+    def local_range(self, nq: int) -> tuple[int, int]:
+        return self.begin - self.head_lo * nq, self.end - self.begin
+
+
+def shard_items(heads: int, nq: int, world: int, rank: int) -> Shard:
+    """Contiguous, balanced split of the H·Nq head-major work items. A rank needs the Q/K/V of every head it touches
+    (selection is joint over all query blocks of a (head, slice) row), so heads shared by two ranks are computed by
+    both; attention runs only on the rank's own items."""
+    total = heads * nq
+    b = total * rank // world
+    e = total * (rank + 1) // world
+    if e <= b:
+        return Shard(b, b, 0, -1)
+    return Shard(b, e, b // nq, (e - 1) // nq)
 
 
 def kernel_block_attention(q, k, v, block_mask, heads: int, workspace=None, stream=None):

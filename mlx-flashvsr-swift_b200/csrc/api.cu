@@ -148,14 +148,16 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
 
 fvsr_status run_attention(const fvsr_lcsa_params* p, const Dims& d, const void* q, const void* k, const void* v,
                           int64_t kv_rows, const KvPages& pages, const int32_t* kidx, const int32_t* kcnt, void* out,
-                          cudaStream_t st) {
+                          cudaStream_t st, int item_begin = 0, int item_count = -1) {
     fvsr_status s = check_device_sm100();
     if (s != FVSR_OK) return s;
+    if (item_count < 0) item_count = d.heads * d.nq;
     if (p->dtype == FVSR_BF16) {
-        FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, st), "bf16 attention launch");
+        FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, item_begin, item_count, st),
+                "bf16 attention launch");
     } else {
         FVSR_CU(launch_attn_f32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
-                                pages, d.heads, d.nq, d.nk, kidx, kcnt, static_cast<float*>(out), st),
+                                pages, d.heads, d.nq, d.nk, kidx, kcnt, static_cast<float*>(out), item_begin, item_count, st),
                 "fp32 attention launch");
     }
     return FVSR_OK;
@@ -252,6 +254,23 @@ fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const 
         return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
     return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out,
                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                      const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
+                                      int32_t item_count, fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!q || !k || !v || !kidx || !kcnt || !out) return fail(FVSR_EINVAL, "q, k, v, kidx, kcnt and out are required");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
+    const int64_t items = (int64_t)d.heads * d.nq;
+    if (item_begin < 0 || item_count < 0 || (int64_t)item_begin + item_count > items)
+        return fail(FVSR_EINVAL, "item range [%d, %d) is outside [0, %lld)", item_begin, item_begin + item_count,
+                    (long long)items);
+    return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out,
+                         reinterpret_cast<cudaStream_t>(stream), item_begin, item_count);
 }
 
 fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,

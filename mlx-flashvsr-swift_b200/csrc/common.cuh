@@ -40,11 +40,13 @@ size_t select_hist_bytes(int heads, int q_slices);
 size_t attn_bf16_smem_bytes(int nk);
 cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
                                  cudaStream_t st);
+// Attention over work items [item_begin, item_begin + item_count), item = h·nq + qb (head-major).
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
-                            int nk, const int32_t* kidx, const int32_t* kcnt, float* out, cudaStream_t st);
+                            int nk, const int32_t* kidx, const int32_t* kcnt, float* out, int item_begin,
+                            int item_count, cudaStream_t st);
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
-                             cudaStream_t st);
+                             int item_begin, int item_count, cudaStream_t st);
 // Reads and clears the device-side timeout word of the current device (1 if a wait gave up since the last read).
 cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st);
 

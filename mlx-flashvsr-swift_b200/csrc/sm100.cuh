@@ -1,5 +1,6 @@
 // sm100.cuh — thin inline-PTX wrappers for the Blackwell (sm_100a) features the attention kernel uses:
-// mbarriers with bounded waits, TMA 2-D tile loads (no multicast), tcgen05 MMA / TMEM allocation / TMEM load-store,
+// mbarriers with bounded waits, TMA 2-D tile loads (each CTA loads its own tiles), tcgen05 MMA / TMEM allocation /
+// TMEM load-store,
 // and the shared-memory matrix descriptors of the 128-byte-swizzled operand layouts.
 #pragma once
 
@@ -59,7 +60,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
-// ---- TMA (tiled, no multicast) ----
+// ---- TMA (tiled, one destination CTA per load) ----
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
