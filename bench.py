@@ -224,10 +224,15 @@ def run_ours(args):
         pkg._check(L.fvsr_lcsa_select(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx), pkg._ptr(kcnt),
                                       None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
 
+    order = torch.empty(max(item_count, 1), dtype=torch.int32, device=dev)
+
     def attention_call(q, k, v, out):
+        """Longest-first item schedule, then the attention over this rank's items."""
+        pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p), pkg._ptr(kcnt), item_begin, item_count, pkg._ptr(order),
+                                          pkg._stream()))
         pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
                                                pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(out), item_begin, item_count,
-                                               pkg._stream()))
+                                               pkg._ptr(order), pkg._stream()))
 
     def layer_call(l, out):
         """One layer through the C ABI: fvsr_lcsa_select (pool Q, pool K, scores + softmax, threshold + lists),
@@ -376,7 +381,7 @@ def run_ours(args):
                          "traffic": (tr or {}).get("bytes_per_launch"),
                          "traffic_source": (tr or {}).get("source")},
             "clocks": clk,
-            "gpu_launches": 7 * layers * args.steps,  # per layer: pool, scores, softmax, 2 histogram passes, finish, attention
+            "gpu_launches": 8 * layers * args.steps,  # per layer: pool, scores, softmax, 2 histogram passes, finish, order, attention
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:

@@ -112,13 +112,22 @@ fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const void* q, c
 fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
                                 const int32_t* kidx, const int32_t* kcnt, void* out, fvsr_stream_t stream);
 
-/* fvsr_lcsa_attention restricted to the work items [item_begin, item_begin + item_count), item = h·Nq + qb
- * (head-major): the query-block sharding unit when one (head, query block) space is split across GPUs. Rows of
- * `out` outside the range are not written. The reference has no multi-device path; its per-item semantics are
- * SparseAttention.swift:17-153 (one threadgroup per (query block, head)). */
+/* Work items are the (head, query block) pairs, item = h·Nq + qb (head-major). */
+
+/* Longest-first schedule of the items [item_begin, item_begin + item_count): order receives the item ids sorted by
+ * decreasing kcnt within each head (ties by id), heads kept in order, so long items start first and short ones fill
+ * the tail of the launch. order has item_count entries. No reference counterpart (scheduling only). */
+fvsr_status fvsr_lcsa_item_order(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin,
+                                 int32_t item_count, int32_t* order, fvsr_stream_t stream);
+
+/* fvsr_lcsa_attention restricted to the items [item_begin, item_begin + item_count), in the order given by `order`
+ * (a permutation of the range from fvsr_lcsa_item_order, or NULL for ascending): the query-block sharding unit when
+ * one (head, query block) space is split across GPUs. Rows of `out` outside the range are not written. The
+ * reference has no multi-device path; its per-item semantics are SparseAttention.swift:17-153 (one threadgroup per
+ * (query block, head)). */
 fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
                                       const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
-                                      int32_t item_count, fvsr_stream_t stream);
+                                      int32_t item_count, const int32_t* order, fvsr_stream_t stream);
 
 /* kernelBlockAttention with the reference's own argument form (SparseAttention.swift:169-177): block_mask
  * (H, Nq, Nk) fp32, kept where > 0.5. Builds the index lists in `workspace`, then runs fvsr_lcsa_attention. */

@@ -29,7 +29,7 @@ EXPORTED = [
     "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
-    "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range",
+    "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range", "fvsr_lcsa_item_order",
 ]
 
 
@@ -87,7 +87,8 @@ def lib() -> ctypes.CDLL:
         "fvsr_kv_cache_state": ([P, P, ctypes.POINTER(I32)], ctypes.c_int),
         "fvsr_lcsa_forward": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_lcsa_select_noalloc": ([PP, P, P, P, P, P, P, P, P], ctypes.c_int),
-        "fvsr_lcsa_attention_range": ([PP, P, P, P, P, P, P, I32, I32, P], ctypes.c_int),
+        "fvsr_lcsa_attention_range": ([PP, P, P, P, P, P, P, I32, I32, P, P], ctypes.c_int),
+        "fvsr_lcsa_item_order": ([PP, P, I32, I32, P, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -250,14 +251,26 @@ def block_sparse_attention(q, k, v, kidx, kcnt, geom: Geometry, out=None, stream
     return out.reshape(shape)
 
 
+def item_order(kcnt, geom: Geometry, item_begin: int, item_count: int, order=None, stream=None):
+    """Longest-first order of the items [item_begin, item_begin + item_count) within each head."""
+    torch = _torch()
+    if order is None:
+        order = torch.empty(item_count, dtype=torch.int32, device=kcnt.device)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_item_order(ctypes.byref(p), _ptr(kcnt), int(item_begin), int(item_count), _ptr(order),
+                                      _stream(stream)))
+    return order
+
+
 def block_sparse_attention_range(q, k, v, kidx, kcnt, geom: Geometry, item_begin: int, item_count: int, out,
-                                 stream=None):
-    """block_sparse_attention for work items [item_begin, item_begin + item_count) only (item = h·Nq + qb)."""
+                                 order=None, stream=None):
+    """block_sparse_attention for work items [item_begin, item_begin + item_count) only (item = h·Nq + qb), in the
+    given order (from item_order) or ascending."""
     q2, k2, v2, o2 = _rows(q), _rows(k), _rows(v), _rows(out)
     g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(q2)})
     p = g.params()
     _check(lib().fvsr_lcsa_attention_range(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
-                                           _ptr(o2), int(item_begin), int(item_count), _stream(stream)))
+                                           _ptr(o2), int(item_begin), int(item_count), _ptr(order), _stream(stream)))
     return out
 
 

@@ -89,6 +89,7 @@ struct Workspace {
     int32_t* kidx;
     int32_t* kcnt;
     uint32_t* hist;
+    int32_t* order;
     size_t bytes;
 };
 
@@ -107,6 +108,7 @@ Workspace layout(const Dims& d, void* base) {
     w.kidx = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * d.nk * 4));
     w.kcnt = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * 4));
     w.hist = reinterpret_cast<uint32_t*>(take(select_hist_bytes(d.heads, d.q_slices)));
+    w.order = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * 4));
     w.bytes = off;
     return w;
 }
@@ -148,16 +150,18 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
 
 fvsr_status run_attention(const fvsr_lcsa_params* p, const Dims& d, const void* q, const void* k, const void* v,
                           int64_t kv_rows, const KvPages& pages, const int32_t* kidx, const int32_t* kcnt, void* out,
-                          cudaStream_t st, int item_begin = 0, int item_count = -1) {
+                          cudaStream_t st, int item_begin = 0, int item_count = -1, const int32_t* order = nullptr) {
     fvsr_status s = check_device_sm100();
     if (s != FVSR_OK) return s;
     if (item_count < 0) item_count = d.heads * d.nq;
     if (p->dtype == FVSR_BF16) {
-        FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, item_begin, item_count, st),
+        FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, item_begin, item_count,
+                                 order, st),
                 "bf16 attention launch");
     } else {
         FVSR_CU(launch_attn_f32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
-                                pages, d.heads, d.nq, d.nk, kidx, kcnt, static_cast<float*>(out), item_begin, item_count, st),
+                                pages, d.heads, d.nq, d.nk, kidx, kcnt, static_cast<float*>(out), item_begin, item_count,
+                                order, st),
                 "fp32 attention launch");
     }
     return FVSR_OK;
@@ -256,9 +260,24 @@ fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const 
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
+fvsr_status fvsr_lcsa_item_order(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin, int32_t item_count,
+                                 int32_t* order, fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!kcnt || !order) return fail(FVSR_EINVAL, "kcnt and order are required");
+    const int64_t items = (int64_t)d.heads * d.nq;
+    if (item_begin < 0 || item_count < 0 || (int64_t)item_begin + item_count > items)
+        return fail(FVSR_EINVAL, "item range [%d, %d) is outside [0, %lld)", item_begin, item_begin + item_count,
+                    (long long)items);
+    FVSR_CU(launch_item_order(kcnt, d.nq, item_begin, item_count, order, reinterpret_cast<cudaStream_t>(stream)),
+            "item order launch");
+    return FVSR_OK;
+}
+
 fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
                                       const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
-                                      int32_t item_count, fvsr_stream_t stream) {
+                                      int32_t item_count, const int32_t* order, fvsr_stream_t stream) {
     Dims d;
     fvsr_status s = check_params(p, &d);
     if (s != FVSR_OK) return s;
@@ -270,7 +289,7 @@ fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, 
         return fail(FVSR_EINVAL, "item range [%d, %d) is outside [0, %lld)", item_begin, item_begin + item_count,
                     (long long)items);
     return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out,
-                         reinterpret_cast<cudaStream_t>(stream), item_begin, item_count);
+                         reinterpret_cast<cudaStream_t>(stream), item_begin, item_count, order);
 }
 
 fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
@@ -285,7 +304,8 @@ fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, c
         return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     FVSR_CU(launch_mask_to_lists(block_mask, d.heads, d.nq, d.nk, w.kidx, w.kcnt, st), "mask to lists launch");
-    return fvsr_lcsa_attention(p, q, k, v, w.kidx, w.kcnt, out, stream);
+    FVSR_CU(launch_item_order(w.kcnt, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
+    return fvsr_lcsa_attention_range(p, q, k, v, w.kidx, w.kcnt, out, 0, d.heads * d.nq, w.order, stream);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -434,8 +454,9 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     FVSR_CU(launch_pool(q, pp.dtype, d.nq, (int)d.channels, w.pooled_q, nullptr, st), "pool q launch");
     s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, st);
     if (s != FVSR_OK) return s;
+    FVSR_CU(launch_item_order(lc, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
     s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
-                      out, st);
+                      out, st, 0, d.heads * d.nq, w.order);
     if (s != FVSR_OK) return s;
     return fvsr_kv_cache_trim(cache);
 }

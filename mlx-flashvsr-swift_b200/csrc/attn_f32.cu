@@ -28,10 +28,10 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
                                                        const float* __restrict__ v, KvPages pages, int heads, int nq,
                                                        int nk, const int32_t* __restrict__ kidx,
                                                        const int32_t* __restrict__ kcnt, float* __restrict__ out,
-                                                       int item_begin) {
+                                                       int item_begin, const int32_t* __restrict__ order) {
     extern __shared__ float4 smem4[];
     F32Smem& sm = *reinterpret_cast<F32Smem*>(smem4);
-    const int item = item_begin + blockIdx.x;
+    const int item = order ? order[blockIdx.x] : item_begin + (int)blockIdx.x;
     const int h = item / nq, qb = item % nq;
     const int64_t ld = (int64_t)heads * kD;
     const int tid = threadIdx.x;
@@ -132,12 +132,12 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
 
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
                             int nk, const int32_t* kidx, const int32_t* kcnt, float* out, int item_begin,
-                            int item_count, cudaStream_t st) {
+                            int item_count, const int32_t* order, cudaStream_t st) {
     if (item_count <= 0) return cudaSuccess;
     const int smem = (int)sizeof(F32Smem);
     cudaError_t e = cudaFuncSetAttribute(attn_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    attn_f32_kernel<<<item_count, 256, smem, st>>>(q, k, v, pages, heads, nq, nk, kidx, kcnt, out, item_begin);
+    attn_f32_kernel<<<item_count, 256, smem, st>>>(q, k, v, pages, heads, nq, nk, kidx, kcnt, out, item_begin, order);
     return cudaGetLastError();
 }
 

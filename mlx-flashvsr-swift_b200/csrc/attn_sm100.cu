@@ -77,6 +77,7 @@ struct AttnArgs {
     __nv_bfloat16* out;
     int heads, nq, nk;
     int item_begin;
+    const int32_t* order;  // optional item order (longest first within each head); NULL = ascending
     float scale_log2;
     KvPages pages;
 };
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const int item = a.item_begin + blockIdx.x;
+    const int item = a.order ? a.order[blockIdx.x] : a.item_begin + (int)blockIdx.x;
     const int h = item / a.nq, qb = item % a.nq;
     const int64_t ld = (int64_t)a.heads * kD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -368,7 +369,7 @@ size_t attn_bf16_smem_bytes(int nk) { return 1024 + kOffList + sizeof(int32_t) *
 
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
-                             int item_begin, int item_count, cudaStream_t st) {
+                             int item_begin, int item_count, const int32_t* order, cudaStream_t st) {
     if (item_count <= 0) return cudaSuccess;
     CUtensorMap mq, mk, mv;
     const int64_t channels = (int64_t)heads * kD;
@@ -386,6 +387,7 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     a.nq = nq;
     a.nk = nk;
     a.item_begin = item_begin;
+    a.order = order;
     a.scale_log2 = (1.0f / sqrtf((float)kD)) * 1.4426950408889634f;
     a.pages = pages;
     attn_bf16_sm100_kernel<<<item_count, kThreads, smem, st>>>(mq, mk, mv, a);

@@ -40,13 +40,17 @@ size_t select_hist_bytes(int heads, int q_slices);
 size_t attn_bf16_smem_bytes(int nk);
 cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
                                  cudaStream_t st);
-// Attention over work items [item_begin, item_begin + item_count), item = h·nq + qb (head-major).
+// Attention over work items [item_begin, item_begin + item_count), item = h·nq + qb (head-major); CTA b takes
+// item order[b] when an order is given (a permutation of the range), else item_begin + b.
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
                             int nk, const int32_t* kidx, const int32_t* kcnt, float* out, int item_begin,
-                            int item_count, cudaStream_t st);
+                            int item_count, const int32_t* order, cudaStream_t st);
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
-                             int item_begin, int item_count, cudaStream_t st);
+                             int item_begin, int item_count, const int32_t* order, cudaStream_t st);
+// Longest-first order of the items [item_begin, item_begin + item_count) within each head (stable by item id).
+cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int item_count, int32_t* order,
+                              cudaStream_t st);
 // Reads and clears the device-side timeout word of the current device (1 if a wait gave up since the last read).
 cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st);
 

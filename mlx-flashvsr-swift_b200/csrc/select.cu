@@ -485,3 +485,45 @@ cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, i
 }
 
 }  // namespace fvsr
+
+namespace fvsr {
+
+namespace {
+
+// One CTA per head segment of the range: rank of each item = items of the segment with a longer key list, or an
+// equal one and a smaller id; the item goes to that position inside its segment (segments keep head-major order).
+__global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restrict__ kcnt, int nq, int item_begin,
+                                                         int item_count, int32_t* __restrict__ order) {
+    __shared__ int32_t sc[4096];
+    const int h = item_begin / nq + blockIdx.x;
+    const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
+    const int n = s1 - s0;
+    if (n <= 0) return;
+    if (n > 4096) {  // no room to rank: keep ascending order
+        for (int i = threadIdx.x; i < n; i += blockDim.x) order[s0 - item_begin + i] = s0 + i;
+        return;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = kcnt[s0 + i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int ci = sc[i];
+        int rank = 0;
+        for (int t = 0; t < n; ++t) {
+            const int ct = sc[t];
+            rank += (ct > ci) || (ct == ci && t < i);
+        }
+        order[s0 - item_begin + rank] = s0 + i;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int item_count, int32_t* order,
+                              cudaStream_t st) {
+    if (item_count <= 0) return cudaSuccess;
+    const int h0 = item_begin / nq, h1 = (item_begin + item_count - 1) / nq;
+    item_order_kernel<<<h1 - h0 + 1, 256, 0, st>>>(kcnt, nq, item_begin, item_count, order);
+    return cudaGetLastError();
+}
+
+}  // namespace fvsr

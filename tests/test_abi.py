@@ -43,7 +43,7 @@ def test_workspace_size_matches_layout(fvsr):
     n = fvsr.workspace_size(g)
     a = lambda x: (x + 255) // 256 * 256  # noqa: E731
     c = 12 * 128
-    want = a(g.nq * c * 4) + a(g.nk * c * 4) + a(12 * g.nq * g.nk * 4) * 2 + a(12 * g.nq * 4) + a(12 * 1 * 5136 * 4)
+    want = a(g.nq * c * 4) + a(g.nk * c * 4) + a(12 * g.nq * g.nk * 4) * 2 + a(12 * g.nq * 4) + a(12 * 1 * 5136 * 4) + a(12 * g.nq * 4)
     assert n == want
 
 

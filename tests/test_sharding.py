@@ -87,7 +87,15 @@ def test_range_attention_reproduces_one_gpu_items(fvsr):
         sl = fvsr.draft_block_mask_and_probs(ql, kl, gl, want_mask=False, want_probs=False)
         out = torch.zeros_like(ql)
         lb, lc = sh.local_range(g.nq)
-        fvsr.block_sparse_attention_range(ql, kl, vl, sl["kidx"], sl["kcnt"], gl, lb, lc, out)
+        order = fvsr.item_order(sl["kcnt"], gl, lb, lc) if r % 2 == 0 else None   # the schedule changes no result
+        if order is not None:
+            o = order.cpu().numpy()
+            assert sorted(o.tolist()) == list(range(lb, lb + lc))
+            kc = sl["kcnt"].view(-1).cpu().numpy()
+            for hseg in range(sh.heads):   # longest first within each head segment, heads in order
+                seg = [x for x in o if x // g.nq == hseg]
+                assert all(kc[a] >= kc[b] for a, b in zip(seg, seg[1:]))
+        fvsr.block_sparse_attention_range(ql, kl, vl, sl["kidx"], sl["kcnt"], gl, lb, lc, out, order=order)
         torch.cuda.synchronize()
         for it in range(sh.begin, sh.end):
             h, qb = divmod(it, g.nq)
