@@ -141,7 +141,7 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
                        const KvPages& pk_pages, int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs,
                        uint32_t* hist, cudaStream_t st) {
     FVSR_CU(launch_select_scores(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range,
-                                 p->q_slices, p->topk, probs, hist, st),
+                                 p->q_slices, p->topk, probs, hist, st, /*clear_hist=*/false),
             "select scores launch");
     FVSR_CU(launch_select_threshold(probs, d.heads, d.nq, d.nk, p->q_slices, p->topk, hist, kidx, kcnt, mask, st),
             "select threshold launch");
@@ -243,7 +243,7 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const float* pk = pooled_k ? pooled_k : w.pooled_k;
     FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, pooled_k ? nullptr : k, pooled_k ? 0 : d.nk, w.pooled_k, p->dtype,
-                         (int)d.channels, st),
+                         (int)d.channels, st, w.hist, select_hist_bytes(d.heads, d.q_slices) / 4),
             "pool launch");
     return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, w.hist, st);
 }
@@ -451,7 +451,9 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
         pages.page_block[i] = (i < (int)cache->pages.size() ? cache->pages[i] : 0) * d.s;
     int32_t* li = kidx ? kidx : w.kidx;
     int32_t* lc = kcnt ? kcnt : w.kcnt;
-    FVSR_CU(launch_pool(q, pp.dtype, d.nq, (int)d.channels, w.pooled_q, nullptr, st), "pool q launch");
+    FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, nullptr, 0, nullptr, pp.dtype, (int)d.channels, st, w.hist,
+                         select_hist_bytes(d.heads, d.q_slices) / 4),
+            "pool q launch");
     s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, st);
     if (s != FVSR_OK) return s;
     FVSR_CU(launch_item_order(lc, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");

@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
                                                        int item_begin, const int32_t* __restrict__ order) {
     extern __shared__ float4 smem4[];
     F32Smem& sm = *reinterpret_cast<F32Smem*>(smem4);
+    griddep_wait_then_release();
     const int item = order ? order[blockIdx.x] : item_begin + (int)blockIdx.x;
     const int h = item / nq, qb = item % nq;
     const int64_t ld = (int64_t)heads * kD;
@@ -137,8 +138,8 @@ cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, cons
     const int smem = (int)sizeof(F32Smem);
     cudaError_t e = cudaFuncSetAttribute(attn_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    attn_f32_kernel<<<item_count, 256, smem, st>>>(q, k, v, pages, heads, nq, nk, kidx, kcnt, out, item_begin, order);
-    return cudaGetLastError();
+    return launch_pdl(attn_f32_kernel, dim3(item_count), dim3(256), (size_t)smem, st, q, k, v, pages, heads, nq, nk,
+                      kidx, kcnt, out, item_begin, order);
 }
 
 }  // namespace fvsr

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
+    griddep_wait_then_release();
     const int item = a.order ? a.order[blockIdx.x] : a.item_begin + (int)blockIdx.x;
     const int h = item / a.nq, qb = item % a.nq;
     const int64_t ld = (int64_t)a.heads * kD;
@@ -390,8 +391,7 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     a.order = order;
     a.scale_log2 = (1.0f / sqrtf((float)kD)) * 1.4426950408889634f;
     a.pages = pages;
-    attn_bf16_sm100_kernel<<<item_count, kThreads, smem, st>>>(mq, mk, mv, a);
-    return cudaGetLastError();
+    return launch_pdl(attn_bf16_sm100_kernel, dim3(item_count), dim3(kThreads), smem, st, mq, mk, mv, a);
 }
 
 cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st) {

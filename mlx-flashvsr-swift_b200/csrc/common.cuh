@@ -24,15 +24,40 @@ __host__ __device__ inline int32_t kv_phys_block(const KvPages& pg, int32_t j) {
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
+// Programmatic dependent launch: every kernel of the path first waits for the kernel before it in the stream to have
+// completed (griddepcontrol.wait — a hardware wait, and a no-op when launched without the attribute), then lets the
+// next kernel start launching, so launch latency and CTA ramp-up overlap the previous kernel's tail.
+__device__ __forceinline__ void griddep_wait_then_release() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ---- launchers (each returns the launch's cudaError_t) ----
 cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
                         cudaStream_t st);
-// Pools two tensors (n1 and n2 blocks) in one launch.
+// Pools two tensors (n1 and n2 blocks) in one launch; also clears zero_words 32-bit words at `zero` (the selection's
+// histograms, which the next kernels accumulate into).
 cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,
-                         float* out2, int dtype, int channels, cudaStream_t st);
+                         float* out2, int dtype, int channels, cudaStream_t st, uint32_t* zero = nullptr,
+                         size_t zero_words = 0);
 cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
                                  int bh, int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist,
-                                 cudaStream_t st);
+                                 cudaStream_t st, bool clear_hist = true);
 cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
                                     uint32_t* hist, int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st);
 size_t select_scores_smem_bytes(int nk);

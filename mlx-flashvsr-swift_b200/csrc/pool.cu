@@ -18,8 +18,14 @@ constexpr int kPoolChannels = kPoolLanes * 8;  // 512 channels per CTA
 template <int DT>
 __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, int channels, float* __restrict__ out,
                                                    void* __restrict__ copy_dst, int n1, const void* __restrict__ x2,
-                                                   float* __restrict__ out2) {
+                                                   float* __restrict__ out2, uint32_t* __restrict__ zero,
+                                                   size_t zero_words) {
     __shared__ float part[4][kPoolChannels];
+    griddep_wait_then_release();
+    if (zero) {
+        const size_t nb = (size_t)gridDim.x * gridDim.y, bid = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+        for (size_t w = bid * 256 + threadIdx.x; w < zero_words; w += nb * 256) zero[w] = 0;
+    }
     const int lane = threadIdx.x & (kPoolLanes - 1);
     const int g = threadIdx.x / kPoolLanes;  // token group: tokens [32g, 32g + 32)
     const int c0 = blockIdx.x * kPoolChannels + lane * 8;
@@ -104,14 +110,14 @@ cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels,
 }
 
 cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,
-                         float* out2, int dtype, int channels, cudaStream_t st) {
+                         float* out2, int dtype, int channels, cudaStream_t st, uint32_t* zero, size_t zero_words) {
     if (n1 + n2 == 0) return cudaSuccess;
     dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)(n1 + n2));
     if (dtype == 1)
-        pool_kernel<1><<<grid, 256, 0, st>>>(x1, channels, out1, copy_dst, (int)n1, x2, out2);
-    else
-        pool_kernel<0><<<grid, 256, 0, st>>>(x1, channels, out1, copy_dst, (int)n1, x2, out2);
-    return cudaGetLastError();
+        return launch_pdl(pool_kernel<1>, grid, dim3(256), 0, st, x1, channels, out1, copy_dst, (int)n1, x2, out2, zero,
+                          zero_words);
+    return launch_pdl(pool_kernel<0>, grid, dim3(256), 0, st, x1, channels, out1, copy_dst, (int)n1, x2, out2, zero,
+                      zero_words);
 }
 
 }  // namespace fvsr

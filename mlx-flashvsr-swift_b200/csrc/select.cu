@@ -185,6 +185,7 @@ __device__ __forceinline__ uint32_t row_rank0(int64_t n, int topk) {
 __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restrict__ pq, const float* __restrict__ pk,
                                                             KvPages pages, int heads, int nq, int nk, int bh, int bw,
                                                             int local_range, float sqrt_d, float* __restrict__ scores) {
+    griddep_wait_then_release();
     extern __shared__ float4 score_smem[];
     float* sq = reinterpret_cast<float*>(score_smem);  // [kTI][kPS]
     float* sk = sq + kTI * kPS;                         // [kTJ][kPS]
@@ -267,6 +268,7 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
 __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* __restrict__ probs, int nq, int nk,
                                                                        int q_slices,
                                                              int topk, uint32_t* __restrict__ hist) {
+    griddep_wait_then_release();
     __shared__ uint32_t shist[2][kBins1];
     const int h = blockIdx.y;
     const int i0 = blockIdx.x * kSoftRows;
@@ -348,6 +350,7 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
 // Passes 2 and 3 of the radix select: one CTA per kHistChunk entries of one (head, query slice) row.
 __global__ void __launch_bounds__(256) select_hist_kernel(const float* __restrict__ probs, int nq, int nk, int q_slices,
                                                           int topk, uint32_t* __restrict__ hist, int pass) {
+    griddep_wait_then_release();
     __shared__ uint32_t sh[kBins2];
     const int row = blockIdx.y;
     const int h = row / q_slices, t = row % q_slices;
@@ -388,6 +391,7 @@ __global__ void __launch_bounds__(256) select_finish_kernel(const float* __restr
                                                             int q_slices, int topk, const uint32_t* __restrict__ hist,
                                                             int32_t* __restrict__ kidx, int32_t* __restrict__ kcnt,
                                                             uint8_t* __restrict__ mask) {
+    griddep_wait_then_release();
     const int row = blockIdx.y;
     const int h = row / q_slices, t = row % q_slices;
     const int nqs = nq / q_slices;
@@ -422,6 +426,7 @@ __global__ void __launch_bounds__(256) select_finish_kernel(const float* __restr
 
 __global__ void __launch_bounds__(256) mask_to_lists_kernel(const float* __restrict__ mask, int rows, int nk,
                                                             int32_t* __restrict__ kidx, int32_t* __restrict__ kcnt) {
+    griddep_wait_then_release();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     const float* m = mask + (int64_t)warp * nk;
@@ -446,20 +451,19 @@ size_t select_hist_bytes(int heads, int q_slices) { return sizeof(uint32_t) * (s
 
 cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
                                  int bh, int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist,
-                                 cudaStream_t st) {
-    cudaError_t e = cudaMemsetAsync(hist, 0, select_hist_bytes(heads, q_slices), st);
-    if (e != cudaSuccess) return e;
+                                 cudaStream_t st, bool clear_hist) {
+    cudaError_t e = cudaSuccess;
+    if (clear_hist && (e = cudaMemsetAsync(hist, 0, select_hist_bytes(heads, q_slices), st)) != cudaSuccess) return e;
     const int smem = (int)select_scores_smem_bytes(nk);
     e = cudaFuncSetAttribute(select_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const float sqrt_d = sqrtf((float)kD);
     dim3 grid((nk + kTJ - 1) / kTJ, (nq + kTI - 1) / kTI, heads);
-    select_scores_kernel<<<grid, 256, smem, st>>>(pq, pk, pk_pages, heads, nq, nk, bh, bw, local_range, sqrt_d, probs);
-    e = cudaGetLastError();
+    e = launch_pdl(select_scores_kernel, grid, dim3(256), (size_t)smem, st, pq, pk, pk_pages, heads, nq, nk, bh, bw,
+                   local_range, sqrt_d, probs);
     if (e != cudaSuccess) return e;
     dim3 sgrid((nq + kSoftRows - 1) / kSoftRows, heads);
-    select_softmax_kernel<<<sgrid, kSoftRows * 32, 0, st>>>(probs, nq, nk, q_slices, topk, hist);
-    return cudaGetLastError();
+    return launch_pdl(select_softmax_kernel, sgrid, dim3(kSoftRows * 32), 0, st, probs, nq, nk, q_slices, topk, hist);
 }
 
 cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
@@ -468,20 +472,20 @@ cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int n
     const int64_t n = (int64_t)(nq / q_slices) * nk;
     dim3 hgrid((unsigned)((n + kHistChunk - 1) / kHistChunk), rows);
     for (int pass = 2; pass <= 3; ++pass) {
-        select_hist_kernel<<<hgrid, 256, 0, st>>>(probs, nq, nk, q_slices, topk, hist, pass);
-        cudaError_t e = cudaGetLastError();
+        const cudaError_t e =
+            launch_pdl(select_hist_kernel, hgrid, dim3(256), 0, st, probs, nq, nk, q_slices, topk, hist, pass);
         if (e != cudaSuccess) return e;
     }
     dim3 fgrid((nq / q_slices + kFinishRows - 1) / kFinishRows, rows);
-    select_finish_kernel<<<fgrid, 256, 0, st>>>(probs, nq, nk, q_slices, topk, hist, kidx, kcnt, mask);
-    return cudaGetLastError();
+    return launch_pdl(select_finish_kernel, fgrid, dim3(256), 0, st, probs, nq, nk, q_slices, topk, hist, kidx, kcnt,
+                      mask);
 }
 
 cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
                                  cudaStream_t st) {
     const int rows = heads * nq;
-    mask_to_lists_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(mask, rows, nk, kidx, kcnt);
-    return cudaGetLastError();
+    return launch_pdl(mask_to_lists_kernel, dim3((rows * 32 + 255) / 256), dim3(256), 0, st, mask, rows, nk, kidx,
+                      kcnt);
 }
 
 }  // namespace fvsr
@@ -494,6 +498,7 @@ namespace {
 // equal one and a smaller id; the item goes to that position inside its segment (segments keep head-major order).
 __global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restrict__ kcnt, int nq, int item_begin,
                                                          int item_count, int32_t* __restrict__ order) {
+    griddep_wait_then_release();
     __shared__ int32_t sc[4096];
     const int h = item_begin / nq + blockIdx.x;
     const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
@@ -522,8 +527,7 @@ cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int i
                               cudaStream_t st) {
     if (item_count <= 0) return cudaSuccess;
     const int h0 = item_begin / nq, h1 = (item_begin + item_count - 1) / nq;
-    item_order_kernel<<<h1 - h0 + 1, 256, 0, st>>>(kcnt, nq, item_begin, item_count, order);
-    return cudaGetLastError();
+    return launch_pdl(item_order_kernel, dim3(h1 - h0 + 1), dim3(256), 0, st, kcnt, nq, item_begin, item_count, order);
 }
 
 }  // namespace fvsr
