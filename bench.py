@@ -192,7 +192,9 @@ def run_ours(args):
         # the config's (head, query block) items split across ranks (strong scaling, no data-path collective: LCSA
         # heads are independent, so each rank holds the Q/K/V of the heads its items touch, as a tensor-parallel
         # QKV projection leaves them); inputs are seeded per head, so the ranks together solve the one-GPU problem
-        sh = pkg.shard_items(g.heads, g.nq, world, rank)
+        sh_world, sh_rank = (world, rank) if not args.as_rank else (int(args.as_rank.split("/")[1]),
+                                                                    int(args.as_rank.split("/")[0]))
+        sh = pkg.shard_items(g.heads, g.nq, sh_world, sh_rank)
         g_loc = pkg.Geometry(**{**g.__dict__, "heads": max(sh.heads, 1)})
         item_begin, item_count = sh.local_range(g.nq) if sh.heads > 0 else (0, 0)
 
@@ -225,9 +227,19 @@ def run_ours(args):
                                       None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
 
     order = torch.empty(max(item_count, 1), dtype=torch.int32, device=dev)
+    use_split = shard and not args.no_split
+    sched = torch.empty(pkg.schedule_size(g_loc, item_count) if use_split else 1, dtype=torch.uint8, device=dev)
 
     def attention_call(q, k, v, out):
-        """Longest-first item schedule, then the attention over this rank's items."""
+        """Sharded: the balanced unit schedule (long key lists split, partials merged) and the attention over it.
+        Otherwise: the longest-first item order, then the attention over the rank's items."""
+        if use_split:
+            pkg._check(L.fvsr_lcsa_schedule(ctypes.byref(p), pkg._ptr(kcnt), item_begin, item_count, pkg._ptr(sched),
+                                            sched.numel(), pkg._stream()))
+            pkg._check(L.fvsr_lcsa_attention_scheduled(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
+                                                       pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(out), item_begin,
+                                                       item_count, pkg._ptr(sched), sched.numel(), pkg._stream()))
+            return
         pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p), pkg._ptr(kcnt), item_begin, item_count, pkg._ptr(order),
                                           pkg._stream()))
         pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
@@ -373,7 +385,9 @@ def run_ours(args):
                        "kept_triples_per_layer": total_kept / layers, "l2": "inputs > L2 (371 MB per layer), no flush",
                        "launch": "eager" if args.no_graph else "CUDA graph of one step",
                        "parallelism": (f"{world} GPUs, (head, query block) items sharded, no collective" if shard
-                                       else (f"{world} independent streams" if world > 1 else "1 GPU"))},
+                                       else (f"{world} independent streams" if world > 1 else "1 GPU")),
+                       **({"emulated_rank": args.as_rank} if shard and args.as_rank else {}),
+                       **({"schedule": "split key lists" if use_split else "longest-first items"} if shard else {})},
             "ms_per_layer": ms / layers,
             "breakdown_ms_per_layer": {"attention": att_avg, "pool+select": sel_ms},
             "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
@@ -381,7 +395,8 @@ def run_ours(args):
                          "traffic": (tr or {}).get("bytes_per_launch"),
                          "traffic_source": (tr or {}).get("source")},
             "clocks": clk,
-            "gpu_launches": 8 * layers * args.steps,  # per layer: pool, scores, softmax, 2 histogram passes, finish, order, attention
+            # per layer: pool, scores, softmax, 2 histogram passes, finish, order (or schedule), attention (+ combine)
+            "gpu_launches": (9 if use_split else 8) * layers * args.steps,
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:
@@ -406,6 +421,10 @@ def main():
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--as-rank", default=None, metavar="R/N",
+                    help="development: one GPU times rank R's share of an N-way sharded run (no process group)")
+    ap.add_argument("--no-split", action="store_true",
+                    help="sharded runs: longest-first item order without splitting long key lists")
     ap.add_argument("--no-graph", action="store_true", help="launch the step's kernels one by one instead of a CUDA graph")
     ap.add_argument("--shard", dest="shard", action="store_true", default=None,
                     help="split the config's (head, query block) items across the ranks (default for config 5)")

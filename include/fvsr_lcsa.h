@@ -129,6 +129,25 @@ fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, 
                                       const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
                                       int32_t item_count, const int32_t* order, fvsr_stream_t stream);
 
+/* Balanced schedule of the items [item_begin, item_begin + item_count) — no counterpart in the reference (it is the
+ * B200 kernel's work distribution). With S kept key blocks in the range and M multiprocessors on the current device,
+ * the bf16 lane cuts every key list longer than T = max(ceil(S / 2M), 16) blocks into ceil(len / T) near-equal
+ * chunks, so a short range (few CTA waves, as on each GPU of a sharded problem) is not bounded by its longest items;
+ * units (item, chunk) run longest first and split items are merged afterwards. The fp32 lane orders without
+ * splitting. fvsr_lcsa_schedule_size gives the bytes of the device buffer (header, units, order, fp32 partial
+ * results: about 66 KB × 4M + 20 B × item_count); the buffer is reused by fvsr_lcsa_attention_scheduled. */
+fvsr_status fvsr_lcsa_schedule_size(const fvsr_lcsa_params* p, int32_t item_count, size_t* bytes);
+fvsr_status fvsr_lcsa_schedule(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin,
+                               int32_t item_count, void* schedule, size_t schedule_bytes, fvsr_stream_t stream);
+
+/* fvsr_lcsa_attention_range over a schedule from fvsr_lcsa_schedule (same p, kcnt and range, same device): the
+ * attention over its units, then the merge of split items. Same output as fvsr_lcsa_attention_range up to the
+ * summation order of split key lists. */
+fvsr_status fvsr_lcsa_attention_scheduled(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                          const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
+                                          int32_t item_count, const void* schedule, size_t schedule_bytes,
+                                          fvsr_stream_t stream);
+
 /* kernelBlockAttention with the reference's own argument form (SparseAttention.swift:169-177): block_mask
  * (H, Nq, Nk) fp32, kept where > 0.5. Builds the index lists in `workspace`, then runs fvsr_lcsa_attention. */
 fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,

@@ -29,7 +29,8 @@ EXPORTED = [
     "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
-    "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range", "fvsr_lcsa_item_order",
+    "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range", "fvsr_lcsa_item_order", "fvsr_lcsa_schedule_size",
+    "fvsr_lcsa_schedule", "fvsr_lcsa_attention_scheduled",
 ]
 
 
@@ -89,6 +90,9 @@ def lib() -> ctypes.CDLL:
         "fvsr_lcsa_select_noalloc": ([PP, P, P, P, P, P, P, P, P], ctypes.c_int),
         "fvsr_lcsa_attention_range": ([PP, P, P, P, P, P, P, I32, I32, P, P], ctypes.c_int),
         "fvsr_lcsa_item_order": ([PP, P, I32, I32, P, P], ctypes.c_int),
+        "fvsr_lcsa_schedule_size": ([PP, I32, ctypes.POINTER(SZ)], ctypes.c_int),
+        "fvsr_lcsa_schedule": ([PP, P, I32, I32, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_attention_scheduled": ([PP, P, P, P, P, P, P, I32, I32, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -271,6 +275,67 @@ def block_sparse_attention_range(q, k, v, kidx, kcnt, geom: Geometry, item_begin
     p = g.params()
     _check(lib().fvsr_lcsa_attention_range(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
                                            _ptr(o2), int(item_begin), int(item_count), _ptr(order), _stream(stream)))
+    return out
+
+
+def schedule_size(geom: Geometry, item_count: int) -> int:
+    """Bytes of the device buffer fvsr_lcsa_schedule fills for a range of item_count items (current device)."""
+    n = ctypes.c_size_t(0)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_schedule_size(ctypes.byref(p), int(item_count), ctypes.byref(n)))
+    return n.value
+
+
+def make_schedule(kcnt, geom: Geometry, item_begin: int, item_count: int, buf=None, stream=None):
+    """Work schedule of the items [item_begin, item_begin + item_count): for a short range (at most 8 items per SM)
+    the persistent kernel's partition — per head, the head's kept key blocks in equal shares per SM, cut items merged
+    afterwards — else the longest-first item order. Returns the uint8 device buffer (reused by
+    block_sparse_attention_scheduled)."""
+    torch = _torch()
+    nbytes = schedule_size(geom, item_count)
+    if buf is None:
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=kcnt.device)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_schedule(ctypes.byref(p), _ptr(kcnt), int(item_begin), int(item_count), _ptr(buf),
+                                    buf.numel(), _stream(stream)))
+    return buf
+
+
+def schedule_view(buf, geom: Geometry, item_count: int):
+    """Host view of a persistent-mode schedule buffer (synchronises): header (segments, cut items, pieces, heads of
+    the range, empty items), per-SM segment ranges, segments (item, first list position, length, piece slot or -1),
+    merge records (item, first slot, pieces) and the empty items."""
+    import numpy as np
+    torch = _torch()
+    torch.cuda.synchronize(buf.device)
+    b = buf.cpu().numpy()
+    a = lambda x: (x + 255) & ~255
+    G = torch.cuda.get_device_properties(buf.device).multi_processor_count
+    hr = min(geom.heads, (item_count - 1) // geom.nq + 2)
+    off_seg_begin = a(32) + a(item_count * 4)
+    off_segs = off_seg_begin + a((G + 1) * 4)
+    off_comb = off_segs + a((item_count + G * hr) * 16)
+    off_empties = off_comb + a(G * hr * 16)
+    hdr = b[:20].view(np.int32)
+    n_segs, n_comb, n_empty = int(hdr[0]), int(hdr[1]), int(hdr[4])
+    return ({"segments": n_segs, "cut_items": n_comb, "pieces": int(hdr[2]), "heads": int(hdr[3]),
+             "empty_items": n_empty},
+            b[off_seg_begin:off_seg_begin + 4 * (G + 1)].view(np.int32),
+            b[off_segs:off_segs + 16 * n_segs].view(np.int32).reshape(n_segs, 4),
+            b[off_comb:off_comb + 16 * n_comb].view(np.int32).reshape(n_comb, 4),
+            b[off_empties:off_empties + 4 * n_empty].view(np.int32))
+
+
+def block_sparse_attention_scheduled(q, k, v, kidx, kcnt, geom: Geometry, item_begin: int, item_count: int, out,
+                                     schedule, stream=None):
+    """block_sparse_attention_range over a schedule from make_schedule (same kcnt and range): the persistent bf16
+    kernel, then the merge of cut items and the zeros of empty ones (the fp32 lane runs the per-item kernel)."""
+    q2, k2, v2, o2 = _rows(q), _rows(k), _rows(v), _rows(out)
+    g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(q2)})
+    p = g.params()
+    _check(lib().fvsr_lcsa_attention_scheduled(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
+                                               _ptr(o2), int(item_begin), int(item_count), _ptr(schedule),
+                                               schedule.numel(), _stream(stream)))
     return out
 
 

@@ -292,6 +292,89 @@ fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, 
                          reinterpret_cast<cudaStream_t>(stream), item_begin, item_count, order);
 }
 
+namespace {
+
+fvsr_status sched_geometry(const fvsr_lcsa_params* p, Dims* d, int32_t item_begin, int32_t item_count,
+                           fvsr::SchedLayout* L) {
+    fvsr_status s = check_params(p, d);
+    if (s != FVSR_OK) return s;
+    const int64_t items = (int64_t)d->heads * d->nq;
+    if (item_begin < 0 || item_count < 0 || (int64_t)item_begin + item_count > items)
+        return fail(FVSR_EINVAL, "item range [%d, %d) is outside [0, %lld)", item_begin, item_begin + item_count,
+                    (long long)items);
+    int dev = 0, nsm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess || nsm <= 0) {
+        cudaGetLastError();
+        return fail(FVSR_ECUDA, "cannot read the device's multiprocessor count");
+    }
+    *L = fvsr::sched_layout(item_count, d->nq, d->heads, nsm);
+    return FVSR_OK;
+}
+
+}  // namespace
+
+fvsr_status fvsr_lcsa_schedule_size(const fvsr_lcsa_params* p, int32_t item_count, size_t* bytes) {
+    Dims d;
+    fvsr::SchedLayout L;
+    if (!bytes) return fail(FVSR_EINVAL, "bytes is NULL");
+    fvsr_status s = sched_geometry(p, &d, 0, item_count, &L);
+    if (s != FVSR_OK) return s;
+    *bytes = L.bytes;
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_schedule(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin, int32_t item_count,
+                               void* schedule, size_t schedule_bytes, fvsr_stream_t stream) {
+    Dims d;
+    fvsr::SchedLayout L;
+    fvsr_status s = sched_geometry(p, &d, item_begin, item_count, &L);
+    if (s != FVSR_OK) return s;
+    if (!kcnt || !schedule) return fail(FVSR_EINVAL, "kcnt and schedule are required");
+    if (!aligned16(schedule)) return fail(FVSR_EINVAL, "schedule must be 16-byte aligned");
+    if (schedule_bytes < L.bytes)
+        return fail(FVSR_ENOMEM, "schedule of %zu bytes is smaller than the %zu required", schedule_bytes, L.bytes);
+    if (item_count == 0) return FVSR_OK;
+    s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    FVSR_CU(fvsr::launch_schedule(kcnt, d.nk, d.nq, item_begin, item_count, L, schedule,
+                                  reinterpret_cast<cudaStream_t>(stream)),
+            "schedule launch");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_attention_scheduled(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
+                                          const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
+                                          int32_t item_count, const void* schedule, size_t schedule_bytes,
+                                          fvsr_stream_t stream) {
+    Dims d;
+    fvsr::SchedLayout L;
+    fvsr_status s = sched_geometry(p, &d, item_begin, item_count, &L);
+    if (s != FVSR_OK) return s;
+    if (!q || !k || !v || !kidx || !kcnt || !out || !schedule)
+        return fail(FVSR_EINVAL, "q, k, v, kidx, kcnt, out and schedule are required");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(schedule))
+        return fail(FVSR_EINVAL, "q, k, v, out and schedule must be 16-byte aligned");
+    if (schedule_bytes < L.bytes)
+        return fail(FVSR_ENOMEM, "schedule of %zu bytes is smaller than the %zu required", schedule_bytes, L.bytes);
+    if (item_count == 0) return FVSR_OK;
+    s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // long ranges, and the fp32 lane: the per-item kernel (in the schedule's longest-first order when it has one)
+    const bool persistent = fvsr::sched_persistent(L, item_begin, d.nq);
+    if (!persistent || p->dtype != FVSR_BF16)
+        return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out, st,
+                             item_begin, item_count,
+                             persistent ? nullptr
+                                        : reinterpret_cast<const int32_t*>(static_cast<const uint8_t*>(schedule) +
+                                                                           L.off_order));
+    FVSR_CU(fvsr::launch_attn_bf16_persist(q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), d.heads, d.nq, d.nk,
+                                           kidx, L, schedule, out, st),
+            "persistent bf16 attention launch");
+    return FVSR_OK;
+}
+
 fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
                                      const float* block_mask, void* out, void* workspace, size_t workspace_bytes,
                                      fvsr_stream_t stream) {

@@ -403,8 +403,11 @@ cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st) {
     if (v) {
         const int zero = 0;
         e = cudaMemcpyToSymbol(g_fvsr_timeout, &zero, sizeof(int));
+        if (e != cudaSuccess) return e;
     }
-    *flag = v;
+    int vp = 0;
+    e = read_and_clear_persist_error(&vp);
+    *flag = v | vp;
     return e;
 }
 

@@ -73,10 +73,35 @@ cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, cons
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
                              int item_begin, int item_count, const int32_t* order, cudaStream_t st);
+// Work schedule of an item range (schedule.cu). A short range inside one head (at most kPersistItemsPerSm items per
+// SM) gets the persistent kernel's partition: the head's kept key blocks cut into G equal shares, CTA c walking its
+// share as segments (item, first list position, length, partial slot or −1); items cut by a share boundary are
+// merged, and empty items zero-filled, by launch_combine. Other ranges get the longest-first item order for the
+// per-item kernel. One buffer (sized for either) holds the one chosen.
+constexpr int kPersistItemsPerSm = 8;
+constexpr int kSchedItemCap = 4096;   // items of a persistent range (shared-memory prefix arrays)
+constexpr int kSchedHeadCap = 63;     // heads of a persistent range
+constexpr int kSchedPairCap = 16384;  // (CTA, head) pairs of a persistent range
+struct SchedLayout {
+    int G, item_count, Hr, max_segs, max_parts, max_comb;
+    bool persistent;
+    size_t off_hdr, off_order, off_seg_begin, off_segs, off_comb, off_empties, off_ml, off_opart, bytes;
+};
+SchedLayout sched_layout(int item_count, int nq, int heads, int G);
+bool sched_persistent(const SchedLayout& L, int item_begin, int nq);  // the mode a range gets
+cudaError_t launch_schedule(const int32_t* kcnt, int nk, int nq, int item_begin, int item_count,
+                            const SchedLayout& L, void* buf, cudaStream_t st);
+cudaError_t launch_combine(const SchedLayout& L, const void* buf, int heads, int nq, void* out, cudaStream_t st);
+// Persistent bf16 attention over a schedule (grid G), then the combine.
+cudaError_t launch_attn_bf16_persist(const void* q, const void* k, const void* v, int64_t kv_rows,
+                                     const KvPages& pages, int heads, int nq, int nk, const int32_t* kidx,
+                                     const SchedLayout& L, const void* sched, void* out, cudaStream_t st);
 // Longest-first order of the items [item_begin, item_begin + item_count) within each head (stable by item id).
 cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int item_count, int32_t* order,
                               cudaStream_t st);
-// Reads and clears the device-side timeout word of the current device (1 if a wait gave up since the last read).
+// Reads and clears the persistent kernel's timeout word of the current device.
+cudaError_t read_and_clear_persist_error(int* flag);
+// Reads and clears the device-side timeout words of the current device (1 if a wait gave up since the last read).
 cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st);
 
 }  // namespace fvsr

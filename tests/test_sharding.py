@@ -110,3 +110,117 @@ def test_range_attention_reproduces_one_gpu_items(fvsr):
             hl = h - sh.head_lo
             assert not out[qb * 128:(qb + 1) * 128, hl * 128:(hl + 1) * 128].any()
     fvsr.device_check()
+
+
+def _config5_rank(fvsr, world, rank, dtype=None):
+    """Config 5 as rank `rank` of `world` holds it: the heads its items touch, and its range in local items."""
+    cfgs = importlib.import_module("fvsr_b200.configs")
+    cfg = cfgs.CONFIGS[5]
+    g = cfg.geometry()
+    sh = fvsr.shard_items(g.heads, g.nq, world, rank)
+    one = fvsr.Geometry(**{**g.__dict__, "heads": 1})
+    per_head = [cfgs.synth_qkv(cfg, one, 900 + h) for h in range(sh.head_lo, sh.head_hi + 1)]
+    q, k, v = (torch.cat([ph[i] for ph in per_head], dim=1).contiguous() for i in range(3))
+    gl = fvsr.Geometry(**{**g.__dict__, "heads": sh.heads})
+    sel = fvsr.draft_block_mask_and_probs(q, k, gl, want_mask=False, want_probs=False)
+    if dtype == "f32":
+        q, k, v = q.float(), k.float(), v.float()
+        gl = fvsr.Geometry(**{**gl.__dict__, "dtype": 0})
+    lb, lc = sh.local_range(g.nq)
+    return gl, q, k, v, sel, lb, lc
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,rank", [(12, 0), (24, 1)])
+def test_schedule_gives_every_sm_an_equal_share(fvsr, world, rank):
+    """A range inside one head: the persistent partition (equal key-block shares, cut items merged)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    gl, q, k, v, sel, lb, lc = _config5_rank(fvsr, world, rank)
+    assert lb // gl.nq == (lb + lc - 1) // gl.nq
+    buf = fvsr.make_schedule(sel["kcnt"], gl, lb, lc)
+    hdr, seg_begin, segs, comb, empties = fvsr.schedule_view(buf, gl, lc)
+    kc = sel["kcnt"].view(-1).cpu().numpy()[lb:lb + lc].astype(np.int64)
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    assert hdr["heads"] == 1
+    assert sorted(empties.tolist()) == [lb + i for i in range(lc) if kc[i] == 0] and hdr["empty_items"] == len(empties)
+    assert seg_begin[0] == 0 and seg_begin[G] == hdr["segments"] and (np.diff(seg_begin) >= 0).all()
+    S = int(kc.sum())
+    Q = max(-(-S // G), 1)
+    per_sm = [int(segs[seg_begin[c]:seg_begin[c + 1], 2].sum()) for c in range(G)]
+    assert per_sm == [min(Q, max(0, S - c * Q)) for c in range(G)]
+    # every non-empty item's key list [0, cnt) is covered once; cut items have consecutive piece slots
+    by_item = {}
+    for it, b, n, slot in segs.tolist():
+        by_item.setdefault(it, []).append((b, n, slot))
+    assert sorted(by_item) == [lb + i for i in range(lc) if kc[i] > 0]
+    cut = {}
+    for it, parts in by_item.items():
+        parts.sort()
+        assert parts[0][0] == 0 and sum(n for _, n, _ in parts) == kc[it - lb]
+        assert all(parts[i][0] + parts[i][1] == parts[i + 1][0] for i in range(len(parts) - 1))
+        if len(parts) == 1:
+            assert parts[0][2] == -1
+        else:
+            slots = [sl for _, _, sl in parts]
+            assert slots == list(range(slots[0], slots[0] + len(parts)))
+            cut[it] = (slots[0], len(parts))
+    assert cut and {int(c[0]): (int(c[1]), int(c[2])) for c in comb} == cut
+    assert hdr["cut_items"] == len(cut) <= G - 1 and hdr["pieces"] == sum(n for _, n in cut.values())
+    fvsr.device_check()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,rank,dtype", [(12, 0, "bf16"), (24, 1, "bf16"), (8, 0, "bf16"), (12, 0, "f32")])
+def test_scheduled_attention_matches_range_attention(fvsr, orc, world, rank, dtype):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    gl, q, k, v, sel, lb, lc = _config5_rank(fvsr, world, rank, dtype)
+    ref_out = torch.zeros_like(q)
+    fvsr.block_sparse_attention_range(q, k, v, sel["kidx"], sel["kcnt"], gl, lb, lc, ref_out,
+                                      order=fvsr.item_order(sel["kcnt"], gl, lb, lc))
+    buf = fvsr.make_schedule(sel["kcnt"], gl, lb, lc)
+    out = torch.full_like(q, 7.0)                         # empty items must be overwritten with zeros
+    fvsr.block_sparse_attention_scheduled(q, k, v, sel["kidx"], sel["kcnt"], gl, lb, lc, out, buf)
+    torch.cuda.synchronize()
+    nq = gl.nq
+
+    def block(t, it):
+        h, qb = divmod(it, nq)
+        return t[qb * 128:(qb + 1) * 128, h * 128:(h + 1) * 128]
+
+    persistent = dtype == "bf16" and lb // nq == (lb + lc - 1) // nq
+    cut = set()
+    if persistent:
+        _, _, _, comb, _ = fvsr.schedule_view(buf, gl, lc)
+        cut = {int(c[0]) for c in comb}
+        assert cut
+    for it in range(lb, lb + lc):                         # whole items: the per-item kernel's exact arithmetic
+        if it not in cut:
+            assert torch.equal(block(out, it), block(ref_out, it)), it
+    if cut:                                               # cut items: merged pieces vs the fp32 oracle (bf16 bar)
+        items = np.array(sorted(cut)[:6], np.int32)
+        ref = orc.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                            sel["kidx"].cpu().numpy(), sel["kcnt"].cpu().numpy(), gl.heads, items=items)
+        for it in items:
+            h, qb = divmod(int(it), nq)
+            r = ref[qb * 128:(qb + 1) * 128, h * 128:(h + 1) * 128]
+            cmp = orc.compare(block(out, int(it)).float().cpu().numpy(), r)
+            assert cmp["rel"] <= 1e-2, (int(it), cmp)
+            cmp2 = orc.compare(block(out, int(it)).float().cpu().numpy(),
+                               block(ref_out, int(it)).float().cpu().numpy())
+            assert cmp2["rel"] <= 1e-2, (int(it), cmp2)
+    fvsr.device_check()
+
+
+def test_schedule_entry_points_validate(fvsr):
+    import ctypes
+    L = fvsr.lib()
+    g = fvsr.Geometry(heads=2, bh=4, bw=4, q_slices=1, kv_slices=3, local_range=5, topk=10, dtype=1)
+    p = g.params()
+    n = ctypes.c_size_t(0)
+    assert L.fvsr_lcsa_schedule_size(ctypes.byref(p), -1, ctypes.byref(n)) == fvsr.FVSR_EINVAL
+    assert L.fvsr_lcsa_schedule_size(ctypes.byref(p), 2 * g.nq + 1, ctypes.byref(n)) == fvsr.FVSR_EINVAL
+    assert L.fvsr_lcsa_schedule(ctypes.byref(p), None, 0, 4, None, 0, None) != fvsr.FVSR_OK
+    assert L.fvsr_lcsa_attention_scheduled(ctypes.byref(p), None, None, None, None, None, None, 5, -2, None, 0,
+                                           None) == fvsr.FVSR_EINVAL
