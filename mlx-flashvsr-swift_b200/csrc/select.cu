@@ -193,19 +193,26 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
     const int i0 = blockIdx.y * kTI, j0 = blockIdx.x * kTJ;
     const int64_t ld = (int64_t)heads * kD;
     const int tid = threadIdx.x;
-    for (int idx = tid; idx < kTI * 32; idx += 256) {
-        const int r = idx >> 5, e4 = idx & 31;
-        const int i = i0 + r;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < nq) v = __ldg(reinterpret_cast<const float4*>(pq + i * ld + h * kD) + e4);
-        *reinterpret_cast<float4*>(sq + r * kPS + e4 * 4) = v;
-    }
-    for (int idx = tid; idx < kTJ * 32; idx += 256) {
-        const int r = idx >> 5, e4 = idx & 31;
-        const int j = j0 + r;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < nk) v = __ldg(reinterpret_cast<const float4*>(pk + (int64_t)kv_phys_block(pages, j) * ld + h * kD) + e4);
-        *reinterpret_cast<float4*>(sk + r * kPS + e4 * 4) = v;
+    {  // stage the tile's pooled rows: all 16 loads of a thread in flight before the first store
+        constexpr int kPer = (kTI * 32) / 256;
+        static_assert(kTI == kTJ && (kTI * 32) % 256 == 0, "staging layout");
+        float4 vq[kPer], vk[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int idx = tid + 256 * k, r = idx >> 5, e4 = idx & 31;
+            const int i = i0 + r, j = j0 + r;
+            vq[k] = i < nq ? __ldg(reinterpret_cast<const float4*>(pq + i * ld + h * kD) + e4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            vk[k] = j < nk ? __ldg(reinterpret_cast<const float4*>(pk + (int64_t)kv_phys_block(pages, j) * ld + h * kD) +
+                                   e4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int idx = tid + 256 * k, r = idx >> 5, e4 = idx & 31;
+            *reinterpret_cast<float4*>(sq + r * kPS + e4 * 4) = vq[k];
+            *reinterpret_cast<float4*>(sk + r * kPS + e4 * 4) = vk[k];
+        }
     }
     __syncthreads();
     const int ty = tid >> 4, tx = tid & 15;
@@ -265,9 +272,11 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
 // Softmax over the key blocks of one (head, query block) row per warp, in place (scores → probs), plus the pass-1
 // histogram of each (head, query slice) row. A CTA's rows lie in at most two slices whenever Nq/q_slices ≥ 8; rows
 // of any further slice go straight to global atomics.
+// NCH > 0: the row (at most NCH·256 key blocks) stays in registers between the three passes; NCH = 0 re-reads it.
+template <int NCH>
 __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* __restrict__ probs, int nq, int nk,
-                                                                       int q_slices,
-                                                             int topk, uint32_t* __restrict__ hist) {
+                                                                       int q_slices, int topk,
+                                                                       uint32_t* __restrict__ hist) {
     griddep_wait_then_release();
     __shared__ uint32_t shist[2][kBins1];
     const int h = blockIdx.y;
@@ -280,34 +289,58 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
     const int i = i0 + warp;
     if (i < nq) {  // warp-uniform
         float* row = probs + ((int64_t)h * nq + i) * nk;
-        float m = -INFINITY;
-        for (int jb = 0; jb < nk; jb += 256) {
-            float v[8];
+        constexpr int kR = NCH > 0 ? NCH * 8 : 1;
+        float rv[kR];
+        if (NCH > 0) {  // all loads in flight at once
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int j = jb + 32 * u + lane;
-                v[u] = j < nk ? row[j] : -INFINITY;
+            for (int c = 0; c < kR; ++c) {
+                const int j = 256 * (c >> 3) + 32 * (c & 7) + lane;
+                rv[c] = j < nk ? row[j] : -INFINITY;
             }
+        }
+        float m = -INFINITY;
+        if (NCH > 0) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) m = fmaxf(m, v[u]);
+            for (int c = 0; c < kR; ++c) m = fmaxf(m, rv[c]);
+        } else {
+            for (int jb = 0; jb < nk; jb += 256) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int j = jb + 32 * u + lane;
+                    v[u] = j < nk ? row[j] : -INFINITY;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) m = fmaxf(m, v[u]);
+            }
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float part = 0.0f;
-        for (int jb = 0; jb < nk; jb += 256) {
-            float v[8];
+        if (NCH > 0) {  // same order as below: j ≡ lane (mod 32), increasing j
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int j = jb + 32 * u + lane;
-                v[u] = j < nk ? row[j] : -INFINITY;
+            for (int c = 0; c < kR; ++c) {
+                const int j = 256 * (c >> 3) + 32 * (c & 7) + lane;
+                const float e = fvsr_exp(__fsub_rn(rv[c], m));
+                rv[c] = j < nk ? e : 0.0f;
+                if (j < nk) part = __fadd_rn(part, e);
             }
+        } else {
+            for (int jb = 0; jb < nk; jb += 256) {
+                float v[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int j = jb + 32 * u + lane;
-                const float e = fvsr_exp(__fsub_rn(v[u], m));
-                if (j < nk) {
-                    row[j] = e;
-                    part = __fadd_rn(part, e);
+                for (int u = 0; u < 8; ++u) {
+                    const int j = jb + 32 * u + lane;
+                    v[u] = j < nk ? row[j] : -INFINITY;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int j = jb + 32 * u + lane;
+                    const float e = fvsr_exp(__fsub_rn(v[u], m));
+                    if (j < nk) {
+                        row[j] = e;
+                        part = __fadd_rn(part, e);
+                    }
                 }
             }
         }
@@ -315,23 +348,28 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
         for (int o = 16; o >= 1; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
         const int sl = i / nqs, local = sl - slice0;
         uint32_t* gh = hist + (int64_t)(h * q_slices + sl) * kHistPerRow;
-        for (int jb = 0; jb < nk; jb += 256) {
-            float v[8];
+        auto emit = [&](int j, float v) {
+            const float p = v == 0.0f ? 0.0f : __fdiv_rn(v, part);  // 0 / sum = +0 exactly
+            if (j < nk) row[j] = p;
+            const uint32_t bin = __float_as_uint(p) >> 21;
+            if (local < 2)
+                hist_add(&shist[local][0], bin, j < nk);
+            else if (j < nk)
+                atomicAdd(gh + bin, 1u);
+        };
+        if (NCH > 0) {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int j = jb + 32 * u + lane;
-                v[u] = j < nk ? row[j] : 0.0f;
-            }
+            for (int c = 0; c < kR; ++c) emit(256 * (c >> 3) + 32 * (c & 7) + lane, rv[c]);
+        } else {
+            for (int jb = 0; jb < nk; jb += 256) {
+                float v[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int j = jb + 32 * u + lane;
-                const float p = v[u] == 0.0f ? 0.0f : __fdiv_rn(v[u], part);  // 0 / sum = +0 exactly
-                if (j < nk) row[j] = p;
-                const uint32_t bin = __float_as_uint(p) >> 21;
-                if (local < 2)
-                    hist_add(&shist[local][0], bin, j < nk);
-                else if (j < nk)
-                    atomicAdd(gh + bin, 1u);
+                for (int u = 0; u < 8; ++u) {
+                    const int j = jb + 32 * u + lane;
+                    v[u] = j < nk ? row[j] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) emit(jb + 32 * u + lane, v[u]);
             }
         }
     }
@@ -463,7 +501,14 @@ cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages
                    local_range, sqrt_d, probs);
     if (e != cudaSuccess) return e;
     dim3 sgrid((nq + kSoftRows - 1) / kSoftRows, heads);
-    return launch_pdl(select_softmax_kernel, sgrid, dim3(kSoftRows * 32), 0, st, probs, nq, nk, q_slices, topk, hist);
+    auto soft = [&](auto kernel) {
+        return launch_pdl(kernel, sgrid, dim3(kSoftRows * 32), 0, st, probs, nq, nk, q_slices, topk, hist);
+    };
+    if (nk <= 256) return soft(select_softmax_kernel<1>);
+    if (nk <= 512) return soft(select_softmax_kernel<2>);
+    if (nk <= 768) return soft(select_softmax_kernel<3>);
+    if (nk <= 1024) return soft(select_softmax_kernel<4>);
+    return soft(select_softmax_kernel<0>);
 }
 
 cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
