@@ -228,6 +228,8 @@ def run_ours(args):
 
     order = torch.empty(max(item_count, 1), dtype=torch.int32, device=dev)
     use_split = shard and not args.no_split
+    persistent = use_split and pkg.schedule_is_persistent(
+        g_loc, item_begin, item_count, torch.cuda.get_device_properties(dev).multi_processor_count)
     sched = torch.empty(pkg.schedule_size(g_loc, item_count) if use_split else 1, dtype=torch.uint8, device=dev)
 
     def attention_call(q, k, v, out):
@@ -387,7 +389,8 @@ def run_ours(args):
                        "parallelism": (f"{world} GPUs, (head, query block) items sharded, no collective" if shard
                                        else (f"{world} independent streams" if world > 1 else "1 GPU")),
                        **({"emulated_rank": args.as_rank} if shard and args.as_rank else {}),
-                       **({"schedule": "split key lists" if use_split else "longest-first items"} if shard else {})},
+                       **({"schedule": "persistent equal shares" if persistent else "longest-first items"}
+                          if shard else {})},
             "ms_per_layer": ms / layers,
             "breakdown_ms_per_layer": {"attention": att_avg, "pool+select": sel_ms},
             "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
@@ -395,8 +398,9 @@ def run_ours(args):
                          "traffic": (tr or {}).get("bytes_per_launch"),
                          "traffic_source": (tr or {}).get("source")},
             "clocks": clk,
-            # per layer: pool, scores, softmax, 2 histogram passes, finish, order (or schedule), attention (+ combine)
-            "gpu_launches": (9 if use_split else 8) * layers * args.steps,
+            # per layer: pool, scores, softmax, 2 histogram passes, finish, order (or schedule), attention, and the
+            # combine step when the range runs the persistent kernel
+            "gpu_launches": (9 if persistent else 8) * layers * args.steps,
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:

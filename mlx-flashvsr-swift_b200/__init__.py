@@ -286,6 +286,16 @@ def schedule_size(geom: Geometry, item_count: int) -> int:
     return n.value
 
 
+def schedule_is_persistent(geom: Geometry, item_begin: int, item_count: int, sms: int) -> bool:
+    """Whether make_schedule gives the range the persistent partition (the C library's rule: a bf16 range inside one
+    head with at most 8 items per SM); otherwise it gets the longest-first order of the per-item kernel."""
+    if item_count <= 0 or geom.dtype != FVSR_BF16:
+        return False
+    hr = min(geom.heads, (item_count - 1) // geom.nq + 2)
+    room = item_count <= 8 * sms and item_count <= 4096 and hr <= 63 and sms * hr <= 16384
+    return room and item_begin // geom.nq == (item_begin + item_count - 1) // geom.nq
+
+
 def make_schedule(kcnt, geom: Geometry, item_begin: int, item_count: int, buf=None, stream=None):
     """Work schedule of the items [item_begin, item_begin + item_count): for a short range (at most 8 items per SM)
     the persistent kernel's partition — per head, the head's kept key blocks in equal shares per SM, cut items merged

@@ -189,7 +189,9 @@ def test_scheduled_attention_matches_range_attention(fvsr, orc, world, rank, dty
         h, qb = divmod(it, nq)
         return t[qb * 128:(qb + 1) * 128, h * 128:(h + 1) * 128]
 
-    persistent = dtype == "bf16" and lb // nq == (lb + lc - 1) // nq
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    persistent = fvsr.schedule_is_persistent(gl, lb, lc, G)
+    assert persistent == (dtype == "bf16" and lb // nq == (lb + lc - 1) // nq)
     cut = set()
     if persistent:
         _, _, _, comb, _ = fvsr.schedule_view(buf, gl, lc)
