@@ -3,7 +3,9 @@
 //
 // HBM-bound: algorithmic bytes = nblocks·128·C·elt read (+ the same written when copying) + nblocks·C·4 written.
 // Layout: one CTA covers one 128-token block × 512 channels; 4 token groups × 64 channel lanes, 8 channels per lane
-// (one 128-bit load per token for bf16), so a warp reads 512 contiguous bytes of a token row per load.
+// (one 128-bit load per token for bf16), so a warp reads 512 contiguous bytes of a token row per load. With at most
+// 256 channels (the one or two heads of a sharded rank) the 64 lanes are split into bpc = 64 / lanes groups that
+// pool bpc consecutive blocks at once, each block with exactly the arithmetic of the one-block layout.
 #include "common.cuh"
 
 namespace fvsr {
@@ -19,7 +21,7 @@ template <int DT>
 __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, int channels, float* __restrict__ out,
                                                    void* __restrict__ copy_dst, int n1, const void* __restrict__ x2,
                                                    float* __restrict__ out2, uint32_t* __restrict__ zero,
-                                                   size_t zero_words) {
+                                                   size_t zero_words, int lanes, int nblocks) {
     __shared__ float part[4][kPoolChannels];
     griddep_wait_then_release();
     if (zero) {
@@ -28,8 +30,10 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
     }
     const int lane = threadIdx.x & (kPoolLanes - 1);
     const int g = threadIdx.x / kPoolLanes;  // token group: tokens [32g, 32g + 32)
-    const int c0 = blockIdx.x * kPoolChannels + lane * 8;
-    int64_t b = blockIdx.y;
+    const int sub = lane / lanes, cl = lane % lanes;  // block within the CTA, channel lane within the block
+    const int c0 = blockIdx.x * kPoolChannels + cl * 8;
+    int64_t b = (int64_t)blockIdx.y * (kPoolLanes / lanes) + sub;
+    const bool live = b < nblocks;
     if (b >= n1) {
         b -= n1;
         x = x2;
@@ -39,7 +43,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    if (c0 < channels) {
+    if (live && c0 < channels) {
         // 8 tokens per batch: all 8 loads are issued before their sums (which stay in token order)
         for (int t0 = 32 * g; t0 < 32 * g + 32; t0 += 8) {
             if (DT == 1) {
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
 #pragma unroll
     for (int i = 0; i < 8; ++i) part[g][lane * 8 + i] = acc[i];
     __syncthreads();
-    if (g == 0 && c0 < channels) {
+    if (g == 0 && live && c0 < channels) {
         float r[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -112,12 +116,17 @@ cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels,
 cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,
                          float* out2, int dtype, int channels, cudaStream_t st, uint32_t* zero, size_t zero_words) {
     if (n1 + n2 == 0) return cudaSuccess;
-    dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)(n1 + n2));
+    // channel lanes one block needs (a power of two ≤ 64); the rest of the 64 pool further blocks
+    int lanes = 1;
+    while (lanes < kPoolLanes && lanes * 8 < channels) lanes <<= 1;
+    const int bpc = kPoolLanes / lanes;
+    const int64_t nb = n1 + n2;
+    dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)((nb + bpc - 1) / bpc));
     if (dtype == 1)
         return launch_pdl(pool_kernel<1>, grid, dim3(256), 0, st, x1, channels, out1, copy_dst, (int)n1, x2, out2, zero,
-                          zero_words);
+                          zero_words, lanes, (int)nb);
     return launch_pdl(pool_kernel<0>, grid, dim3(256), 0, st, x1, channels, out1, copy_dst, (int)n1, x2, out2, zero,
-                      zero_words);
+                      zero_words, lanes, (int)nb);
 }
 
 }  // namespace fvsr

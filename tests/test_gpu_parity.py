@@ -51,11 +51,13 @@ def gather_rows(x, items, nq):
 # ------------------------------------------------------------------------------------------------------------------
 # pooling
 # ------------------------------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("dtype", ["bf16", "f32"])
-def test_pool_bit_exact(fvsr, orc, cfgs, dtype):
-    g = fvsr.Geometry(heads=12, bh=1, bw=1, q_slices=1, kv_slices=1, dtype=fvsr.FVSR_BF16 if dtype == "bf16" else fvsr.FVSR_F32)
+@pytest.mark.parametrize("dtype,heads", [("bf16", 12), ("f32", 12), ("bf16", 2), ("bf16", 1), ("f32", 2), ("bf16", 5)])
+def test_pool_bit_exact(fvsr, orc, cfgs, dtype, heads):
+    """12 heads: 512-channel CTAs; 1, 2 heads: several blocks per CTA (a sharded rank's Q/K); 5: a partial CTA."""
+    g = fvsr.Geometry(heads=heads, bh=1, bw=1, q_slices=1, kv_slices=1,
+                      dtype=fvsr.FVSR_BF16 if dtype == "bf16" else fvsr.FVSR_F32)
     gen = torch.Generator(device="cuda").manual_seed(7)
-    x = torch.randn((37 * 128, 12 * 128), generator=gen, device="cuda")
+    x = torch.randn((37 * 128, heads * 128), generator=gen, device="cuda")
     if dtype == "bf16":
         x = x.to(torch.bfloat16)
     got = fvsr.pool(x, g).cpu().numpy()
