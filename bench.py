@@ -176,16 +176,14 @@ def run_reference(args):
 # ---------------------------------------------------------------------------------------------------------------
 def run_ours(args):
     import torch
-    import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     pkg, cfgs = load_pkg()
+    import importlib
+    ranks = importlib.import_module("fvsr_b200.ranks")
+    info = ranks.rank_info()
+    world, rank, local = info.world, info.rank, info.local
+    torch.cuda.set_device(local)
+    ranks.init(info, "nccl", timeout_s=120, device=torch.device("cuda", local))
     cfg = cfgs.CONFIGS[args.config]
     g = cfg.geometry()
     layers = args.layers
@@ -270,10 +268,7 @@ def run_ours(args):
         kept.append(int(kcnt.view(-1)[item_begin:item_begin + item_count].sum().item()))
     flops_per_step = 4.0 * 128 ** 3 * sum(kept)
     total_kept = sum(kept)
-    if world > 1:
-        t = torch.tensor([float(total_kept)], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        total_kept = int(t.item())
+    total_kept = int(round(ranks.sum_over_ranks(total_kept, dev)))
     flops_all_ranks = 4.0 * 128 ** 3 * total_kept
 
     for _ in range(args.warmup):
@@ -289,8 +284,7 @@ def run_ours(args):
         graph.replay()
         torch.cuda.synchronize()
         run_step = graph.replay
-    if world > 1:
-        dist.barrier()
+    ranks.barrier()
     uuid = None
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
@@ -306,11 +300,7 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = ranks.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     pkg.device_check()
 
     # dominant kernel: the bf16 attention alone, CUDA events on the launching stream, over all layers
@@ -401,8 +391,7 @@ def run_ours(args):
             e2e_step(t)
             torch.cuda.synchronize()
             kept_phase.append(int(kcnt_f.sum().item()))
-        if world > 1:
-            dist.barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
@@ -413,12 +402,8 @@ def run_ours(args):
         pkg.device_check()
         e2e_ms = f0.elapsed_time(f1) / args.e2e_steps
         e2e_flops = 4.0 * 128 ** 3 * sum(kept_phase[t % nrot] for t in range(args.e2e_steps)) / args.e2e_steps
-        if world > 1:
-            tt = torch.tensor([e2e_ms, e2e_flops], device=dev, dtype=torch.float64)
-            mx = tt.clone()
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            dist.all_reduce(tt, op=dist.ReduceOp.SUM)
-            e2e_ms, e2e_flops = float(mx[0].item()), float(tt[1].item())
+        e2e_ms = ranks.max_over_ranks(e2e_ms, dev)
+        e2e_flops = ranks.sum_over_ranks(e2e_flops, dev)
         for c in caches:
             c.close()
         e2e = {"value": e2e_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
@@ -452,8 +437,7 @@ def run_ours(args):
             torch.cuda.current_stream().synchronize()
 
         e2e_step()
-        if world > 1:
-            dist.barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
@@ -461,11 +445,7 @@ def run_ours(args):
             e2e_step()
         f1.record(stream)
         torch.cuda.synchronize()
-        e2e_ms = f0.elapsed_time(f1) / args.e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+        e2e_ms = ranks.max_over_ranks(f0.elapsed_time(f1) / args.e2e_steps, dev)
         e2e = {"value": flops_all_ranks / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "kind": e2e_kind}
 
@@ -507,9 +487,8 @@ def run_ours(args):
             except Exception as exc:  # the baseline is reported, never required
                 line["cpu_baseline"] = {"error": str(exc)}
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.barrier()
+    ranks.shutdown()
 
 
 def main():
