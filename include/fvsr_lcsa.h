@@ -114,9 +114,10 @@ fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const 
 
 /* Work items are the (head, query block) pairs, item = h·Nq + qb (head-major). */
 
-/* Longest-first schedule of the items [item_begin, item_begin + item_count): order receives the item ids sorted by
- * decreasing kcnt within each head (ties by id), heads kept in order, so long items start first and short ones fill
- * the tail of the launch. order has item_count entries. No reference counterpart (scheduling only). */
+/* Longest-first schedule of the items [item_begin, item_begin + item_count): order receives the non-empty item ids
+ * (kcnt > 0) sorted by decreasing kcnt within each head (ties by id), heads kept in order, then the empty items of the
+ * range by id — so long items start first, short ones fill the tail of the launch, and the items that only write
+ * zeros come last. order has item_count entries. No reference counterpart (scheduling only). */
 fvsr_status fvsr_lcsa_item_order(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin,
                                  int32_t item_count, int32_t* order, fvsr_stream_t stream);
 

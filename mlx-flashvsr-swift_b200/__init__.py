@@ -256,7 +256,8 @@ def block_sparse_attention(q, k, v, kidx, kcnt, geom: Geometry, out=None, stream
 
 
 def item_order(kcnt, geom: Geometry, item_begin: int, item_count: int, order=None, stream=None):
-    """Longest-first order of the items [item_begin, item_begin + item_count) within each head."""
+    """Longest-first order of the items [item_begin, item_begin + item_count): the non-empty items of each head in
+    turn by decreasing kcnt (ties by id), then the range's empty items by id."""
     torch = _torch()
     if order is None:
         order = torch.empty(item_count, dtype=torch.int32, device=kcnt.device)

@@ -96,7 +96,8 @@ cudaError_t launch_combine(const SchedLayout& L, const void* buf, int heads, int
 cudaError_t launch_attn_bf16_persist(const void* q, const void* k, const void* v, int64_t kv_rows,
                                      const KvPages& pages, int heads, int nq, int nk, const int32_t* kidx,
                                      const SchedLayout& L, const void* sched, void* out, cudaStream_t st);
-// Longest-first order of the items [item_begin, item_begin + item_count) within each head (stable by item id).
+// Longest-first order of the items [item_begin, item_begin + item_count): the non-empty items of each head in turn
+// by decreasing kcnt (stable by item id), then all empty items of the range by id.
 cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int item_count, int32_t* order,
                               cudaStream_t st);
 // Reads and clears the persistent kernel's timeout word of the current device.

@@ -539,21 +539,57 @@ namespace fvsr {
 
 namespace {
 
-// One CTA per head segment of the range: rank of each item = items of the segment with a longer key list, or an
-// equal one and a smaller id; the item goes to that position inside its segment (segments keep head-major order).
+// One CTA per head segment of the range. The order is: the non-empty items of each head segment in turn (segments in
+// head order), longest key list first within a segment (ties by id); then every empty item of the range, ascending.
+// Empty items only write zeros, so they go last: placed between heads they would delay the next head's long items.
+// Rank of a non-empty item inside its segment = items of the segment with a longer key list, or an equal one and a
+// smaller id; empty items rank after all non-empty ones, by id.
 __global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restrict__ kcnt, int nq, int item_begin,
                                                          int item_count, int32_t* __restrict__ order) {
     griddep_wait_then_release();
     __shared__ int32_t sc[4096];
+    __shared__ int cnt[4];  // non-empty before this segment, empty before it, non-empty in the range, in the segment
     const int h = item_begin / nq + blockIdx.x;
     const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
     const int n = s1 - s0;
     if (n <= 0) return;
-    if (n > 4096) {  // no room to rank: keep ascending order
-        for (int i = threadIdx.x; i < n; i += blockDim.x) order[s0 - item_begin + i] = s0 + i;
+    if (threadIdx.x < 4) cnt[threadIdx.x] = 0;
+    __syncthreads();
+    {
+        int a = 0, b = 0, c = 0, d = 0;
+        for (int i = threadIdx.x; i < item_count; i += blockDim.x) {
+            const int it = item_begin + i;
+            const bool nz = kcnt[it] > 0;
+            c += nz;
+            if (it < s0) {
+                a += nz;
+                b += !nz;
+            } else if (it < s1) {
+                d += nz;
+            }
+        }
+        atomicAdd(&cnt[0], a);
+        atomicAdd(&cnt[1], b);
+        atomicAdd(&cnt[2], c);
+        atomicAdd(&cnt[3], d);
+    }
+    __syncthreads();
+    const int ne_before = cnt[0], e_before = cnt[1], ne_total = cnt[2], ne_seg = cnt[3];
+    auto place = [&](int i, int rank, bool nz) {  // rank: position inside the segment, non-empty items first
+        const int pos = nz ? ne_before + rank : ne_total + e_before + (rank - ne_seg);
+        order[pos] = s0 + i;
+    };
+    if (n > 4096) {  // no room to rank: each class in ascending id order
+        if (threadIdx.x == 0) {
+            int a = 0, b = 0;
+            for (int i = 0; i < n; ++i) {
+                const bool nz = kcnt[s0 + i] > 0;
+                place(i, nz ? a++ : ne_seg + b++, nz);
+            }
+        }
         return;
     }
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = kcnt[s0 + i];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = max(kcnt[s0 + i], 0);
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int ci = sc[i];
@@ -562,7 +598,7 @@ __global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restri
             const int ct = sc[t];
             rank += (ct > ci) || (ct == ci && t < i);
         }
-        order[s0 - item_begin + rank] = s0 + i;
+        place(i, rank, ci > 0);
     }
 }
 

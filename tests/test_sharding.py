@@ -95,6 +95,12 @@ def test_range_attention_reproduces_one_gpu_items(fvsr):
             for hseg in range(sh.heads):   # longest first within each head segment, heads in order
                 seg = [x for x in o if x // g.nq == hseg]
                 assert all(kc[a] >= kc[b] for a, b in zip(seg, seg[1:]))
+            nz = [kc[x] > 0 for x in o]     # every empty item after every non-empty one, empties by id
+            assert nz == sorted(nz, reverse=True)
+            empties = [x for x in o if kc[x] <= 0]
+            assert empties == sorted(empties)
+            heads_nz = [x // g.nq for x in o if kc[x] > 0]
+            assert heads_nz == sorted(heads_nz)
         fvsr.block_sparse_attention_range(ql, kl, vl, sl["kidx"], sl["kcnt"], gl, lb, lc, out, order=order)
         torch.cuda.synchronize()
         for it in range(sh.begin, sh.end):
