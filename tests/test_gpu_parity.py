@@ -115,6 +115,36 @@ def test_select_topk_edge_cases(fvsr, orc, cfgs):
         assert np.array_equal(r["kcnt"].cpu().numpy(), kcnt)
 
 
+@pytest.mark.parametrize("kv_slices", [12, 32], ids=["nk960", "nk2560_max"])
+def test_long_key_rows_select_and_attend(fvsr, orc, cfgs, kv_slices):
+    """Key rows longer than any config's: 960 key blocks (the softmax's four-chunk register path) and the supported
+    maximum of 2560 (its streaming path) — selection bit-exact, bf16 attention on sampled items within the bf16 bar;
+    one more slice is refused before any launch."""
+    g = fvsr.Geometry(heads=2, bh=8, bw=10, q_slices=1, kv_slices=kv_slices, local_range=11, topk=0,
+                      dtype=fvsr.FVSR_BF16)
+    g.topk = int(0.25 * g.allowed_per_row())
+    gen = torch.Generator(device="cuda").manual_seed(100 + kv_slices)
+    q = torch.randn((g.nq * 128, g.channels), generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.randn((g.nk * 128, g.channels), generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn((g.nk * 128, g.channels), generator=gen, device="cuda").to(torch.bfloat16)
+    r = fvsr.draft_block_mask_and_probs(q, k, g)
+    out = fvsr.block_sparse_attention(q, k, v, r["kidx"], r["kcnt"], g)
+    torch.cuda.synchronize()
+    loc = orc.local_block_mask(g.bh, g.bw, g.local_range)
+    probs, mask, kidx, kcnt = orc.draft_block_mask_and_probs(npf(q), npf(k), g.heads, 1, g.s, loc, g.topk)
+    assert np.array_equal(r["probs"].cpu().numpy().view(np.uint32), probs.view(np.uint32))
+    assert np.array_equal(r["kidx"].cpu().numpy(), kidx) and np.array_equal(r["kcnt"].cpu().numpy(), kcnt)
+    items = sample_items(g.heads, g.nq, 8, kv_slices)
+    ref = orc.attention(npf(q), npf(k), npf(v), kidx, kcnt, g.heads, items=items)
+    cmp = orc.compare(gather_rows(npf(out), items, g.nq), gather_rows(ref, items, g.nq))
+    assert cmp["rel"] <= REL_BF16, cmp
+    import ctypes
+    over = fvsr.Geometry(**{**g.__dict__, "kv_slices": 2560 // g.s + 1})
+    n = ctypes.c_size_t(0)
+    assert fvsr.lib().fvsr_lcsa_workspace_size(ctypes.byref(over.params()), ctypes.byref(n)) == fvsr.FVSR_EUNSUPPORTED
+    fvsr.device_check()
+
+
 # ------------------------------------------------------------------------------------------------------------------
 # attention against the reference's own oracle outputs (golden fixtures, Diag.swift:86-98 recipe)
 # ------------------------------------------------------------------------------------------------------------------
