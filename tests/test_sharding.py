@@ -232,3 +232,27 @@ def test_schedule_entry_points_validate(fvsr):
     assert L.fvsr_lcsa_schedule(ctypes.byref(p), None, 0, 4, None, 0, None) != fvsr.FVSR_OK
     assert L.fvsr_lcsa_attention_scheduled(ctypes.byref(p), None, None, None, None, None, None, 5, -2, None, 0,
                                            None) == fvsr.FVSR_EINVAL
+
+
+@pytest.mark.gpu
+def test_scheduled_attention_with_every_item_empty(fvsr):
+    """topk = 0 keeps nothing: the persistent partition has no work, and every item of the range is written as
+    zeros by the combine step (SparseAttention.swift:47-53)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    gl, q, k, v, _, lb, lc = _config5_rank(fvsr, 12, 0)
+    g0 = fvsr.Geometry(**{**gl.__dict__, "topk": 0})
+    sel = fvsr.draft_block_mask_and_probs(q, k, g0, want_mask=False, want_probs=False)
+    assert int(sel["kcnt"].sum()) == 0
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    assert fvsr.schedule_is_persistent(g0, lb, lc, G)
+    buf = fvsr.make_schedule(sel["kcnt"], g0, lb, lc)
+    out = torch.full_like(q, 7.0)
+    fvsr.block_sparse_attention_scheduled(q, k, v, sel["kidx"], sel["kcnt"], g0, lb, lc, out, buf)
+    torch.cuda.synchronize()
+    hdr, seg_begin, segs, comb, empties = fvsr.schedule_view(buf, g0, lc)
+    assert hdr["segments"] == 0 and hdr["cut_items"] == 0 and hdr["empty_items"] == lc
+    for it in range(lb, lb + lc):
+        h, qb = divmod(it, g0.nq)
+        assert not out[qb * 128:(qb + 1) * 128, h * 128:(h + 1) * 128].any(), it
+    fvsr.device_check()
