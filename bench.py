@@ -59,49 +59,61 @@ def profiled_traffic():
 # clocks sampler (nvidia-smi during the timed region)
 # ---------------------------------------------------------------------------------------------------------------
 class Clocks:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """nvidia-smi samples (every 50 ms) of SM clock and throttle reasons; only the samples taken inside the timed
+    region count. The sampler is started, and its first sample awaited, before the region begins."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_uuid: str | None):
         self.proc = None
         self.uuid = device_uuid
+        self.first = ""
+        self.window = None
 
     def start(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
         if self.uuid:
             cmd += ["-i", self.uuid]
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import select
+            if select.select([self.proc.stdout], [], [], 5.0)[0]:  # running once it has printed a line
+                self.first = self.proc.stdout.readline()
         except Exception:
             self.proc = None
+
+    def mark(self, t0: float, t1: float):
+        self.window = (t0, t1)
 
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.06)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except Exception:
             self.proc.kill()
             out = ""
-        sms, maxs, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        import datetime
+        rows = []
+        for line in (self.first + out).strip().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sms.append(float(f[1]))
-                maxs.append(float(f[2]))
+                t = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((t, float(f[2]), float(f[3]), f[6:10]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxs) if maxs else None,
-                "reasons": sorted(reasons), "samples": len(sms)}
+        inside = [r for r in rows if self.window and self.window[0] <= r[0] <= self.window[1]]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {n for r in inside for n, v in zip(names, r[3]) if v.lower().startswith("active")}
+        sms = [r[1] for r in inside]
+        return {"sm_mhz": statistics.median(sms) if sms else None,
+                "sm_max_mhz": max(r[2] for r in rows) if rows else None, "reasons": sorted(reasons),
+                "samples": len(sms), "sample_interval_ms": 50}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -294,11 +306,13 @@ def run_ours(args):
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    t_begin = time.time()
     e0.record(stream)
     for _ in range(args.steps):
         run_step()
     e1.record(stream)
     torch.cuda.synchronize()
+    clocks.mark(t_begin, time.time())
     clk = clocks.stop()
     ms = ranks.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
     pkg.device_check()
