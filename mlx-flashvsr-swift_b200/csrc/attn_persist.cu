@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             };
             bool ok = issue_s(0) && (total < 2 || issue_s(1));
             // S_{j+2} lands in the buffer of P_{j−1}: PV_{j−1} was issued first, and one thread's MMAs run in order
-            for (int j = 0; ok && j < total; ++j) ok = (j + 2 >= total || issue_s(j + 2)) && issue_pv(j);
+            for (int j = 0; ok && j < total; ++j) ok = issue_pv(j) && (j + 2 >= total || issue_s(j + 2));
         }
     } else {
         // ------------- softmax sets + per-segment epilogue -------------
