@@ -505,6 +505,77 @@ def run_ours(args):
     ranks.shutdown()
 
 
+def run_kv_append(args):
+    """The window cache's in-place append (fvsr_kv_cache_append + trim, DiT.swift:507-511, 532-538) as HBM traffic:
+    per chunk the chunk's q_slices new slices of K and V are read and written into their cache pages and the K slices
+    are pooled. Prints one JSON line: achieved GB/s of those algorithmic bytes against the measured copy bandwidth."""
+    import torch
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[args.config]
+    g = cfg.geometry()
+    kv_len = g.kv_slices - g.q_slices
+    rows = g.q_slices * g.s * 128
+    elt = 2 if cfg.dtype == "bf16" else 4
+    # enough distinct source chunks that successive appends read more than the 126 MB L2 holds
+    nbuf = max(2, -(-3 * 126_000_000 // (2 * rows * g.channels * elt)))
+    srcs = [cfgs.synth_qkv(cfg, g, 777 + i, kv_rows=rows)[1:] for i in range(nbuf)]
+    cache = pkg.KVCache(g, kv_len, g.q_slices)
+    while cache.slices < kv_len:
+        cache.append(srcs[0][0][: g.s * 128], srcs[0][1][: g.s * 128], 1)
+    # K and V new rows read once and written once; the pooled K vectors (fp32, one per block and head) written once.
+    bytes_per = 2 * 2 * rows * g.channels * elt + g.q_slices * g.s * g.channels * 4
+    n = max(args.steps, 1) * 20
+    it = [0]
+
+    def one():
+        k, v = srcs[it[0] % nbuf]
+        it[0] += 1
+        cache.append(k, v, g.q_slices)
+        cache.trim()
+
+    for _ in range(max(args.warmup, 3)):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # host-launched: one C-ABI append + trim per chunk, as a caller issues them
+    e0.record()
+    for _ in range(n):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    eager_us = e0.elapsed_time(e1) * 1e3 / n
+    # device rate: the same n appends captured once in a CUDA graph (pages chosen at capture) and replayed
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(n):
+            one()
+    reps = 5
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    pkg.device_check()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n)
+    del graph
+    _, hbm, kind = peaks()
+    gbs = bytes_per / (us * 1e-6) / 1e9
+    cache.close()
+    print(json.dumps({"metric": f"KV-cache append GB/s, config {args.config} chunk", "value": gbs, "unit": "GB/s",
+                      "us_per_chunk": us, "bytes_per_chunk": bytes_per, "chunks": reps * n, "gpu_launches": reps * n,
+                      "launch": "CUDA graph of the appends",
+                      "eager": {"us_per_chunk": eager_us, "value": bytes_per / (eager_us * 1e-6) / 1e9,
+                                "note": "one host call of fvsr_kv_cache_append + trim per chunk (host-paced)"},
+                      "l2": f"{nbuf} source chunks rotated ({nbuf * 2 * rows * g.channels * elt / 1e6:.0f} MB > L2)",
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                                   "peak_kind": kind},
+                      "config": {"workload": f"config {args.config}: {cfg.name}", "new_slices": g.q_slices,
+                                 "slice_blocks": g.s, "heads": g.heads, "dtype": cfg.dtype}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -524,7 +595,12 @@ def main():
                     help="split the config's (head, query block) items across the ranks (default for config 5)")
     ap.add_argument("--replicas", dest="shard", action="store_false",
                     help="one independent copy of the config per rank (default except for config 5)")
+    ap.add_argument("--kv-append", action="store_true",
+                    help="measure the window cache's in-place append (HBM GB/s) instead of the layer step")
     args = ap.parse_args()
+    if args.kv_append:
+        run_kv_append(args)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":

@@ -172,8 +172,8 @@ fvsr_status fvsr_kv_cache_destroy(fvsr_kv_cache* cache);
 fvsr_status fvsr_kv_cache_reset(fvsr_kv_cache* cache);
 /* Number of slices currently held. */
 fvsr_status fvsr_kv_cache_slices(const fvsr_kv_cache* cache, int32_t* slices);
-/* Append new_slices slices of keys/values (new_slices·s·128, H·128) in p->dtype: copies them into free pages and
- * pools the keys (the concat of DiT.swift:508-511). */
+/* Append new_slices slices of keys/values (new_slices·s·128, H·128) in p->dtype: one kernel launch on `stream` copies
+ * them into free pages and pools the keys (the concat of DiT.swift:508-511). */
 fvsr_status fvsr_kv_cache_append(fvsr_kv_cache* cache, const void* k_new, const void* v_new, int32_t new_slices,
                                  fvsr_stream_t stream);
 /* DiT.swift:532-538: if more than kv_len slices are held, drop the oldest one. Host-side only. */

@@ -457,23 +457,24 @@ fvsr_status fvsr_kv_cache_append(fvsr_kv_cache* c, const void* k_new, const void
     if (new_slices < 1 || (int)c->pages.size() + new_slices > c->capacity)
         return fail(FVSR_EINVAL, "appending %d slices to %zu exceeds the capacity %d", new_slices, c->pages.size(), c->capacity);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // lowest free arena page for each new slice, then one launch copies keys and values and pools the keys
+    KvPages dst{};
+    dst.s = c->d.s;
+    std::vector<int32_t> pages = c->pages;
     for (int t = 0; t < new_slices; ++t) {
         int page = -1;
         for (int cand = 0; cand < c->capacity && page < 0; ++cand) {
             bool used = false;
-            for (int32_t u : c->pages) used |= (u == cand);
+            for (int32_t u : pages) used |= (u == cand);
             if (!used) page = cand;
         }
-        const int64_t src_off = (int64_t)t * c->page_bytes();
-        uint8_t* kd = static_cast<uint8_t*>(c->k_arena) + (int64_t)page * c->page_bytes();
-        uint8_t* vd = static_cast<uint8_t*>(c->v_arena) + (int64_t)page * c->page_bytes();
-        FVSR_CU(launch_pool(static_cast<const uint8_t*>(k_new) + src_off, c->p.dtype, c->d.s, (int)c->d.channels,
-                            c->pk_arena + (int64_t)page * c->d.s * c->d.channels, kd, st),
-                "cache append (copy + pool keys)");
-        FVSR_CU(cudaMemcpyAsync(vd, static_cast<const uint8_t*>(v_new) + src_off, c->page_bytes(), cudaMemcpyDeviceToDevice, st),
-                "cache append (values)");
-        c->pages.push_back(page);
+        dst.page_block[t] = page * c->d.s;
+        pages.push_back(page);
     }
+    FVSR_CU(launch_append(k_new, v_new, c->p.dtype, (int64_t)new_slices * c->d.s, (int)c->d.channels, dst, c->k_arena,
+                          c->v_arena, c->pk_arena, st),
+            "cache append launch");
+    c->pages = pages;
     return FVSR_OK;
 }
 

@@ -50,6 +50,10 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // ---- launchers (each returns the launch's cudaError_t) ----
 cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
                         cudaStream_t st);
+// The cache append in one launch: nblocks new key/value blocks (k_new, v_new, window order) are copied to arena blocks
+// dst.page_block[b / dst.s] + b % dst.s of k_arena / v_arena and the keys pooled into pk_arena (same arena blocks).
+cudaError_t launch_append(const void* k_new, const void* v_new, int dtype, int64_t nblocks, int channels,
+                          const KvPages& dst, void* k_arena, void* v_arena, float* pk_arena, cudaStream_t st);
 // Pools two tensors (n1 and n2 blocks) in one launch; also clears zero_words 32-bit words at `zero` (the selection's
 // histograms, which the next kernels accumulate into).
 cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,

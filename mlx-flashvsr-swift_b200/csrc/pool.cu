@@ -106,7 +106,109 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
     }
 }
 
+// The cache append of DiT.swift:508-511 in one launch: new key block b (of nblocks = slices·s) is pooled into the pooled
+// key arena and copied, with value block b, into arena block dst.page_block[b / s] + b % s. The pooling arithmetic is
+// the one above (token order within each group of 32, groups combined (g0+g1)+(g2+g3)), so the pooled keys are
+// bit-identical to pool_kernel's. Key and value rows of a batch of U tokens are all loaded before any is stored.
+// Algorithmic bytes: 2·nblocks·128·C·elt read + the same written + nblocks·C·4 written.
+template <int DT>
+__global__ void __launch_bounds__(256, 4) append_kernel(const void* __restrict__ k_new, const void* __restrict__ v_new,
+                                                     int channels, int nblocks, const __grid_constant__ KvPages dst,
+                                                     void* __restrict__ k_arena,
+                                                     void* __restrict__ v_arena, float* __restrict__ pk_arena,
+                                                     int lanes) {
+    constexpr int U = DT == 1 ? 4 : 2;               // tokens per batch (64 registers: 4 CTAs per SM)
+    constexpr int W = DT == 1 ? 1 : 2;               // uint4 words per 8 channels
+    __shared__ float part[4][kPoolChannels];
+    griddep_wait_then_release();
+    const int lane = threadIdx.x & (kPoolLanes - 1);
+    const int g = threadIdx.x / kPoolLanes;
+    const int sub = lane / lanes, cl = lane % lanes;
+    const int c0 = blockIdx.x * kPoolChannels + cl * 8;
+    const int64_t b = (int64_t)blockIdx.y * (kPoolLanes / lanes) + sub;
+    const bool live = b < nblocks && c0 < channels;
+    const int64_t pb = live ? (int64_t)dst.page_block[b / dst.s] + b % dst.s : 0;  // arena block
+    const int row_words = channels * (DT == 1 ? 2 : 4) / 16;                       // uint4 words per token row
+    const int64_t cw = (int64_t)c0 * (DT == 1 ? 2 : 4) / 16;
+    const int64_t first = (b * kBlock + 32 * g) * row_words + cw;            // this thread's first token row
+    const int64_t first_dst = (pb * kBlock + 32 * g) * row_words + cw;
+    const uint4* ks = static_cast<const uint4*>(k_new) + first;
+    const uint4* vs = static_cast<const uint4*>(v_new) + first;
+    uint4* kd = static_cast<uint4*>(k_arena) + first_dst;
+    uint4* vd = static_cast<uint4*>(v_arena) + first_dst;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    if (live) {
+#pragma unroll 1
+        for (int t = 0; t < 32; t += U) {
+            uint4 kv[U][W], vv[U][W];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int w = 0; w < W; ++w) {
+                    kv[u][w] = __ldcs(ks + u * row_words + w);
+                    vv[u][w] = __ldcs(vs + u * row_words + w);
+                }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+#pragma unroll
+                for (int w = 0; w < W; ++w) {
+                    kd[u * row_words + w] = kv[u][w];
+                    vd[u * row_words + w] = vv[u][w];
+                }
+                if constexpr (DT == 1) {
+                    const uint32_t x[4] = {kv[u][0].x, kv[u][0].y, kv[u][0].z, kv[u][0].w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[2 * i] = __fadd_rn(acc[2 * i], bf16_bits_to_float(x[i] & 0xFFFFu));
+                        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], bf16_bits_to_float(x[i] >> 16));
+                    }
+                } else {
+                    const uint32_t x[8] = {kv[u][0].x, kv[u][0].y, kv[u][0].z, kv[u][0].w,
+                                           kv[u][W - 1].x, kv[u][W - 1].y, kv[u][W - 1].z, kv[u][W - 1].w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], __uint_as_float(x[i]));
+                }
+            }
+            ks += U * row_words;
+            vs += U * row_words;
+            kd += U * row_words;
+            vd += U * row_words;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) part[g][lane * 8 + i] = acc[i];
+    __syncthreads();
+    if (g == 0 && live) {
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = lane * 8 + i;
+            const float sum = __fadd_rn(__fadd_rn(part[0][c], part[1][c]), __fadd_rn(part[2][c], part[3][c]));
+            r[i] = __fmul_rn(sum, 0.0078125f);
+        }
+        float4* o = reinterpret_cast<float4*>(pk_arena + pb * channels + c0);
+        o[0] = make_float4(r[0], r[1], r[2], r[3]);
+        o[1] = make_float4(r[4], r[5], r[6], r[7]);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_append(const void* k_new, const void* v_new, int dtype, int64_t nblocks, int channels,
+                          const KvPages& dst, void* k_arena, void* v_arena, float* pk_arena, cudaStream_t st) {
+    if (nblocks == 0) return cudaSuccess;
+    int lanes = 1;
+    while (lanes < kPoolLanes && lanes * 8 < channels) lanes <<= 1;
+    const int bpc = kPoolLanes / lanes;
+    dim3 grid((channels + kPoolChannels - 1) / kPoolChannels, (unsigned)((nblocks + bpc - 1) / bpc));
+    if (dtype == 1)
+        return launch_pdl(append_kernel<1>, grid, dim3(256), 0, st, k_new, v_new, channels, (int)nblocks, dst, k_arena,
+                          v_arena, pk_arena, lanes);
+    return launch_pdl(append_kernel<0>, grid, dim3(256), 0, st, k_new, v_new, channels, (int)nblocks, dst, k_arena,
+                      v_arena, pk_arena, lanes);
+}
 
 cudaError_t launch_pool(const void* x, int dtype, int64_t nblocks, int channels, float* out, void* copy_dst,
                         cudaStream_t st) {

@@ -288,5 +288,30 @@ def test_streaming_forward_matches_reference_semantics(fvsr, orc, cfgs, kv_len, 
     fvsr.device_check()
 
 
+@pytest.mark.parametrize("heads,dtype", [(12, "bf16"), (3, "f32"), (1, "bf16")])
+def test_cache_append_pages(fvsr, heads, dtype):
+    """The one-launch append writes every new slice into its own page: gather() returns the last kv_len slices in
+    order after appends of 1 and 3 slices wrap the page ring, for channel counts of 1, 3 and 12 heads."""
+    g = fvsr.Geometry(heads=heads, bh=3, bw=5, q_slices=3, kv_slices=5, local_range=11,
+                      dtype=fvsr.FVSR_BF16 if dtype == "bf16" else fvsr.FVSR_F32)
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    rows = g.s * 128
+    cache = fvsr.KVCache(g, kv_len=2, max_new_slices=3)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    ks, vs = [], []
+    for n in (3, 1, 3, 1, 1, 3):
+        k = torch.randn((n * rows, g.channels), generator=gen, device="cuda").to(tdt)
+        v = torch.randn((n * rows, g.channels), generator=gen, device="cuda").to(tdt)
+        cache.append(k, v, n)
+        ks += list(k.split(rows))
+        vs += list(v.split(rows))
+        gk, gv = cache.gather()
+        assert torch.equal(gk, torch.cat(ks[-cache.slices:])) and torch.equal(gv, torch.cat(vs[-cache.slices:]))
+        while cache.slices > 2:
+            cache.trim()
+    cache.close()
+    fvsr.device_check()
+
+
 def test_device_check_clean(fvsr, cfgs):
     fvsr.device_check()
