@@ -192,6 +192,40 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
                               fvsr_kv_cache* cache, void* out, int32_t* kidx, int32_t* kcnt, void* workspace,
                               size_t workspace_bytes, fvsr_stream_t stream);
 
+/* ---- Token-order entry points: the q/k/v side and the output side of blockForward's self-attention ----
+ * Token grid of a chunk: (F, Hp, Wp) = (2·q_slices, 8·bh, 8·bw) patches, L = F·Hp·Wp = Nq·128 tokens in token order
+ * (row (f·Hp + y)·Wp + x), the layout the Swift DiT holds before windowPartition and after windowReverse. At most 16
+ * heads (FVSR_EUNSUPPORTED beyond).
+ *
+ * Rounding points (the reference's, with its order of operations): WanRMSNorm (DiT.swift:34-47)
+ *   ss = Σ_c x_c² in fp32, inv = 1/√(ss / C + eps) correctly rounded, n = T(x·inv), y = T(n·w)
+ * where Σ runs as 32 lane partials (lane l sums x² over channels 128·i + 4l .. 4l + 3 for i = 0..H−1 in order) combined
+ * by a butterfly v_l += v_{l^o}, o = 16, 8, 4, 2, 1 (MLX's reduction order is unspecified; this is the library's);
+ * ropeApply (DiT.swift:100-107) on each head's pairs (2j, 2j+1) with the token's (cos_j, sin_j):
+ *   re' = T(re·cos − im·sin), im' = T(re·sin + im·cos), every product and sum rounded to fp32;
+ * T = the storage type (bf16 round-to-nearest-even, or fp32).
+ *
+ * fvsr_lcsa_prepare: q_lin, k_lin, v_lin (L, H·128) token order, the three linear outputs of DiT.swift:497-499 →
+ * q_win, k_win, v_win (L, H·128) window order (DiT.swift:504-506) after norm (q, k; weight NULL = skipped) and
+ * rotation (q, k; tables NULL = skipped), plus optional pooled_q / pooled_k (Nq, H·128) fp32 block means of q_win /
+ * k_win, bit-identical to fvsr_lcsa_pool of those outputs. norm_q / norm_k: (H·128) in p->dtype. rope_cos / rope_sin:
+ * (L, 64) fp32, row = token, the tables RopeTables.grid builds (DiT.swift:80-97). One kernel launch. */
+fvsr_status fvsr_lcsa_prepare(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin, const void* v_lin,
+                              const void* norm_q, const void* norm_k, float eps, const float* rope_cos,
+                              const float* rope_sin, void* q_win, void* k_win, void* v_win, float* pooled_q,
+                              float* pooled_k, fvsr_stream_t stream);
+
+/* One streaming layer from the linear outputs to the input of the output projection — DiT.swift:499-539 between
+ * sa.q/k/v and sa.o: fvsr_lcsa_prepare with k and v written straight into the cache's new pages (the append) and the
+ * pooled keys into its pooled arena, selection over cache ⊕ current, attention, trim, and the output written in token
+ * order (windowReverse, DiT.swift:539, fused into the attention's epilogue). q_win: caller-owned (L, H·128) buffer
+ * that receives the window-ordered q. out: (L, H·128) token order. Same workspace as fvsr_lcsa_forward. */
+fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin,
+                                     const void* v_lin, const void* norm_q, const void* norm_k, float eps,
+                                     const float* rope_cos, const float* rope_sin, fvsr_kv_cache* cache, void* q_win,
+                                     void* out, int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                                     fvsr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -30,7 +30,7 @@ EXPORTED = [
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
     "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range", "fvsr_lcsa_item_order", "fvsr_lcsa_schedule_size",
-    "fvsr_lcsa_schedule", "fvsr_lcsa_attention_scheduled",
+    "fvsr_lcsa_schedule", "fvsr_lcsa_attention_scheduled", "fvsr_lcsa_prepare", "fvsr_lcsa_forward_tokens",
 ]
 
 
@@ -93,6 +93,9 @@ def lib() -> ctypes.CDLL:
         "fvsr_lcsa_schedule_size": ([PP, I32, ctypes.POINTER(SZ)], ctypes.c_int),
         "fvsr_lcsa_schedule": ([PP, P, I32, I32, P, SZ, P], ctypes.c_int),
         "fvsr_lcsa_attention_scheduled": ([PP, P, P, P, P, P, P, I32, I32, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_prepare": ([PP, P, P, P, P, P, ctypes.c_float, P, P, P, P, P, P, P, P], ctypes.c_int),
+        "fvsr_lcsa_forward_tokens": ([PP, P, P, P, P, P, ctypes.c_float, P, P, P, P, P, P, P, P, SZ, P],
+                                     ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -476,6 +479,98 @@ def lcsa_forward(q, k_new, v_new, cache: KVCache, geom: Geometry, out=None, kidx
     p = geom.params()
     _check(lib().fvsr_lcsa_forward(ctypes.byref(p), _ptr(q2), _ptr(_rows(k_new)), _ptr(_rows(v_new)), cache.handle,
                                    _ptr(out), _ptr(kidx), _ptr(kcnt), _ptr(ws), ws.numel(), _stream(stream)))
+    return out
+
+
+def rope_tables(f: int, h: int, w: int, t0: int = 0, head_dim: int = 128, theta: float = 10000.0, device="cuda"):
+    """RopeTables (DiT.swift:52-97): for every token of an (f, h, w) patch grid in token order, temporal positions
+    starting at t0, the 64 (cos, sin) entries of the 3-D factorised rotation — temporal 44 | height 42 | width 42 of a
+    128-wide head, each axis's frequencies normalised by its own sub-dimension, angles in float64, tables in fp32.
+    Returns (cos, sin), each (f·h·w, 64) fp32."""
+    import numpy as np
+    torch = _torch()
+    if head_dim != 128:
+        raise FVSRError(FVSR_EINVAL, "head_dim must be 128")
+    if t0 < 0 or t0 + f > 1024 or h > 1024 or w > 1024:
+        raise FVSRError(FVSR_EINVAL, "positions must stay below 1024 (RopeTables.end)")
+    d_hw = head_dim // 3
+    d_t = head_dim - 2 * d_hw
+
+    def table(dim, positions):
+        j = np.arange(dim // 2, dtype=np.float64)
+        freq = 1.0 / np.power(theta, 2.0 * j / dim)
+        ang = np.asarray(positions, dtype=np.float64)[:, None] * freq[None, :]
+        return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+    ct, st = table(d_t, np.arange(t0, t0 + f))
+    ch, sh = table(d_hw, np.arange(h))
+    cw, sw = table(d_hw, np.arange(w))
+
+    def grid(tt, th, tw):
+        n = tt.shape[1] + th.shape[1] + tw.shape[1]
+        g = np.empty((f, h, w, n), np.float32)
+        g[..., : tt.shape[1]] = tt[:, None, None, :]
+        g[..., tt.shape[1]: tt.shape[1] + th.shape[1]] = th[None, :, None, :]
+        g[..., tt.shape[1] + th.shape[1]:] = tw[None, None, :, :]
+        return torch.from_numpy(g.reshape(f * h * w, n)).to(device)
+
+    return grid(ct, ch, cw), grid(st, sh, sw)
+
+
+def _token_inputs(geom: Geometry, q_lin, k_lin, v_lin, norm_q, norm_k, rope):
+    rows = geom.nq * 128
+    ts = [_rows(t) for t in (q_lin, k_lin, v_lin)]
+    for t in ts:
+        if t.shape != (rows, geom.channels):
+            raise FVSRError(FVSR_EINVAL, f"linear outputs must be ({rows}, {geom.channels}), got {tuple(t.shape)}")
+    for wt in (norm_q, norm_k):
+        if wt is not None and (wt.dtype != ts[0].dtype or tuple(wt.shape) != (geom.channels,) or not wt.is_contiguous()
+                               or not wt.is_cuda):
+            raise FVSRError(FVSR_EINVAL, f"norm weights must be contiguous CUDA ({geom.channels},) in the q dtype")
+    cos, sin = rope if rope is not None else (None, None)
+    for t in (cos, sin):
+        if t is not None and (t.dtype != _torch().float32 or tuple(t.shape) != (rows, 64) or not t.is_contiguous()):
+            raise FVSRError(FVSR_EINVAL, f"rotation tables must be contiguous ({rows}, 64) fp32")
+    return ts, cos, sin
+
+
+def lcsa_prepare(q_lin, k_lin, v_lin, geom: Geometry, norm_q=None, norm_k=None, eps: float = 1e-6, rope=None,
+                 pooled: bool = True, stream=None) -> dict:
+    """The q/k/v side of one layer (DiT.swift:497-506) from the linear outputs (token order, (Nq·128, H·128)):
+    WanRMSNorm of q and k (weights norm_q / norm_k, None = skipped), ropeApply with rope = (cos, sin) tables from
+    rope_tables (None = skipped), windowPartition of all three, and the pooled q / k the selection reads.
+    Returns {"q", "k", "v"} window-ordered and, with pooled, {"pooled_q", "pooled_k"} (Nq, H·128) fp32."""
+    torch = _torch()
+    (q, k, v), cos, sin = _token_inputs(geom, q_lin, k_lin, v_lin, norm_q, norm_k, rope)
+    res = {"q": torch.empty_like(q), "k": torch.empty_like(k), "v": torch.empty_like(v)}
+    if pooled:
+        res["pooled_q"] = torch.empty((geom.nq, geom.channels), dtype=torch.float32, device=q.device)
+        res["pooled_k"] = torch.empty_like(res["pooled_q"])
+    p = geom.params()
+    _check(lib().fvsr_lcsa_prepare(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(norm_q), _ptr(norm_k), eps,
+                                   _ptr(cos), _ptr(sin), _ptr(res["q"]), _ptr(res["k"]), _ptr(res["v"]),
+                                   _ptr(res.get("pooled_q")), _ptr(res.get("pooled_k")), _stream(stream)))
+    return res
+
+
+def lcsa_forward_tokens(q_lin, k_lin, v_lin, cache: KVCache, geom: Geometry, norm_q=None, norm_k=None,
+                        eps: float = 1e-6, rope=None, q_win=None, out=None, kidx=None, kcnt=None, workspace=None,
+                        stream=None):
+    """One streaming layer from the linear outputs to the input of the output projection (DiT.swift:499-539):
+    prepare (k, v straight into the cache), select over cache ⊕ current, attend, trim; returns the output in token
+    order (windowReverse fused). geom.q_slices = the chunk's slices; geom.kv_slices is taken from the cache."""
+    torch = _torch()
+    (q, k, v), cos, sin = _token_inputs(geom, q_lin, k_lin, v_lin, norm_q, norm_k, rope)
+    if q_win is None:
+        q_win = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
+    full = Geometry(**{**geom.__dict__, "kv_slices": min(cache.slices + geom.q_slices, cache.capacity)})
+    ws = workspace if workspace is not None else make_workspace(full, q.device)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_forward_tokens(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(norm_q), _ptr(norm_k), eps,
+                                          _ptr(cos), _ptr(sin), cache.handle, _ptr(q_win), _ptr(out), _ptr(kidx),
+                                          _ptr(kcnt), _ptr(ws), ws.numel(), _stream(stream)))
     return out
 
 

@@ -150,18 +150,19 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
 
 fvsr_status run_attention(const fvsr_lcsa_params* p, const Dims& d, const void* q, const void* k, const void* v,
                           int64_t kv_rows, const KvPages& pages, const int32_t* kidx, const int32_t* kcnt, void* out,
-                          cudaStream_t st, int item_begin = 0, int item_count = -1, const int32_t* order = nullptr) {
+                          cudaStream_t st, int item_begin = 0, int item_count = -1, const int32_t* order = nullptr,
+                          OutRows rows = {}) {
     fvsr_status s = check_device_sm100();
     if (s != FVSR_OK) return s;
     if (item_count < 0) item_count = d.heads * d.nq;
     if (p->dtype == FVSR_BF16) {
         FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, item_begin, item_count,
-                                 order, st),
+                                 order, st, rows),
                 "bf16 attention launch");
     } else {
         FVSR_CU(launch_attn_f32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
                                 pages, d.heads, d.nq, d.nk, kidx, kcnt, static_cast<float*>(out), item_begin, item_count,
-                                order, st),
+                                order, st, rows),
                 "fp32 attention launch");
     }
     return FVSR_OK;
@@ -181,6 +182,58 @@ struct fvsr_kv_cache {
     int64_t page_rows() const { return (int64_t)d.s * 128; }
     int64_t page_bytes() const { return page_rows() * d.channels * d.elt; }
 };
+
+namespace {
+
+// The arena pages new_slices appended slices take (the lowest free ones, in slice order): *dst maps new window w to
+// arena block dst->page_block[w / s] + w % s, *pages is the cache's page list after the append.
+void choose_pages(const fvsr_kv_cache* c, int new_slices, KvPages* dst, std::vector<int32_t>* pages) {
+    *dst = KvPages{};
+    dst->s = c->d.s;
+    *pages = c->pages;
+    for (int t = 0; t < new_slices; ++t) {
+        int page = -1;
+        for (int cand = 0; cand < c->capacity && page < 0; ++cand) {
+            bool used = false;
+            for (int32_t u : *pages) used |= (u == cand);
+            if (!used) page = cand;
+        }
+        dst->page_block[t] = page * c->d.s;
+        pages->push_back(page);
+    }
+}
+
+// Host checks shared by the two token-order entry points; fills the parts of *a that do not depend on destinations.
+fvsr_status check_prepare_inputs(const fvsr_lcsa_params* p, const Dims& d, const void* q_lin, const void* k_lin,
+                                 const void* v_lin, const void* norm_q, const void* norm_k, float eps,
+                                 const float* rope_cos, const float* rope_sin, PrepArgs* a) {
+    if (d.heads > kPrepMaxHeads)
+        return fail(FVSR_EUNSUPPORTED, "the token-order path supports at most %d heads, got %d", kPrepMaxHeads, d.heads);
+    if (!q_lin || !k_lin || !v_lin) return fail(FVSR_EINVAL, "q_lin, k_lin and v_lin are required");
+    if (!aligned16(q_lin) || !aligned16(k_lin) || !aligned16(v_lin))
+        return fail(FVSR_EINVAL, "q_lin, k_lin and v_lin must be 16-byte aligned");
+    if ((rope_cos == nullptr) != (rope_sin == nullptr))
+        return fail(FVSR_EINVAL, "rope_cos and rope_sin are given together or not at all");
+    if (rope_cos && (!aligned16(rope_cos) || !aligned16(rope_sin)))
+        return fail(FVSR_EINVAL, "rope_cos and rope_sin must be 16-byte aligned");
+    if ((norm_q || norm_k) && !(eps >= 0.0f && eps < 1e30f)) return fail(FVSR_EINVAL, "eps must be finite and >= 0");
+    *a = PrepArgs{};
+    a->x[0] = q_lin;
+    a->x[1] = k_lin;
+    a->x[2] = v_lin;
+    a->norm_w[0] = norm_q;
+    a->norm_w[1] = norm_k;
+    a->cosv = rope_cos;
+    a->sinv = rope_sin;
+    a->eps = eps;
+    a->heads = d.heads;
+    a->bh = p->bh;
+    a->bw = p->bw;
+    a->nq = d.nq;
+    return FVSR_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -459,18 +512,8 @@ fvsr_status fvsr_kv_cache_append(fvsr_kv_cache* c, const void* k_new, const void
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     // lowest free arena page for each new slice, then one launch copies keys and values and pools the keys
     KvPages dst{};
-    dst.s = c->d.s;
-    std::vector<int32_t> pages = c->pages;
-    for (int t = 0; t < new_slices; ++t) {
-        int page = -1;
-        for (int cand = 0; cand < c->capacity && page < 0; ++cand) {
-            bool used = false;
-            for (int32_t u : pages) used |= (u == cand);
-            if (!used) page = cand;
-        }
-        dst.page_block[t] = page * c->d.s;
-        pages.push_back(page);
-    }
+    std::vector<int32_t> pages;
+    choose_pages(c, new_slices, &dst, &pages);
     FVSR_CU(launch_append(k_new, v_new, c->p.dtype, (int64_t)new_slices * c->d.s, (int)c->d.channels, dst, c->k_arena,
                           c->v_arena, c->pk_arena, st),
             "cache append launch");
@@ -543,6 +586,90 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     FVSR_CU(launch_item_order(lc, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
     s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
                       out, st, 0, d.heads * d.nq, w.order);
+    if (s != FVSR_OK) return s;
+    return fvsr_kv_cache_trim(cache);
+}
+
+fvsr_status fvsr_lcsa_prepare(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin, const void* v_lin,
+                              const void* norm_q, const void* norm_k, float eps, const float* rope_cos,
+                              const float* rope_sin, void* q_win, void* k_win, void* v_win, float* pooled_q,
+                              float* pooled_k, fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d, /*need_kv=*/false);
+    if (s != FVSR_OK) return s;
+    PrepArgs a;
+    s = check_prepare_inputs(p, d, q_lin, k_lin, v_lin, norm_q, norm_k, eps, rope_cos, rope_sin, &a);
+    if (s != FVSR_OK) return s;
+    if (!q_win || !k_win || !v_win) return fail(FVSR_EINVAL, "q_win, k_win and v_win are required");
+    if (!aligned16(q_win) || !aligned16(k_win) || !aligned16(v_win))
+        return fail(FVSR_EINVAL, "q_win, k_win and v_win must be 16-byte aligned");
+    s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    a.q_out = q_win;
+    a.kv_out[0] = k_win;
+    a.kv_out[1] = v_win;
+    a.pooled[0] = pooled_q;
+    a.pooled[1] = pooled_k;
+    a.kv_pages.s = d.nq;  // one page: window w → block w
+    FVSR_CU(launch_prepare(a, p->dtype, reinterpret_cast<cudaStream_t>(stream)), "prepare launch");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin,
+                                     const void* v_lin, const void* norm_q, const void* norm_k, float eps,
+                                     const float* rope_cos, const float* rope_sin, fvsr_kv_cache* cache, void* q_win,
+                                     void* out, int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                                     fvsr_stream_t stream) {
+    if (!cache) return fail(FVSR_EINVAL, "cache is NULL");
+    if (!p) return fail(FVSR_EINVAL, "params is NULL");
+    if (p->heads != cache->p.heads || p->bh != cache->p.bh || p->bw != cache->p.bw || p->dtype != cache->p.dtype)
+        return fail(FVSR_EINVAL, "params do not match the cache geometry");
+    if (!q_win || !out) return fail(FVSR_EINVAL, "q_win and out are required");
+    if (!aligned16(q_win) || !aligned16(out)) return fail(FVSR_EINVAL, "q_win and out must be 16-byte aligned");
+    if (p->q_slices < 1 || (int)cache->pages.size() + p->q_slices > cache->capacity)
+        return fail(FVSR_EINVAL, "appending %d slices to %zu exceeds the capacity %d", p->q_slices, cache->pages.size(),
+                    cache->capacity);
+    fvsr_lcsa_params pp = *p;
+    pp.kv_slices = (int32_t)cache->pages.size() + p->q_slices;
+    Dims d;
+    fvsr_status s = check_params(&pp, &d);
+    if (s != FVSR_OK) return s;
+    PrepArgs a;
+    s = check_prepare_inputs(&pp, d, q_lin, k_lin, v_lin, norm_q, norm_k, eps, rope_cos, rope_sin, &a);
+    if (s != FVSR_OK) return s;
+    Workspace w = layout(d, workspace);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // norm + rotation + partition of q, k, v; k and v straight into the cache's new pages (the append), pooled k into
+    // the pooled arena, pooled q into the workspace; the selection histograms cleared on the way
+    std::vector<int32_t> new_pages;
+    choose_pages(cache, p->q_slices, &a.kv_pages, &new_pages);
+    a.q_out = q_win;
+    a.kv_out[0] = cache->k_arena;
+    a.kv_out[1] = cache->v_arena;
+    a.pooled[0] = w.pooled_q;
+    a.pooled[1] = cache->pk_arena;
+    a.zero = w.hist;
+    a.zero_words = select_hist_bytes(d.heads, d.q_slices) / 4;
+    FVSR_CU(launch_prepare(a, pp.dtype, st), "prepare launch");
+    cache->pages = new_pages;
+    KvPages pages{};
+    pages.s = d.s;
+    for (int i = 0; i < kMaxPages; ++i)
+        pages.page_block[i] = (i < (int)cache->pages.size() ? cache->pages[i] : 0) * d.s;
+    int32_t* li = kidx ? kidx : w.kidx;
+    int32_t* lc = kcnt ? kcnt : w.kcnt;
+    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, st);
+    if (s != FVSR_OK) return s;
+    FVSR_CU(launch_item_order(lc, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
+    OutRows rows;
+    rows.bh = pp.bh;
+    rows.bw = pp.bw;
+    s = run_attention(&pp, d, q_win, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages,
+                      li, lc, out, st, 0, d.heads * d.nq, w.order, rows);
     if (s != FVSR_OK) return s;
     return fvsr_kv_cache_trim(cache);
 }

@@ -28,7 +28,8 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
                                                        const float* __restrict__ v, KvPages pages, int heads, int nq,
                                                        int nk, const int32_t* __restrict__ kidx,
                                                        const int32_t* __restrict__ kcnt, float* __restrict__ out,
-                                                       int item_begin, const int32_t* __restrict__ order) {
+                                                       int item_begin, const int32_t* __restrict__ order,
+                                                       OutRows rows) {
     extern __shared__ float4 smem4[];
     F32Smem& sm = *reinterpret_cast<F32Smem*>(smem4);
     griddep_wait_then_release();
@@ -39,7 +40,7 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
     const int r = tid >> 1, hf = tid & 1;
     int cnt = kcnt[item];
     cnt = cnt < 0 ? 0 : (cnt > nk ? nk : cnt);
-    float* orow = out + ((int64_t)qb * kBlock + r) * ld + h * kD + hf * 64;
+    float* orow = out + rows.row(qb, r) * ld + h * kD + hf * 64;
     if (cnt == 0) {
         for (int i = 0; i < 16; ++i) reinterpret_cast<float4*>(orow)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         return;
@@ -133,13 +134,13 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
 
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
                             int nk, const int32_t* kidx, const int32_t* kcnt, float* out, int item_begin,
-                            int item_count, const int32_t* order, cudaStream_t st) {
+                            int item_count, const int32_t* order, cudaStream_t st, OutRows rows) {
     if (item_count <= 0) return cudaSuccess;
     const int smem = (int)sizeof(F32Smem);
     cudaError_t e = cudaFuncSetAttribute(attn_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     return launch_pdl(attn_f32_kernel, dim3(item_count), dim3(256), (size_t)smem, st, q, k, v, pages, heads, nq, nk,
-                      kidx, kcnt, out, item_begin, order);
+                      kidx, kcnt, out, item_begin, order, rows);
 }
 
 }  // namespace fvsr

@@ -80,6 +80,7 @@ struct AttnArgs {
     const int32_t* order;  // optional item order (longest first within each head); NULL = ascending
     float scale_log2;
     KvPages pages;
+    OutRows rows;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (cnt == 0) {  // SparseAttention.swift:47-53: a query block that selected nothing writes zeros
         for (int idx = threadIdx.x; idx < kBlock * 16; idx += kThreads) {
             const int r = idx >> 4, c = idx & 15;
-            *reinterpret_cast<uint4*>(a.out + ((int64_t)qb * kBlock + r) * ld + h * kD + c * 8) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(a.out + a.rows.row(qb, r) * ld + h * kD + c * 8) = make_uint4(0, 0, 0, 0);
         }
         return;
     }
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float mf = fmaxf(m0, m1);
             const float l_row = l0 * ex2_approx(m0 - mf) + l1 * ex2_approx(m1 - mf);
             const float inv = 1.0f / l_row;
-            __nv_bfloat16* orow = a.out + ((int64_t)qb * kBlock + r) * ld + h * kD + 64 * st;
+            __nv_bfloat16* orow = a.out + a.rows.row(qb, r) * ld + h * kD + 64 * st;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t ov[32];
@@ -370,7 +371,7 @@ size_t attn_bf16_smem_bytes(int nk) { return 1024 + kOffList + sizeof(int32_t) *
 
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
-                             int item_begin, int item_count, const int32_t* order, cudaStream_t st) {
+                             int item_begin, int item_count, const int32_t* order, cudaStream_t st, OutRows rows) {
     if (item_count <= 0) return cudaSuccess;
     CUtensorMap mq, mk, mv;
     const int64_t channels = (int64_t)heads * kD;
@@ -391,6 +392,7 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     a.order = order;
     a.scale_log2 = (1.0f / sqrtf((float)kD)) * 1.4426950408889634f;
     a.pages = pages;
+    a.rows = rows;
     return launch_pdl(attn_bf16_sm100_kernel, dim3(item_count), dim3(kThreads), smem, st, mq, mk, mv, a);
 }
 

@@ -22,6 +22,24 @@ __host__ __device__ inline int32_t kv_phys_block(const KvPages& pg, int32_t j) {
     return pg.page_block[j / pg.s] + j % pg.s;
 }
 
+// Token r of window (query block) w on the (F, 8·bh, 8·bw) patch grid (windowPartition, DiT.swift:113-118): windows
+// ordered (nf, nh, nw), tokens inside a window (wf, wh, ww). token_row gives the token-order row (the layout
+// windowReverse, DiT.swift:121-126, restores).
+__host__ __device__ __forceinline__ int64_t token_row(int bh, int bw, int w, int r) {
+    const int s = bh * bw, nf = w / s, rem = w - nf * s, nh = rem / bw, nw = rem - nh * bw;
+    const int wf = r >> 6, wh = (r >> 3) & 7, ww = r & 7;
+    return ((int64_t)(2 * nf + wf) * (8 * bh) + 8 * nh + wh) * (8 * bw) + 8 * nw + ww;
+}
+
+// Where the attention writes output row r of query block qb: window order (bw == 0, row qb·128 + r) or token order
+// (windowReverse fused into the epilogue).
+struct OutRows {
+    int bh = 0, bw = 0;
+    __device__ __forceinline__ int64_t row(int qb, int r) const {
+        return bw == 0 ? (int64_t)qb * kBlock + r : token_row(bh, bw, qb, r);
+    }
+};
+
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
 // Programmatic dependent launch: every kernel of the path first waits for the kernel before it in the stream to have
@@ -73,10 +91,28 @@ cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, i
 // item order[b] when an order is given (a permutation of the range), else item_begin + b.
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
                             int nk, const int32_t* kidx, const int32_t* kcnt, float* out, int item_begin,
-                            int item_count, const int32_t* order, cudaStream_t st);
+                            int item_count, const int32_t* order, cudaStream_t st, OutRows rows = {});
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
-                             int item_begin, int item_count, const int32_t* order, cudaStream_t st);
+                             int item_begin, int item_count, const int32_t* order, cudaStream_t st,
+                             OutRows rows = {});
+// The q/k/v side of one layer from the linear outputs (prepare.cu). Token grid (2·q_slices, 8·bh, 8·bw); nq windows.
+struct PrepArgs {
+    const void* x[3];        // q, k, v linear outputs, token order (L, C)
+    const void* norm_w[2];   // RMSNorm weights of q and k (C, dtype) or NULL (no norm)
+    const float* cosv;       // (L, 64) fp32 rotation tables or NULL (no rotation)
+    const float* sinv;
+    void* q_out;             // (L, C) window order
+    void* kv_out[2];         // K and V arenas; window w goes to arena block kv_pages.page_block[w / s] + w % s
+    float* pooled[2];        // pooled q (nq, C) and pooled k (arena blocks, like K) or NULL
+    KvPages kv_pages;
+    uint32_t* zero;          // words cleared before the pass (the selection histograms) or NULL
+    size_t zero_words;
+    float eps;
+    int heads, bh, bw, nq;
+};
+cudaError_t launch_prepare(const PrepArgs& a, int dtype, cudaStream_t st);
+constexpr int kPrepMaxHeads = 16;
 // Work schedule of an item range (schedule.cu). A short range inside one head (at most kPersistItemsPerSm items per
 // SM) gets the persistent kernel's partition: the head's kept key blocks cut into G equal shares, CTA c walking its
 // share as segments (item, first list position, length, partial slot or −1); items cut by a share boundary are

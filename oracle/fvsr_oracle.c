@@ -7,6 +7,8 @@
  *
  * Every function restates one piece of the reference (paths relative to the xocialize/mlx-flashvsr-swift tree):
  *   orc_window_partition / orc_window_reverse  Sources/FlashVSRMLX/DiT.swift:113-126
+ *   orc_prepare                                Sources/FlashVSRMLX/DiT.swift:34-47 (WanRMSNorm), 100-107 (ropeApply),
+ *                                              113-118 (windowPartition) — the q/k/v side of blockForward, 497-506
  *   orc_local_block_mask                       Sources/FlashVSRMLX/DiT.swift:130-145
  *   orc_geometry_topk                          Sources/FlashVSRMLX/DiT.swift:478-485
  *   orc_pool                                   Sources/FlashVSRMLX/DiT.swift:161-162 (fp32 mean over 128 tokens)
@@ -159,6 +161,87 @@ void orc_pool(const void* x, int dtype, int64_t nblocks, int64_t c, float* out) 
             out[b * c + ch] = ((part[0] + part[1]) + (part[2] + part[3])) * 0.0078125f;
         }
     }
+}
+
+/* ------------------------------------------------------------------------------------------------------------ */
+/* The q/k side of blockForward: WanRMSNorm (DiT.swift:34-47), ropeApply (DiT.swift:100-107), windowPartition      */
+/* (DiT.swift:113-118).                                                                                           */
+/* ------------------------------------------------------------------------------------------------------------ */
+
+static inline uint16_t orc_f32_to_bf16(float f) {   /* round to nearest even (NaN stays NaN) */
+    union { float f; uint32_t u; } v;
+    v.f = f;
+    if ((v.u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((v.u >> 16) | 0x40u);
+    return (uint16_t)((v.u + 0x7FFFu + ((v.u >> 16) & 1u)) >> 16);
+}
+
+static inline float orc_round_t(float x, int dtype) { return dtype ? orc_bf16_to_f32(orc_f32_to_bf16(x)) : x; }
+
+/* x (F·H·W, C = heads·128) in token order (row (f·H + y)·W + x), dtype 0 fp32 / 1 bf16 → out, same shape and dtype,
+ * in window order (window (f/2, y/8, x/8), token (f%2, y%8, x%8)). weight: (C) in dtype, or NULL for no norm; cosv /
+ * sinv: (F·H·W, 64) fp32 rows per token, or NULL for no rotation. T = the storage type.
+ *   norm  : ss = Σ x² as 32 partials — partial l sums x·x over channels 128·i + 4l + e for i = 0..heads−1, e = 0..3 in
+ *           that order — combined by the butterfly v[l] = v[l] + v[l ^ o] for o = 16, 8, 4, 2, 1 (all l at once);
+ *           inv = 1/√(ss / C + eps) correctly rounded (evaluated in double); n = T(x·inv); y = T(n·w)
+ *           (DiT.swift:44-45: normalise in fp32, cast to T, times the weight).
+ *   rotate: for each head, pair (2j, 2j+1) = (re, im): re' = T(re·cos_j − im·sin_j), im' = T(re·sin_j + im·cos_j)
+ *           with every product and sum an fp32 operation (DiT.swift:103-106). */
+int orc_prepare(const void* x, int dtype, int f, int h, int w, int heads, const void* weight, float eps,
+                const float* cosv, const float* sinv, void* out) {
+    if (f % 2 || h % 8 || w % 8 || heads < 1) return 1;
+    const int c = heads * ORC_D, nh = h / 8, nw = w / 8;
+    const int64_t ntok = (int64_t)f * h * w;
+#pragma omp parallel for schedule(static)
+    for (int64_t tok = 0; tok < ntok; ++tok) {
+        float* row = (float*)malloc(sizeof(float) * (size_t)c);
+        const int ff = (int)(tok / ((int64_t)h * w)), yy = (int)(tok / w % h), xx = (int)(tok % w);
+        for (int ch = 0; ch < c; ++ch)
+            row[ch] = dtype == 0 ? ((const float*)x)[tok * c + ch] : orc_bf16_to_f32(((const uint16_t*)x)[tok * c + ch]);
+        if (weight) {
+            float v[32], t[32];
+            for (int l = 0; l < 32; ++l) {
+                float acc = 0.0f;
+                for (int i = 0; i < heads; ++i)
+                    for (int e = 0; e < 4; ++e) {
+                        const float xv = row[ORC_D * i + 4 * l + e];
+                        acc = acc + xv * xv;
+                    }
+                v[l] = acc;
+            }
+            for (int o = 16; o > 0; o >>= 1) {
+                for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
+                memcpy(v, t, sizeof(v));
+            }
+            const float ms = v[0] / (float)c;
+            const float a = ms + eps;
+            const float inv = (float)(1.0 / sqrt((double)a));
+            for (int ch = 0; ch < c; ++ch) {
+                const float wv = dtype == 0 ? ((const float*)weight)[ch] : orc_bf16_to_f32(((const uint16_t*)weight)[ch]);
+                const float n = orc_round_t(row[ch] * inv, dtype);
+                row[ch] = orc_round_t(n * wv, dtype);
+            }
+        }
+        if (cosv) {
+            for (int i = 0; i < heads; ++i)
+                for (int j = 0; j < ORC_D / 2; ++j) {
+                    const float re = row[ORC_D * i + 2 * j], im = row[ORC_D * i + 2 * j + 1];
+                    const float cs = cosv[tok * 64 + j], sn = sinv[tok * 64 + j];
+                    row[ORC_D * i + 2 * j] = orc_round_t(re * cs - im * sn, dtype);
+                    row[ORC_D * i + 2 * j + 1] = orc_round_t(re * sn + im * cs, dtype);
+                }
+        }
+        const int64_t win = ((int64_t)(ff / 2) * nh + yy / 8) * nw + xx / 8;
+        const int t = ((ff % 2) * 8 + yy % 8) * 8 + xx % 8;
+        const int64_t o = (win * ORC_BLOCK + t) * c;
+        for (int ch = 0; ch < c; ++ch) {
+            if (dtype == 0)
+                ((float*)out)[o + ch] = row[ch];
+            else
+                ((uint16_t*)out)[o + ch] = orc_f32_to_bf16(row[ch]);
+        }
+        free(row);
+    }
+    return 0;
 }
 
 /* ------------------------------------------------------------------------------------------------------------ */

@@ -40,6 +40,7 @@ def lib() -> ctypes.CDLL:
         _lib.fvsr_exp.restype = F
         _lib.orc_window_partition.argtypes = [P, I, I, I, I, I, P]
         _lib.orc_window_reverse.argtypes = [P, I, I, I, I, I, P]
+        _lib.orc_prepare.argtypes = [P, I, I, I, I, I, P, F, P, P, P]
         _lib.orc_local_block_mask.argtypes = [I, I, I, P]
         _lib.orc_local_block_mask.restype = None
         _lib.orc_geometry_topk.argtypes = [I, ctypes.c_double]
@@ -109,6 +110,26 @@ def window_reverse(x: np.ndarray, b: int, f: int, h: int, w: int) -> np.ndarray:
     out = np.empty((b, f * h * w, c), np.float32)
     if lib().orc_window_reverse(_p(x), b, f, h, w, c, _p(out)) != 0:
         raise ValueError("window reverse needs F even and H, W multiples of 8")
+    return out
+
+
+def prepare(x: np.ndarray, f: int, h: int, w: int, heads: int, weight: np.ndarray | None = None, eps: float = 1e-6,
+            cos: np.ndarray | None = None, sin: np.ndarray | None = None) -> np.ndarray:
+    """DiT.swift:34-47, 100-107, 113-118: x (F·H·W, heads·128) token order, fp32 or bf16 bits → WanRMSNorm (weight
+    given) → ropeApply (cos/sin (F·H·W, 64) fp32 given) → window order, same dtype, with the storage-type rounding
+    points of the reference (see orc_prepare)."""
+    x = np.ascontiguousarray(x)
+    dt = _dtype_code(x)
+    if weight is not None:
+        weight = np.ascontiguousarray(weight, dtype=x.dtype)
+    if (cos is None) != (sin is None):
+        raise ValueError("cos and sin go together")
+    if cos is not None:
+        cos = np.ascontiguousarray(cos, dtype=np.float32)
+        sin = np.ascontiguousarray(sin, dtype=np.float32)
+    out = np.empty_like(x)
+    if lib().orc_prepare(_p(x), dt, f, h, w, heads, _p(weight), float(eps), _p(cos), _p(sin), _p(out)) != 0:
+        raise ValueError("prepare needs F even and H, W multiples of 8")
     return out
 
 

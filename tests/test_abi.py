@@ -95,3 +95,30 @@ def test_topk_formula_and_allowed_counts(fvsr):
     assert cfgs[3].geometry().topk == 8384
     assert cfgs[5].geometry().topk == 14535
     assert cfgs[1].geometry().topk == 96
+
+
+def test_token_order_entry_points_check_arguments_on_host(fvsr):
+    """fvsr_lcsa_prepare / fvsr_lcsa_forward_tokens reject bad arguments before any launch (the addresses below are
+    never dereferenced: every case fails a host check first)."""
+    L = fvsr.lib()
+    fake = ctypes.c_void_p(1 << 20)  # 16-byte aligned, never touched
+    g = fvsr.Geometry(heads=17, bh=2, bw=2, q_slices=1, kv_slices=1, local_range=3, topk=3)
+    p = g.params()
+    args = [fake, fake, fake, None, None, ctypes.c_float(1e-6), None, None, fake, fake, fake, None, None, None]
+    assert L.fvsr_lcsa_prepare(ctypes.byref(p), *args) == fvsr.FVSR_EUNSUPPORTED
+    p.heads = 2
+    bad = list(args)
+    bad[6] = fake  # cos without sin
+    assert L.fvsr_lcsa_prepare(ctypes.byref(p), *bad) == fvsr.FVSR_EINVAL
+    assert b"together" in L.fvsr_last_error()
+    bad = list(args)
+    bad[0] = ctypes.c_void_p((1 << 20) + 8)  # misaligned q_lin
+    assert L.fvsr_lcsa_prepare(ctypes.byref(p), *bad) == fvsr.FVSR_EINVAL
+    bad = list(args)
+    bad[9] = None  # no k_win
+    assert L.fvsr_lcsa_prepare(ctypes.byref(p), *bad) == fvsr.FVSR_EINVAL
+    bad = list(args)
+    bad[3], bad[5] = fake, ctypes.c_float(-1.0)  # a norm with a negative eps
+    assert L.fvsr_lcsa_prepare(ctypes.byref(p), *bad) == fvsr.FVSR_EINVAL
+    assert L.fvsr_lcsa_forward_tokens(ctypes.byref(p), fake, fake, fake, None, None, ctypes.c_float(1e-6), None, None,
+                                      None, fake, fake, None, None, fake, 1 << 20, None) == fvsr.FVSR_EINVAL

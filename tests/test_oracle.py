@@ -173,3 +173,81 @@ def test_select_bad_shapes_rejected(orc):
         orc.select(pq, np.zeros((7, 128), np.float32), 1, 1, 6, np.ones((6, 6), bool), 3)   # Nk not a multiple of s
     with pytest.raises(ValueError):
         orc.select(pq, np.zeros((12, 128), np.float32), 1, 1, 6, np.ones((6, 6), bool), -1)  # negative topk
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# q/k side of blockForward: WanRMSNorm (DiT.swift:34-47), ropeApply (DiT.swift:100-107), windowPartition (113-118)
+# ---------------------------------------------------------------------------------------------------------------
+def _torch_reference_prepare(x, weight, cos, sin, heads, eps, dtype):
+    """DiT.swift:43-46 and 101-107 written with torch's fp32 elementwise ops, as the Swift code composes MLX ops:
+    normalise in fp32, cast to T, times the weight (in T); rotate the (even, odd) pairs in fp32, cast to T."""
+    import torch
+    t = torch.bfloat16 if dtype == "bf16" else torch.float32
+    xt = torch.from_numpy(x).view(torch.bfloat16) if dtype == "bf16" else torch.from_numpy(x)
+    if weight is not None:
+        wt = torch.from_numpy(weight).view(torch.bfloat16) if dtype == "bf16" else torch.from_numpy(weight)
+        xf = xt.float()
+        n = xf * torch.rsqrt((xf * xf).mean(dim=-1, keepdim=True) + eps)
+        xt = n.to(t) * wt
+    if cos is not None:
+        L = xt.shape[0]
+        xf = xt.float().reshape(L, heads, 64, 2)
+        re, im = xf[..., 0], xf[..., 1]
+        c = torch.from_numpy(cos).reshape(L, 1, 64)
+        s = torch.from_numpy(sin).reshape(L, 1, 64)
+        xt = torch.stack([re * c - im * s, re * s + im * c], dim=-1).reshape(L, heads * 128).to(t)
+    out = xt.view(torch.int16).numpy().view(np.uint16) if dtype == "bf16" else xt.numpy()
+    return out
+
+
+def _bf16_ulps(a, b):
+    ia = a.astype(np.int32)
+    ib = b.astype(np.int32)
+    # bf16 bit patterns of finite values: distance in units in the last place (same-sign values)
+    return np.abs(ia - ib)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_prepare_without_norm_and_rotation_is_the_window_partition(orc, dtype):
+    f, h, w, heads = 4, 16, 24, 2
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((f * h * w, heads * 128), dtype=np.float32)
+    if dtype == "bf16":
+        x = orc.f32_to_bf16_bits(x)
+    out = orc.prepare(x, f, h, w, heads)
+    xs = x if dtype == "f32" else x.astype(np.float32)   # partition is a permutation: compare the bit patterns
+    want = orc.window_partition(xs.reshape(1, f, h, w, heads * 128)).reshape(out.shape)
+    assert np.array_equal(out.astype(np.float32) if dtype == "bf16" else out, want)
+
+
+@pytest.mark.parametrize("dtype,heads", [("f32", 3), ("bf16", 2), ("bf16", 12)])
+def test_prepare_matches_the_reference_formulas(orc, dtype, heads):
+    """The rotation is bit-exact against torch's fp32 ops on the same normalised values; the norm agrees within one
+    unit of the storage type's last place (only the sum of squares' order and the rsqrt rounding may differ)."""
+    f, h, w = 2, 8, 16
+    L, C = f * h * w, heads * 128
+    rng = np.random.default_rng(7)
+    x = (rng.standard_normal((L, C)) * 2.0).astype(np.float32)
+    wgt = (1.0 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    ang = rng.uniform(-np.pi, np.pi, (L, 64))
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    if dtype == "bf16":
+        x, wgt = orc.f32_to_bf16_bits(x), orc.f32_to_bf16_bits(wgt)
+    # rotation alone: exact
+    got = orc.prepare(x, f, h, w, heads, cos=cos, sin=sin)
+    want = orc.window_partition(
+        (_torch_reference_prepare(x, None, cos, sin, heads, 1e-6, dtype).astype(np.float32) if dtype == "bf16" else
+         _torch_reference_prepare(x, None, cos, sin, heads, 1e-6, dtype)).reshape(1, f, h, w, C)).reshape(L, C)
+    assert np.array_equal(got.astype(np.float32) if dtype == "bf16" else got, want)
+    # norm (+ rotation): within one ulp of T
+    got = orc.prepare(x, f, h, w, heads, weight=wgt, eps=1e-6, cos=cos, sin=sin)
+    ref = _torch_reference_prepare(x, wgt, cos, sin, heads, 1e-6, dtype)
+    ref = orc.window_partition((ref.astype(np.float32) if dtype == "bf16" else ref).reshape(1, f, h, w, C))
+    ref = ref.reshape(L, C)
+    if dtype == "bf16":
+        d = _bf16_ulps(got, ref.astype(np.uint16))
+        assert d.max() <= 1 and (d == 0).mean() > 0.99, (d.max(), (d == 0).mean())
+    else:
+        # a one-ulp difference of a normalised value, carried through the rotation's cancellations
+        rel = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
+        assert rel.max() <= 8 * np.finfo(np.float32).eps, rel.max()
