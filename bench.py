@@ -15,6 +15,7 @@ on a bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -576,6 +577,106 @@ def run_kv_append(args):
                                  "slice_blocks": g.s, "heads": g.heads, "dtype": cfg.dtype}}), flush=True)
 
 
+def run_prepare(args):
+    """The q/k/v side of one layer (fvsr_lcsa_prepare: WanRMSNorm + ropeApply of q and k, windowPartition of q, k, v,
+    pooled q and k; DiT.swift:34-47, 100-107, 113-118, 161-162) as HBM traffic, and the whole token-order layer
+    (fvsr_lcsa_forward_tokens) beside the window-order one (fvsr_lcsa_forward). Prints one JSON line."""
+    import torch
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[args.config]
+    g = cfg.geometry()
+    L, C = g.nq * 128, g.channels
+    dt = torch.bfloat16 if cfg.dtype == "bf16" else torch.float32
+    elt = 2 if cfg.dtype == "bf16" else 4
+    # enough distinct (q, k, v) sets that successive calls read more than the 126 MB L2 holds
+    nbuf = max(2, -(-3 * 126_000_000 // (3 * L * C * elt)))
+    gen = torch.Generator(device="cuda").manual_seed(4321)
+    srcs = [[torch.randn((L, C), generator=gen, device="cuda").to(dt) for _ in range(3)] for _ in range(nbuf)]
+    wq, wk = ((1.0 + 0.1 * torch.randn((C,), generator=gen, device="cuda")).to(dt) for _ in range(2))
+    tabs = pkg.rope_tables(2 * g.q_slices, 8 * g.bh, 8 * g.bw, t0=4)
+    outs = {n: torch.empty((L, C), dtype=dt, device="cuda") for n in ("q", "k", "v")}
+    pooled = [torch.empty((g.nq, C), dtype=torch.float32, device="cuda") for _ in range(2)]
+    lib, p = pkg.lib(), g.params()
+    it = [0]
+
+    def one():
+        q, k, v = srcs[it[0] % nbuf]
+        it[0] += 1
+        pkg._check(lib.fvsr_lcsa_prepare(ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), wq.data_ptr(),
+                                         wk.data_ptr(), 1e-6, tabs[0].data_ptr(), tabs[1].data_ptr(),
+                                         outs["q"].data_ptr(), outs["k"].data_ptr(), outs["v"].data_ptr(),
+                                         pooled[0].data_ptr(), pooled[1].data_ptr(),
+                                         torch.cuda.current_stream().cuda_stream))
+
+    n = max(args.steps, 1) * 20
+    us = graph_time_us(one, n, max(args.warmup, 3))
+    # algorithmic bytes: q, k, v read and written once; the rotation tables read once; pooled q and k written
+    bytes_per = 2 * 3 * L * C * elt + 2 * L * 64 * 4 + 2 * g.nq * C * 4
+    _, hbm, kind = peaks()
+    gbs = bytes_per / (us * 1e-6) / 1e9
+
+    # whole layer: token-order (prepare into the cache, select, attend, token-order output) vs window-order
+    kv_len = g.kv_slices - g.q_slices
+    layer = {}
+    for mode in ("tokens", "window"):
+        cache = pkg.KVCache(g, kv_len, g.q_slices)
+        while cache.slices < kv_len:
+            cache.append(outs["k"][: g.s * 128], outs["v"][: g.s * 128], 1)
+        full = pkg.Geometry(**{**g.__dict__, "kv_slices": g.kv_slices})
+        ws = pkg.make_workspace(full)
+        out = torch.empty((L, C), dtype=dt, device="cuda")
+        qwin = torch.empty_like(out)
+        it[0] = 0
+
+        def layer_call():
+            q, k, v = srcs[it[0] % nbuf]
+            it[0] += 1
+            if mode == "tokens":
+                pkg.lcsa_forward_tokens(q, k, v, cache, g, norm_q=wq, norm_k=wk, eps=1e-6, rope=tabs, q_win=qwin,
+                                        out=out, workspace=ws)
+            else:
+                pkg.lcsa_forward(q, k, v, cache, g, out=out, workspace=ws)
+
+        layer[mode] = graph_time_us(layer_call, max(args.steps, 1) * 5, max(args.warmup, 3)) / 1e3
+        cache.close()
+    pkg.device_check()
+    print(json.dumps({"metric": f"prepare GB/s (RMSNorm + RoPE + window partition + pooling), config {args.config}",
+                      "value": gbs, "unit": "GB/s", "us_per_call": us, "bytes_per_call": bytes_per,
+                      "gpu_launches": n, "launch": "CUDA graph of the calls",
+                      "l2": f"{nbuf} source sets rotated ({nbuf * 3 * L * C * elt / 1e6:.0f} MB > L2)",
+                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                                   "peak_kind": kind},
+                      "layer_ms": {"forward_tokens (linear outputs in, token order out)": layer["tokens"],
+                                   "forward (window order in and out, no norm or rotation)": layer["window"]},
+                      "config": {"workload": f"config {args.config}: {cfg.name}", "tokens": L, "channels": C,
+                                 "dtype": cfg.dtype}}), flush=True)
+
+
+def graph_time_us(fn, n, warmup):
+    """Device µs per call of fn (which launches on the current stream): n calls captured once in a CUDA graph, the
+    graph replayed after warm-up, CUDA events around the replays."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(n):
+            fn()
+    reps = 5
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / (reps * n)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -597,9 +698,14 @@ def main():
                     help="one independent copy of the config per rank (default except for config 5)")
     ap.add_argument("--kv-append", action="store_true",
                     help="measure the window cache's in-place append (HBM GB/s) instead of the layer step")
+    ap.add_argument("--prepare", action="store_true",
+                    help="measure the token-order q/k/v pass (HBM GB/s) and the token-order layer")
     args = ap.parse_args()
     if args.kv_append:
         run_kv_append(args)
+        return
+    if args.prepare:
+        run_prepare(args)
         return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -25,49 +25,105 @@ namespace {
 constexpr int kPrepThreads = 128;
 constexpr int kPrepMaxC = kPrepMaxHeads * kD;
 
+// Applies norm (inv, weights) and rotation (cs, sn) to one lane's four channels of head i; returns the packed output
+// and adds the output values to acc. bf16: the weight multiply is one bf16x2 multiply — round(n·w) of the exact
+// product, which equals rounding the fp32 product (exact for two bf16 values) — and conversions pack pairs.
 template <int DT>
-struct Lane4;  // four channels of one lane
+struct LaneOps;
+
 template <>
-struct Lane4<1> {
+struct LaneOps<1> {
     using V = uint2;
+    static __device__ __forceinline__ void load_w(const void* wt, uint32_t* wsm, int C) {
+        for (int c = threadIdx.x; c < C / 2; c += kPrepThreads) wsm[c] = static_cast<const uint32_t*>(wt)[c];
+    }
+    static __device__ __forceinline__ float sumsq(const V& v, float ss) {
+        const float x[4] = {__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                            __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u)};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
+        return ss;
+    }
+    static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+        const __nv_bfloat162 h = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                         *reinterpret_cast<const __nv_bfloat162*>(&b));
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ V apply(V v, bool norm, float inv, const uint32_t* wsm, int wbase, bool rope,
+                                              float2 cs, float2 sn, bool pool, float* acc) {
+        if (norm) {
+            const uint2 w = *reinterpret_cast<const uint2*>(wsm + wbase / 2);
+            v.x = mul2(pack2(__fmul_rn(__uint_as_float(v.x << 16), inv),
+                             __fmul_rn(__uint_as_float(v.x & 0xFFFF0000u), inv)), w.x);
+            v.y = mul2(pack2(__fmul_rn(__uint_as_float(v.y << 16), inv),
+                             __fmul_rn(__uint_as_float(v.y & 0xFFFF0000u), inv)), w.y);
+        }
+        if (rope) {
+            const float r0 = __uint_as_float(v.x << 16), i0 = __uint_as_float(v.x & 0xFFFF0000u);
+            const float r1 = __uint_as_float(v.y << 16), i1 = __uint_as_float(v.y & 0xFFFF0000u);
+            v.x = pack2(__fsub_rn(__fmul_rn(r0, cs.x), __fmul_rn(i0, sn.x)),
+                        __fadd_rn(__fmul_rn(r0, sn.x), __fmul_rn(i0, cs.x)));
+            v.y = pack2(__fsub_rn(__fmul_rn(r1, cs.y), __fmul_rn(i1, sn.y)),
+                        __fadd_rn(__fmul_rn(r1, sn.y), __fmul_rn(i1, cs.y)));
+        }
+        if (pool) {
+            acc[0] = __fadd_rn(acc[0], __uint_as_float(v.x << 16));
+            acc[1] = __fadd_rn(acc[1], __uint_as_float(v.x & 0xFFFF0000u));
+            acc[2] = __fadd_rn(acc[2], __uint_as_float(v.y << 16));
+            acc[3] = __fadd_rn(acc[3], __uint_as_float(v.y & 0xFFFF0000u));
+        }
+        return v;
+    }
 };
+
 template <>
-struct Lane4<0> {
+struct LaneOps<0> {
     using V = float4;
+    static __device__ __forceinline__ void load_w(const void* wt, uint32_t* wsm, int C) {
+        for (int c = threadIdx.x; c < C; c += kPrepThreads) wsm[c] = static_cast<const uint32_t*>(wt)[c];
+    }
+    static __device__ __forceinline__ float sumsq(const V& v, float ss) {
+        ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+        ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+        ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+        return __fadd_rn(ss, __fmul_rn(v.w, v.w));
+    }
+    static __device__ __forceinline__ V apply(V v, bool norm, float inv, const uint32_t* wsm, int wbase, bool rope,
+                                              float2 cs, float2 sn, bool pool, float* acc) {
+        if (norm) {
+            const float4 w = *reinterpret_cast<const float4*>(wsm + wbase);
+            v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
+        }
+        if (rope) {
+            const float r0 = v.x, i0 = v.y, r1 = v.z, i1 = v.w;
+            v.x = __fsub_rn(__fmul_rn(r0, cs.x), __fmul_rn(i0, sn.x));
+            v.y = __fadd_rn(__fmul_rn(r0, sn.x), __fmul_rn(i0, cs.x));
+            v.z = __fsub_rn(__fmul_rn(r1, cs.y), __fmul_rn(i1, sn.y));
+            v.w = __fadd_rn(__fmul_rn(r1, sn.y), __fmul_rn(i1, cs.y));
+        }
+        if (pool) {
+            acc[0] = __fadd_rn(acc[0], v.x);
+            acc[1] = __fadd_rn(acc[1], v.y);
+            acc[2] = __fadd_rn(acc[2], v.z);
+            acc[3] = __fadd_rn(acc[3], v.w);
+        }
+        return v;
+    }
 };
-
-__device__ __forceinline__ void unpack4(const uint2& v, float f[4]) {
-    f[0] = bf16_bits_to_float(v.x & 0xFFFFu);
-    f[1] = bf16_bits_to_float(v.x >> 16);
-    f[2] = bf16_bits_to_float(v.y & 0xFFFFu);
-    f[3] = bf16_bits_to_float(v.y >> 16);
-}
-__device__ __forceinline__ void unpack4(const float4& v, float f[4]) {
-    f[0] = v.x;
-    f[1] = v.y;
-    f[2] = v.z;
-    f[3] = v.w;
-}
-// f holds values of the storage type already (to_t), so the bf16 packing keeps the high halves exactly.
-__device__ __forceinline__ void pack4(const float f[4], uint2& v) {
-    v.x = (__float_as_uint(f[0]) >> 16) | (__float_as_uint(f[1]) & 0xFFFF0000u);
-    v.y = (__float_as_uint(f[2]) >> 16) | (__float_as_uint(f[3]) & 0xFFFF0000u);
-}
-__device__ __forceinline__ void pack4(const float f[4], float4& v) { v = make_float4(f[0], f[1], f[2], f[3]); }
-
-template <int DT>
-__device__ __forceinline__ float to_t(float x) {  // round to the storage type (nearest even)
-    if constexpr (DT == 1)
-        return __bfloat162float(__float2bfloat16_rn(x));
-    else
-        return x;
-}
 
 template <int DT, int NH>
 __global__ void __launch_bounds__(kPrepThreads) prepare_kernel(const __grid_constant__ PrepArgs a) {
-    using V = typename Lane4<DT>::V;
+    using Ops = LaneOps<DT>;
+    using V = typename Ops::V;
     __shared__ float part[4][kPrepMaxC];
-    __shared__ float wsm[kPrepMaxC];
+    __shared__ __align__(16) uint32_t wsm[kPrepMaxC];
     griddep_wait_then_release();
     if (a.zero) {
         const size_t nb = (size_t)gridDim.x * gridDim.y, bid = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
@@ -77,73 +133,57 @@ __global__ void __launch_bounds__(kPrepThreads) prepare_kernel(const __grid_cons
     const int heads = a.heads, C = heads * kD, cv = C / 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const void* wt = role < 2 ? a.norm_w[role] : nullptr;
+    const bool norm = wt != nullptr;
     const bool rope = role < 2 && a.cosv != nullptr;
     float* pooled = role < 2 ? a.pooled[role] : nullptr;
-    if (wt) {  // CTA-uniform
-        for (int c = threadIdx.x; c < C; c += kPrepThreads)
-            wsm[c] = DT == 1 ? bf16_bits_to_float(static_cast<const uint16_t*>(wt)[c]) : static_cast<const float*>(wt)[c];
+    if (norm) {  // CTA-uniform
+        Ops::load_w(wt, wsm, C);
         __syncthreads();
     }
     const int64_t blk = role == 0 ? (int64_t)win : (int64_t)kv_phys_block(a.kv_pages, win);
-    const V* src = static_cast<const V*>(a.x[role]);
-    V* dst = static_cast<V*>(role == 0 ? a.q_out : a.kv_out[role - 1]) + blk * kBlock * cv;
+    const V* src = static_cast<const V*>(a.x[role]) + lane;
+    V* dst = static_cast<V*>(role == 0 ? a.q_out : a.kv_out[role - 1]) + blk * kBlock * cv + lane;
     float acc[4 * NH];
 #pragma unroll
     for (int i = 0; i < 4 * NH; ++i) acc[i] = 0.0f;
 
-#pragma unroll 1
-    for (int t = 0; t < 32; ++t) {
-        const int r = 32 * warp + t;
-        const int64_t tok = token_row(a.bh, a.bw, win, r);
-        V raw[NH];
+    // software pipeline: the next token's row and table entries load while this token is computed
+    V nxt[NH];
+    float2 ncs = make_float2(1.0f, 1.0f), nsn = make_float2(0.0f, 0.0f);
+    auto load = [&](int t) {
+        const int64_t tok = token_row(a.bh, a.bw, win, 32 * warp + t);
 #pragma unroll
         for (int i = 0; i < NH; ++i)
-            if (i < heads) raw[i] = __ldcs(src + tok * cv + 32 * i + lane);
-        float2 cs = make_float2(1.0f, 1.0f), sn = make_float2(0.0f, 0.0f);
+            if (i < heads) nxt[i] = __ldcs(src + tok * cv + 32 * i);
         if (rope) {
-            cs = __ldg(reinterpret_cast<const float2*>(a.cosv + tok * 64) + lane);
-            sn = __ldg(reinterpret_cast<const float2*>(a.sinv + tok * 64) + lane);
+            ncs = __ldg(reinterpret_cast<const float2*>(a.cosv + tok * 64) + lane);
+            nsn = __ldg(reinterpret_cast<const float2*>(a.sinv + tok * 64) + lane);
         }
+    };
+    load(0);
+#pragma unroll 1
+    for (int t = 0; t < 32; ++t) {
+        V cur[NH];
+#pragma unroll
+        for (int i = 0; i < NH; ++i) cur[i] = nxt[i];
+        const float2 cs = ncs, sn = nsn;
+        if (t + 1 < 32) load(t + 1);
         float inv = 1.0f;
-        if (wt) {
+        if (norm) {
             float ss = 0.0f;
 #pragma unroll
             for (int i = 0; i < NH; ++i)
-                if (i < heads) {
-                    float f[4];
-                    unpack4(raw[i], f);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
-                }
+                if (i < heads) ss = Ops::sumsq(cur[i], ss);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
             inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)C), a.eps));
         }
+        V* drow = dst + (int64_t)(32 * warp + t) * cv;
 #pragma unroll
         for (int i = 0; i < NH; ++i)
-            if (i < heads) {
-                float f[4];
-                unpack4(raw[i], f);
-                if (wt) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        f[e] = to_t<DT>(__fmul_rn(to_t<DT>(__fmul_rn(f[e], inv)), wsm[kD * i + 4 * lane + e]));
-                }
-                if (rope) {
-                    const float r0 = f[0], i0 = f[1], r1 = f[2], i1 = f[3];
-                    f[0] = to_t<DT>(__fsub_rn(__fmul_rn(r0, cs.x), __fmul_rn(i0, sn.x)));
-                    f[1] = to_t<DT>(__fadd_rn(__fmul_rn(r0, sn.x), __fmul_rn(i0, cs.x)));
-                    f[2] = to_t<DT>(__fsub_rn(__fmul_rn(r1, cs.y), __fmul_rn(i1, sn.y)));
-                    f[3] = to_t<DT>(__fadd_rn(__fmul_rn(r1, sn.y), __fmul_rn(i1, cs.y)));
-                }
-                if (pooled) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[4 * i + e] = __fadd_rn(acc[4 * i + e], f[e]);
-                }
-                V o;
-                pack4(f, o);
-                dst[(int64_t)r * cv + 32 * i + lane] = o;
-            }
+            if (i < heads)
+                drow[32 * i] = Ops::apply(cur[i], norm, inv, wsm, kD * i + 4 * lane, rope, cs, sn, pooled != nullptr,
+                                          acc + 4 * i);
     }
 
     if (pooled) {  // CTA-uniform
