@@ -37,15 +37,11 @@ struct LaneOps<1> {
     static __device__ __forceinline__ void load_w(const void* wt, uint32_t* wsm, int C) {
         for (int c = threadIdx.x; c < C / 2; c += kPrepThreads) wsm[c] = static_cast<const uint32_t*>(wt)[c];
     }
-    static __device__ __forceinline__ float sumsq(const V& v, float ss) {
-        const float x[4] = {__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
-                            __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u)};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
-        return ss;
+    static __device__ __forceinline__ float2 unpack2(uint32_t w) {  // bf16 pair → (low, high) as fp32
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
     }
-    static __device__ __forceinline__ uint32_t pack2(float a, float b) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    static __device__ __forceinline__ uint32_t pack2(float2 f) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
         return *reinterpret_cast<const uint32_t*>(&h);
     }
     static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
@@ -53,28 +49,36 @@ struct LaneOps<1> {
                                          *reinterpret_cast<const __nv_bfloat162*>(&b));
         return *reinterpret_cast<const uint32_t*>(&h);
     }
+    // squares as fp32x2 products (each rounded like a scalar multiply), added one by one in channel order
+    static __device__ __forceinline__ float sumsq(const V& v, float ss) {
+        const float2 x01 = unpack2(v.x), x23 = unpack2(v.y);
+        const float2 p01 = __fmul2_rn(x01, x01), p23 = __fmul2_rn(x23, x23);
+        ss = __fadd_rn(ss, p01.x);
+        ss = __fadd_rn(ss, p01.y);
+        ss = __fadd_rn(ss, p23.x);
+        return __fadd_rn(ss, p23.y);
+    }
+    // one rotation pair: (re·c − im·s, re·s + im·c) with every product and sum rounded to fp32
+    static __device__ __forceinline__ float2 rotate(float2 x, float c, float s) {
+        const float2 a = __fmul2_rn(x, make_float2(c, s)), b = __fmul2_rn(x, make_float2(s, c));
+        return make_float2(__fsub_rn(a.x, a.y), __fadd_rn(b.x, b.y));
+    }
     static __device__ __forceinline__ V apply(V v, bool norm, float inv, const uint32_t* wsm, int wbase, bool rope,
                                               float2 cs, float2 sn, bool pool, float* acc) {
         if (norm) {
             const uint2 w = *reinterpret_cast<const uint2*>(wsm + wbase / 2);
-            v.x = mul2(pack2(__fmul_rn(__uint_as_float(v.x << 16), inv),
-                             __fmul_rn(__uint_as_float(v.x & 0xFFFF0000u), inv)), w.x);
-            v.y = mul2(pack2(__fmul_rn(__uint_as_float(v.y << 16), inv),
-                             __fmul_rn(__uint_as_float(v.y & 0xFFFF0000u), inv)), w.y);
+            const float2 iv = make_float2(inv, inv);
+            v.x = mul2(pack2(__fmul2_rn(unpack2(v.x), iv)), w.x);
+            v.y = mul2(pack2(__fmul2_rn(unpack2(v.y), iv)), w.y);
         }
         if (rope) {
-            const float r0 = __uint_as_float(v.x << 16), i0 = __uint_as_float(v.x & 0xFFFF0000u);
-            const float r1 = __uint_as_float(v.y << 16), i1 = __uint_as_float(v.y & 0xFFFF0000u);
-            v.x = pack2(__fsub_rn(__fmul_rn(r0, cs.x), __fmul_rn(i0, sn.x)),
-                        __fadd_rn(__fmul_rn(r0, sn.x), __fmul_rn(i0, cs.x)));
-            v.y = pack2(__fsub_rn(__fmul_rn(r1, cs.y), __fmul_rn(i1, sn.y)),
-                        __fadd_rn(__fmul_rn(r1, sn.y), __fmul_rn(i1, cs.y)));
+            v.x = pack2(rotate(unpack2(v.x), cs.x, sn.x));
+            v.y = pack2(rotate(unpack2(v.y), cs.y, sn.y));
         }
         if (pool) {
-            acc[0] = __fadd_rn(acc[0], __uint_as_float(v.x << 16));
-            acc[1] = __fadd_rn(acc[1], __uint_as_float(v.x & 0xFFFF0000u));
-            acc[2] = __fadd_rn(acc[2], __uint_as_float(v.y << 16));
-            acc[3] = __fadd_rn(acc[3], __uint_as_float(v.y & 0xFFFF0000u));
+            float2* a2 = reinterpret_cast<float2*>(acc);
+            a2[0] = __fadd2_rn(a2[0], unpack2(v.x));
+            a2[1] = __fadd2_rn(a2[1], unpack2(v.y));
         }
         return v;
     }
