@@ -199,8 +199,9 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
  *
  * Rounding points (the reference's, with its order of operations): WanRMSNorm (DiT.swift:34-47)
  *   ss = Σ_c x_c² in fp32, inv = 1/√(ss / C + eps) correctly rounded, n = T(x·inv), y = T(n·w)
- * where Σ runs as 32 lane partials (lane l sums x² over channels 128·i + 4l .. 4l + 3 for i = 0..H−1 in order) combined
- * by a butterfly v_l += v_{l^o}, o = 16, 8, 4, 2, 1 (MLX's reduction order is unspecified; this is the library's);
+ * where Σ runs as 32 lane partials combined by a butterfly v_l += v_{l^o}, o = 16, 8, 4, 2, 1; lane l's partial is
+ * (s0 + s1) + (s2 + s3) with s_e = the sum of x² over channels 128·i + 4l + e for i = 0..H−1 in order (MLX's reduction
+ * order is unspecified; this is the library's);
  * ropeApply (DiT.swift:100-107) on each head's pairs (2j, 2j+1) with the token's (cos_j, sin_j):
  *   re' = T(re·cos − im·sin), im' = T(re·sin + im·cos), every product and sum rounded to fp32;
  * T = the storage type (bf16 round-to-nearest-even, or fp32).

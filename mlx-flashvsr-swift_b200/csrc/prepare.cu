@@ -12,8 +12,9 @@
 // HBM-bound: algorithmic bytes per window = 3·128·C·elt read + 3·128·C·elt written + 2·128·64·8 rotation tables read
 // (q and k) + 2·C·4 pooled written.
 // Layout: CTA = one window of one tensor (blockIdx.y: 0 q, 1 k, 2 v); warp g walks tokens [32g, 32g + 32) of the
-// window in window order; lane l holds channels 128·i + 4l .. 4l + 3 of every head i, so one token's sum of squares
-// is a lane partial plus a five-step butterfly (every lane ends with the same value: a + b = b + a), both rotation
+// window in window order; lane l holds channels 128·i + 4l + e (e = 0..3) of every head i, so one token's sum of
+// squares is a lane partial — four chains s_e over the heads, combined (s0 + s1) + (s2 + s3) — plus a five-step
+// butterfly (every lane ends with the same value: a + b = b + a), both rotation
 // pairs of a lane use the lane's two table entries j = 2l, 2l + 1, and a warp moves 256 contiguous bytes (bf16) of a
 // head per instruction.
 #include "common.cuh"
@@ -49,14 +50,13 @@ struct LaneOps<1> {
                                          *reinterpret_cast<const __nv_bfloat162*>(&b));
         return *reinterpret_cast<const uint32_t*>(&h);
     }
-    // squares as fp32x2 products (each rounded like a scalar multiply), added one by one in channel order
-    static __device__ __forceinline__ float sumsq(const V& v, float ss) {
+    // the lane's four channel chains (s0, s1) and (s2, s3), each adding this head's square as fp32x2 operations. The
+    // compiler may fuse such a product and sum into one fp32x2 FMA; the square of a bf16 value is exact in fp32, so
+    // fused or not the sum rounds the same.
+    static __device__ __forceinline__ void sumsq(const V& v, float2& s01, float2& s23) {
         const float2 x01 = unpack2(v.x), x23 = unpack2(v.y);
-        const float2 p01 = __fmul2_rn(x01, x01), p23 = __fmul2_rn(x23, x23);
-        ss = __fadd_rn(ss, p01.x);
-        ss = __fadd_rn(ss, p01.y);
-        ss = __fadd_rn(ss, p23.x);
-        return __fadd_rn(ss, p23.y);
+        s01 = __fadd2_rn(s01, __fmul2_rn(x01, x01));
+        s23 = __fadd2_rn(s23, __fmul2_rn(x23, x23));
     }
     // one rotation pair: (re·c − im·s, re·s + im·c) with every product and sum rounded to fp32
     static __device__ __forceinline__ float2 rotate(float2 x, float c, float s) {
@@ -90,11 +90,12 @@ struct LaneOps<0> {
     static __device__ __forceinline__ void load_w(const void* wt, uint32_t* wsm, int C) {
         for (int c = threadIdx.x; c < C; c += kPrepThreads) wsm[c] = static_cast<const uint32_t*>(wt)[c];
     }
-    static __device__ __forceinline__ float sumsq(const V& v, float ss) {
-        ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
-        ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
-        ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
-        return __fadd_rn(ss, __fmul_rn(v.w, v.w));
+    // fp32 squares are not exact: scalar multiply and add, which are never fused
+    static __device__ __forceinline__ void sumsq(const V& v, float2& s01, float2& s23) {
+        s01.x = __fadd_rn(s01.x, __fmul_rn(v.x, v.x));
+        s01.y = __fadd_rn(s01.y, __fmul_rn(v.y, v.y));
+        s23.x = __fadd_rn(s23.x, __fmul_rn(v.z, v.z));
+        s23.y = __fadd_rn(s23.y, __fmul_rn(v.w, v.w));
     }
     static __device__ __forceinline__ V apply(V v, bool norm, float inv, const uint32_t* wsm, int wbase, bool rope,
                                               float2 cs, float2 sn, bool pool, float* acc) {
@@ -174,10 +175,11 @@ __global__ void __launch_bounds__(kPrepThreads) prepare_kernel(const __grid_cons
         if (t + 1 < 32) load(t + 1);
         float inv = 1.0f;
         if (norm) {
-            float ss = 0.0f;
+            float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int i = 0; i < NH; ++i)
-                if (i < heads) ss = Ops::sumsq(cur[i], ss);
+                if (i < heads) Ops::sumsq(cur[i], s01, s23);
+            float ss = __fadd_rn(__fadd_rn(s01.x, s01.y), __fadd_rn(s23.x, s23.y));
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
             inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)C), a.eps));

@@ -180,8 +180,9 @@ static inline float orc_round_t(float x, int dtype) { return dtype ? orc_bf16_to
 /* x (F·H·W, C = heads·128) in token order (row (f·H + y)·W + x), dtype 0 fp32 / 1 bf16 → out, same shape and dtype,
  * in window order (window (f/2, y/8, x/8), token (f%2, y%8, x%8)). weight: (C) in dtype, or NULL for no norm; cosv /
  * sinv: (F·H·W, 64) fp32 rows per token, or NULL for no rotation. T = the storage type.
- *   norm  : ss = Σ x² as 32 partials — partial l sums x·x over channels 128·i + 4l + e for i = 0..heads−1, e = 0..3 in
- *           that order — combined by the butterfly v[l] = v[l] + v[l ^ o] for o = 16, 8, 4, 2, 1 (all l at once);
+ *   norm  : ss = Σ x² as 32 partials — partial l = (s0 + s1) + (s2 + s3), s_e summing x·x over channels
+ *           128·i + 4l + e for i = 0..heads−1 in order — combined by the butterfly v[l] = v[l] + v[l ^ o] for
+ *           o = 16, 8, 4, 2, 1 (all l at once);
  *           inv = 1/√(ss / C + eps) correctly rounded (evaluated in double); n = T(x·inv); y = T(n·w)
  *           (DiT.swift:44-45: normalise in fp32, cast to T, times the weight).
  *   rotate: for each head, pair (2j, 2j+1) = (re, im): re' = T(re·cos_j − im·sin_j), im' = T(re·sin_j + im·cos_j)
@@ -200,13 +201,13 @@ int orc_prepare(const void* x, int dtype, int f, int h, int w, int heads, const 
         if (weight) {
             float v[32], t[32];
             for (int l = 0; l < 32; ++l) {
-                float acc = 0.0f;
+                float se[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 for (int i = 0; i < heads; ++i)
                     for (int e = 0; e < 4; ++e) {
                         const float xv = row[ORC_D * i + 4 * l + e];
-                        acc = acc + xv * xv;
+                        se[e] = se[e] + xv * xv;
                     }
-                v[l] = acc;
+                v[l] = (se[0] + se[1]) + (se[2] + se[3]);
             }
             for (int o = 16; o > 0; o >>= 1) {
                 for (int l = 0; l < 32; ++l) t[l] = v[l] + v[l ^ o];
