@@ -227,6 +227,40 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
                                      void* out, int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
                                      fvsr_stream_t stream);
 
+/* ---- Streaming driver: the LCSA side of FlashVSR's chunk loop ----
+ * Mirrors FlashVSRPipeline.chunk / FlashVSRDiT.step (Pipeline.swift:95-102, 112-131; DiT.swift:472-485, 554-578) for
+ * the self-attention of `layers` DiT blocks at an output size out_h × out_w (multiples of 128; spatial blocks
+ * bh = out_h/128, bw = out_w/128):
+ *   - chunk k covers latents [0, 6) for k = 0 (3 temporal slices), [4 + 2k, 6 + 2k) after (1 slice);
+ *   - RoPE temporal start t0 = the chunk's first latent; tables as RopeTables (DiT.swift:52-97), built on the device;
+ *   - topk = Int(Double(s²)·topk_ratio) − 1 (DiT.swift:482), topk_ratio <= 0 → 2·768·1280 / (out_h·out_w)
+ *     (Pipeline.swift:68); kvLen = Int(kv_ratio) (Pipeline.swift:129); local range as given (default 11);
+ *   - one window K/V cache per block (DiT.swift:507-511, 532-538). */
+typedef struct fvsr_stream fvsr_stream;
+
+/* Geometry of chunk k without a device: the layer params (kv_slices = q_slices; the caches set it per call) and the
+ * chunk's latent range [latent_begin, latent_end) (latent_begin is the RoPE t0). Host only. */
+fvsr_status fvsr_stream_chunk_geometry(int32_t heads, int32_t out_h, int32_t out_w, int32_t dtype, double topk_ratio,
+                                       int32_t local_range, int32_t k, fvsr_lcsa_params* p, int32_t* latent_begin,
+                                       int32_t* latent_end);
+/* Allocates the caches (kvLen + 3 slice pages each) and the rotation tables. */
+fvsr_status fvsr_stream_create(int32_t heads, int32_t out_h, int32_t out_w, int32_t layers, int32_t dtype,
+                               double topk_ratio, double kv_ratio, int32_t local_range, fvsr_stream** s);
+fvsr_status fvsr_stream_destroy(fvsr_stream* s);
+/* A new clip (FlashVSRPipeline.begin, Pipeline.swift:105-108): empties every cache; the next chunk is 0. Host only. */
+fvsr_status fvsr_stream_begin(fvsr_stream* s);
+/* Workspace bytes fvsr_stream_layer needs for every chunk of this stream. */
+fvsr_status fvsr_stream_workspace_size(const fvsr_stream* s, size_t* bytes);
+/* Starts chunk k (k = 0, 1, 2, … in order after fvsr_stream_begin): builds its RoPE tables on `stream`. */
+fvsr_status fvsr_stream_start_chunk(fvsr_stream* s, int32_t k, fvsr_stream_t stream);
+/* Device pointers to the current chunk's (tokens, 64) fp32 RoPE tables. */
+fvsr_status fvsr_stream_rope(const fvsr_stream* s, const float** rope_cos, const float** rope_sin, int64_t* tokens);
+/* Self-attention of block `layer` in the current chunk: fvsr_lcsa_forward_tokens with the chunk's geometry and
+ * tables and that block's cache. q_lin/k_lin/v_lin: (tokens, H·128) token order; out: (tokens, H·128) token order. */
+fvsr_status fvsr_stream_layer(fvsr_stream* s, int32_t layer, const void* q_lin, const void* k_lin, const void* v_lin,
+                              const void* norm_q, const void* norm_k, float eps, void* q_win, void* out,
+                              void* workspace, size_t workspace_bytes, fvsr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

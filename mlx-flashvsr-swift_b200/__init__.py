@@ -31,6 +31,8 @@ EXPORTED = [
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
     "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range", "fvsr_lcsa_item_order", "fvsr_lcsa_schedule_size",
     "fvsr_lcsa_schedule", "fvsr_lcsa_attention_scheduled", "fvsr_lcsa_prepare", "fvsr_lcsa_forward_tokens",
+    "fvsr_stream_chunk_geometry", "fvsr_stream_create", "fvsr_stream_destroy", "fvsr_stream_begin",
+    "fvsr_stream_workspace_size", "fvsr_stream_start_chunk", "fvsr_stream_rope", "fvsr_stream_layer",
 ]
 
 
@@ -96,6 +98,16 @@ def lib() -> ctypes.CDLL:
         "fvsr_lcsa_prepare": ([PP, P, P, P, P, P, ctypes.c_float, P, P, P, P, P, P, P, P], ctypes.c_int),
         "fvsr_lcsa_forward_tokens": ([PP, P, P, P, P, P, ctypes.c_float, P, P, P, P, P, P, P, P, SZ, P],
                                      ctypes.c_int),
+        "fvsr_stream_chunk_geometry": ([I32, I32, I32, I32, ctypes.c_double, I32, I32, PP, ctypes.POINTER(I32),
+                                        ctypes.POINTER(I32)], ctypes.c_int),
+        "fvsr_stream_create": ([I32, I32, I32, I32, I32, ctypes.c_double, ctypes.c_double, I32, ctypes.POINTER(P)],
+                               ctypes.c_int),
+        "fvsr_stream_destroy": ([P], ctypes.c_int),
+        "fvsr_stream_begin": ([P], ctypes.c_int),
+        "fvsr_stream_workspace_size": ([P, ctypes.POINTER(SZ)], ctypes.c_int),
+        "fvsr_stream_start_chunk": ([P, I32, P], ctypes.c_int),
+        "fvsr_stream_rope": ([P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(I64)], ctypes.c_int),
+        "fvsr_stream_layer": ([P, I32, P, P, P, P, P, ctypes.c_float, P, P, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -572,6 +584,92 @@ def lcsa_forward_tokens(q_lin, k_lin, v_lin, cache: KVCache, geom: Geometry, nor
                                           _ptr(cos), _ptr(sin), cache.handle, _ptr(q_win), _ptr(out), _ptr(kidx),
                                           _ptr(kcnt), _ptr(ws), ws.numel(), _stream(stream)))
     return out
+
+
+def chunk_geometry(k: int, heads: int, out_h: int, out_w: int, dtype: int = FVSR_BF16, topk_ratio: float = 0.0,
+                   local_range: int = 11):
+    """The step geometry of streaming chunk k (Pipeline.swift:95-102, DiT.swift:478-485), host only:
+    (Geometry, latent_begin, latent_end); latent_begin is the chunk's RoPE temporal start t0."""
+    p = Params()
+    b, e = ctypes.c_int32(0), ctypes.c_int32(0)
+    _check(lib().fvsr_stream_chunk_geometry(heads, out_h, out_w, dtype, float(topk_ratio), local_range, k,
+                                            ctypes.byref(p), ctypes.byref(b), ctypes.byref(e)))
+    g = Geometry(heads=p.heads, bh=p.bh, bw=p.bw, q_slices=p.q_slices, kv_slices=p.kv_slices,
+                 local_range=p.local_range, topk=p.topk, dtype=p.dtype)
+    return g, int(b.value), int(e.value)
+
+
+class _DeviceArray:
+    """An fp32 device buffer of the library, seen by torch through __cuda_array_interface__ (copied, never written)."""
+
+    def __init__(self, ptr: int, shape: tuple):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 2,
+                                         "strides": None}
+
+
+class Stream:
+    """The LCSA side of FlashVSR's chunk loop (FlashVSRPipeline.chunk / FlashVSRDiT.step, Pipeline.swift:95-131,
+    DiT.swift:554-578) for `layers` DiT blocks at an output size out_h × out_w: chunk schedule, RoPE tables per chunk,
+    topk, kvLen = int(kv_ratio), one window cache per block. Call begin(), then for k = 0, 1, …: start_chunk(k) and
+    layer(i, q, k, v, norm_q, norm_k) for each block i."""
+
+    def __init__(self, heads: int, out_h: int, out_w: int, layers: int, dtype: int = FVSR_BF16,
+                 topk_ratio: float = 0.0, kv_ratio: float = 3.0, local_range: int = 11):
+        h = ctypes.c_void_p()
+        _check(lib().fvsr_stream_create(heads, out_h, out_w, layers, dtype, float(topk_ratio), float(kv_ratio),
+                                        local_range, ctypes.byref(h)))
+        self.handle = h
+        self.heads, self.out_h, self.out_w, self.layers, self.dtype = heads, out_h, out_w, layers, dtype
+        self.topk_ratio, self.local_range = topk_ratio, local_range
+        self.chunk = -1
+        n = ctypes.c_size_t(0)
+        _check(lib().fvsr_stream_workspace_size(self.handle, ctypes.byref(n)))
+        self.workspace = _torch().empty(int(n.value), dtype=_torch().uint8, device="cuda")
+
+    def close(self):
+        if self.handle:
+            lib().fvsr_stream_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def begin(self):
+        _check(lib().fvsr_stream_begin(self.handle))
+        self.chunk = -1
+
+    def geometry(self, k: int):
+        return chunk_geometry(k, self.heads, self.out_h, self.out_w, self.dtype, self.topk_ratio, self.local_range)
+
+    def start_chunk(self, k: int, stream=None):
+        _check(lib().fvsr_stream_start_chunk(self.handle, k, _stream(stream)))
+        self.chunk = k
+
+    def rope(self):
+        """The current chunk's (tokens, 64) fp32 RoPE tables, copied out of the stream."""
+        torch = _torch()
+        c, s, n = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int64(0)
+        _check(lib().fvsr_stream_rope(self.handle, ctypes.byref(c), ctypes.byref(s), ctypes.byref(n)))
+        out = []
+        for ptr in (c, s):
+            view = _DeviceArray(ptr.value, (int(n.value), 64))
+            out.append(torch.as_tensor(view, device="cuda").clone())
+        return tuple(out)
+
+    def layer(self, i: int, q_lin, k_lin, v_lin, norm_q=None, norm_k=None, eps: float = 1e-6, q_win=None, out=None,
+              stream=None):
+        torch = _torch()
+        g, _, _ = self.geometry(self.chunk)
+        (q, k, v), _, _ = _token_inputs(g, q_lin, k_lin, v_lin, norm_q, norm_k, None)
+        q_win = torch.empty_like(q) if q_win is None else q_win
+        out = torch.empty_like(q) if out is None else out
+        _check(lib().fvsr_stream_layer(self.handle, i, _ptr(q), _ptr(k), _ptr(v), _ptr(norm_q), _ptr(norm_k), eps,
+                                       _ptr(q_win), _ptr(out), _ptr(self.workspace), self.workspace.numel(),
+                                       _stream(stream)))
+        return out
 
 
 def device_check(stream=None) -> None:

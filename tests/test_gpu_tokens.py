@@ -123,3 +123,36 @@ def test_forward_tokens_equals_the_window_path(fvsr, orc, dev, dtype):
     cache_a.close()
     cache_b.close()
     fvsr.device_check()
+
+
+@pytest.mark.parametrize("kv_ratio", [3.0, 1.0])
+def test_stream_driver_equals_manual_layers(fvsr, dev, kv_ratio):
+    """The C++ chunk driver (fvsr_stream_*) over three chunks and two blocks against the same layers called by hand:
+    the reference's schedule (chunk 0: 3 slices, then 1; t0 = 0, then 4 + 2k), its RoPE tables (checked against
+    rope_tables), topk and kvLen, one cache per block — outputs bit-identical."""
+    heads, out_h, out_w, layers = 2, 256, 384, 2
+    st = fvsr.Stream(heads, out_h, out_w, layers, kv_ratio=kv_ratio)
+    st.begin()
+    kv_len = int(kv_ratio)
+    held = 0
+    caches = [fvsr.KVCache(st.geometry(0)[0], kv_len=kv_len, max_new_slices=3) for _ in range(layers)]
+    for chunk in range(3):
+        g, t0, t1 = st.geometry(chunk)
+        st.start_chunk(chunk)
+        cos, sin = st.rope()
+        ref_cos, ref_sin = fvsr.rope_tables(t1 - t0, out_h // 16, out_w // 16, t0=t0)
+        assert (cos - ref_cos).abs().max().item() <= 1e-7 and (sin - ref_sin).abs().max().item() <= 1e-7
+        for i in range(layers):
+            q, k, v, wq, wk = linear_outputs(g, "bf16", 900 + 10 * chunk + i)
+            got = st.layer(i, q, k, v, norm_q=wq, norm_k=wk, eps=1e-6)
+            want = fvsr.lcsa_forward_tokens(q, k, v, caches[i], g, norm_q=wq, norm_k=wk, eps=1e-6, rope=(cos, sin))
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), f"chunk {chunk} layer {i}"
+        # DiT.swift:532-538: after a chunk, drop the oldest slice once if more than kvLen are held
+        held = (0 if chunk == 0 else held) + g.q_slices
+        held -= 1 if held > kv_len else 0
+        assert all(c.slices == held for c in caches)
+    for c in caches:
+        c.close()
+    st.close()
+    fvsr.device_check()
