@@ -652,6 +652,80 @@ def run_prepare(args):
                                  "dtype": cfg.dtype}}), flush=True)
 
 
+def run_stream(args):
+    """Whole chunks through the streaming driver (fvsr_stream_*): the reference's chunk loop for `layers` DiT blocks at
+    the config's output size with the reference's defaults (top-k ratio 2·768·1280/(H·W), kvRatio 3, range 11) —
+    each layer from its linear outputs (token order) to the attention output (token order). Synthetic linear outputs
+    per layer (three rotated sets); chunk 0 (3 slices) and then steady chunks (1 slice against kvLen + 1)."""
+    import torch
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[args.config]
+    out_h, out_w = cfg.bh * 128, cfg.bw * 128
+    layers = args.layers or cfg.layers
+    st = pkg.Stream(cfg.heads, out_h, out_w, layers, pkg.FVSR_BF16 if cfg.dtype == "bf16" else pkg.FVSR_F32)
+    st.begin()
+    dt = torch.bfloat16 if cfg.dtype == "bf16" else torch.float32
+    gen = torch.Generator(device="cuda").manual_seed(2468)
+    C = cfg.heads * 128
+    sets = []
+    for chunk_kind in (0, 1):
+        g = st.geometry(chunk_kind)[0]
+        L = g.nq * 128
+        sets.append([[torch.randn((L, C), generator=gen, device="cuda").to(dt) for _ in range(3)] for _ in range(3)])
+    norms = [[(1.0 + 0.1 * torch.randn((C,), generator=gen, device="cuda")).to(dt) for _ in range(2)]
+             for _ in range(layers)]
+    outs = [torch.empty((st.geometry(k)[0].nq * 128, C), dtype=dt, device="cuda") for k in (0, 1)]
+    qwin = [torch.empty_like(o) for o in outs]
+    kcnts = [torch.zeros((layers, cfg.heads, st.geometry(k)[0].nq), dtype=torch.int32, device="cuda") for k in (0, 1)]
+    kept = {}
+
+    def chunk(k):
+        kind = 0 if k == 0 else 1
+        g = st.geometry(k)[0]
+        st.start_chunk(k)
+        for i in range(layers):
+            q, kk, v = sets[kind][i % 3]
+            st.layer(i, q, kk, v, norm_q=norms[i][0], norm_k=norms[i][1], eps=1e-6, q_win=qwin[kind],
+                     out=outs[kind], kcnt=kcnts[kind][i])
+        return g
+
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.synchronize()
+    e[0].record()
+    g0 = chunk(0)
+    e[1].record()
+    torch.cuda.synchronize()
+    ms0 = e[0].elapsed_time(e[1])
+    kept[0] = int(kcnts[0].sum().item())
+    k = 1
+    for _ in range(max(args.warmup, 3)):
+        chunk(k)
+        k += 1
+    n = max(args.steps, 1)
+    torch.cuda.synchronize()
+    e[0].record()
+    for _ in range(n):
+        g1 = chunk(k)
+        k += 1
+    e[1].record()
+    torch.cuda.synchronize()
+    pkg.device_check()
+    ms1 = e[0].elapsed_time(e[1]) / n
+    kept[1] = int(kcnts[1].sum().item())
+    st.close()
+    fl = cfgs.kept_flops
+    print(json.dumps({"metric": f"streaming chunk through the driver, config {args.config} output size, reference "
+                                "defaults", "value": fl(kept[1]) / (ms1 * 1e-3) / 1e12, "unit": "TFLOP/s",
+                      "ms_per_chunk": ms1, "chunks_timed": n, "layers": layers,
+                      "chunk0": {"ms": ms0, "q_slices": g0.q_slices, "kept_triples": kept[0],
+                                 "tflops": fl(kept[0]) / (ms0 * 1e-3) / 1e12},
+                      "steady": {"q_slices": g1.q_slices, "kv_slices": "kvLen 3 + the current slice", "topk": g1.topk,
+                                 "kept_triples_per_chunk": kept[1]},
+                      "launch": "host C-ABI calls per layer (fvsr_stream_layer), no graph",
+                      "config": {"workload": f"{out_w}x{out_h} output, {cfg.heads} heads, topk ratio default",
+                                 "dtype": cfg.dtype}}), flush=True)
+
+
 def graph_time_us(fn, n, warmup):
     """Device µs per call of fn (which launches on the current stream): n calls captured once in a CUDA graph, the
     graph replayed after warm-up, CUDA events around the replays."""
@@ -700,7 +774,12 @@ def main():
                     help="measure the window cache's in-place append (HBM GB/s) instead of the layer step")
     ap.add_argument("--prepare", action="store_true",
                     help="measure the token-order q/k/v pass (HBM GB/s) and the token-order layer")
+    ap.add_argument("--stream", action="store_true",
+                    help="run whole chunks through the streaming driver (reference chunk loop and defaults)")
     args = ap.parse_args()
+    if args.stream:
+        run_stream(args)
+        return
     if args.kv_append:
         run_kv_append(args)
         return

@@ -256,10 +256,12 @@ fvsr_status fvsr_stream_start_chunk(fvsr_stream* s, int32_t k, fvsr_stream_t str
 /* Device pointers to the current chunk's (tokens, 64) fp32 RoPE tables. */
 fvsr_status fvsr_stream_rope(const fvsr_stream* s, const float** rope_cos, const float** rope_sin, int64_t* tokens);
 /* Self-attention of block `layer` in the current chunk: fvsr_lcsa_forward_tokens with the chunk's geometry and
- * tables and that block's cache. q_lin/k_lin/v_lin: (tokens, H·128) token order; out: (tokens, H·128) token order. */
+ * tables and that block's cache. q_lin/k_lin/v_lin: (tokens, H·128) token order; out: (tokens, H·128) token order;
+ * kidx / kcnt: optional selection outputs as in fvsr_lcsa_forward_tokens (NULL → kept in the workspace). */
 fvsr_status fvsr_stream_layer(fvsr_stream* s, int32_t layer, const void* q_lin, const void* k_lin, const void* v_lin,
                               const void* norm_q, const void* norm_k, float eps, void* q_win, void* out,
-                              void* workspace, size_t workspace_bytes, fvsr_stream_t stream);
+                              int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                              fvsr_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -107,7 +107,7 @@ def lib() -> ctypes.CDLL:
         "fvsr_stream_workspace_size": ([P, ctypes.POINTER(SZ)], ctypes.c_int),
         "fvsr_stream_start_chunk": ([P, I32, P], ctypes.c_int),
         "fvsr_stream_rope": ([P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(I64)], ctypes.c_int),
-        "fvsr_stream_layer": ([P, I32, P, P, P, P, P, ctypes.c_float, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_stream_layer": ([P, I32, P, P, P, P, P, ctypes.c_float, P, P, P, P, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -660,15 +660,15 @@ class Stream:
         return tuple(out)
 
     def layer(self, i: int, q_lin, k_lin, v_lin, norm_q=None, norm_k=None, eps: float = 1e-6, q_win=None, out=None,
-              stream=None):
+              kidx=None, kcnt=None, stream=None):
         torch = _torch()
         g, _, _ = self.geometry(self.chunk)
         (q, k, v), _, _ = _token_inputs(g, q_lin, k_lin, v_lin, norm_q, norm_k, None)
         q_win = torch.empty_like(q) if q_win is None else q_win
         out = torch.empty_like(q) if out is None else out
         _check(lib().fvsr_stream_layer(self.handle, i, _ptr(q), _ptr(k), _ptr(v), _ptr(norm_q), _ptr(norm_k), eps,
-                                       _ptr(q_win), _ptr(out), _ptr(self.workspace), self.workspace.numel(),
-                                       _stream(stream)))
+                                       _ptr(q_win), _ptr(out), _ptr(kidx), _ptr(kcnt), _ptr(self.workspace),
+                                       self.workspace.numel(), _stream(stream)))
         return out
 
 

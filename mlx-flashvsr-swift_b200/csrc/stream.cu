@@ -250,7 +250,8 @@ fvsr_status fvsr_stream_rope(const fvsr_stream* s, const float** rope_cos, const
 
 fvsr_status fvsr_stream_layer(fvsr_stream* s, int32_t layer, const void* q_lin, const void* k_lin, const void* v_lin,
                               const void* norm_q, const void* norm_k, float eps, void* q_win, void* out,
-                              void* workspace, size_t workspace_bytes, fvsr_stream_t stream) {
+                              int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                              fvsr_stream_t stream) {
     if (!s) return sfail(FVSR_EINVAL, "stream is NULL");
     if (s->chunk < 0) return sfail(FVSR_EINVAL, "no chunk started (fvsr_stream_start_chunk)");
     if (layer < 0 || layer >= s->layers) return sfail(FVSR_EINVAL, "layer out of range");
@@ -259,7 +260,7 @@ fvsr_status fvsr_stream_layer(fvsr_stream* s, int32_t layer, const void* q_lin, 
                                      &p, nullptr, nullptr);
     if (st != FVSR_OK) return st;
     return fvsr_lcsa_forward_tokens(&p, q_lin, k_lin, v_lin, norm_q, norm_k, eps, s->rope,
-                                    s->rope + (size_t)s->max_tokens * 64, s->caches[layer], q_win, out, nullptr, nullptr,
+                                    s->rope + (size_t)s->max_tokens * 64, s->caches[layer], q_win, out, kidx, kcnt,
                                     workspace, workspace_bytes, stream);
 }
 
