@@ -4,7 +4,7 @@
 //   abi_driver cpu   host-side validation only (no GPU needed): every bad argument returns its status before any
 //                    launch, with a message in fvsr_last_error().
 //   abi_driver gpu   a small LCSA layer on the device: selection (with and without a workspace), attention, the
-//                    streaming forward over a window cache, and fvsr_device_check.
+//                    streaming forward over a window cache, the streaming driver, and fvsr_device_check.
 // Prints one line per failed check and exits non-zero if any failed.
 #include <cuda_runtime.h>
 
@@ -120,6 +120,37 @@ static int run_cpu() {
     EXPECT_STATUS(fvsr_lcsa_forward(&p, ok_ptr, ok_ptr, ok_ptr, nullptr, ok_ptr, nullptr, nullptr, ok_ptr, bytes,
                                     nullptr),
                   FVSR_EINVAL);
+    // token-order entry points: host checks before any launch
+    {
+        fvsr_lcsa_params b = p;
+        b.heads = 17;
+        EXPECT_STATUS(fvsr_lcsa_prepare(&b, ok_ptr, ok_ptr, ok_ptr, nullptr, nullptr, 1e-6f, nullptr, nullptr, ok_ptr,
+                                        ok_ptr, ok_ptr, nullptr, nullptr, nullptr),
+                      FVSR_EUNSUPPORTED);
+        EXPECT_STATUS(fvsr_lcsa_prepare(&p, ok_ptr, ok_ptr, ok_ptr, nullptr, nullptr, 1e-6f, (const float*)ok_ptr,
+                                        nullptr, ok_ptr, ok_ptr, ok_ptr, nullptr, nullptr, nullptr),
+                      FVSR_EINVAL);
+        EXPECT_STATUS(fvsr_lcsa_forward_tokens(&p, ok_ptr, ok_ptr, ok_ptr, nullptr, nullptr, 1e-6f, nullptr, nullptr,
+                                               nullptr, ok_ptr, ok_ptr, nullptr, nullptr, ok_ptr, bytes, nullptr),
+                      FVSR_EINVAL);
+    }
+    // streaming driver: the reference's chunk schedule and topk rule, host only
+    {
+        fvsr_lcsa_params g;
+        int32_t b = -1, e = -1;
+        EXPECT_STATUS(fvsr_stream_chunk_geometry(12, 1152, 1920, FVSR_BF16, 0.0, 11, 0, &g, &b, &e), FVSR_OK);
+        CHECK(b == 0 && e == 6 && g.q_slices == 3 && g.bh == 9 && g.bw == 15 && g.topk == 16199);
+        EXPECT_STATUS(fvsr_stream_chunk_geometry(12, 1152, 1920, FVSR_BF16, 0.0, 11, 5, &g, &b, &e), FVSR_OK);
+        CHECK(b == 14 && e == 16 && g.q_slices == 1);
+        EXPECT_STATUS(fvsr_stream_chunk_geometry(12, 1000, 1920, FVSR_BF16, 0.0, 11, 0, &g, &b, &e), FVSR_EINVAL);
+        EXPECT_STATUS(fvsr_stream_chunk_geometry(12, 1152, 1920, FVSR_BF16, 0.0, 11, 0, nullptr, &b, &e), FVSR_EINVAL);
+        EXPECT_STATUS(fvsr_stream_create(12, 1152, 1920, 30, FVSR_BF16, 0.0, 3.0, 11, nullptr), FVSR_EINVAL);
+        fvsr_stream* st = nullptr;
+        EXPECT_STATUS(fvsr_stream_create(12, 1152, 1920, 30, FVSR_BF16, 0.0, 0.5, 11, &st), FVSR_EINVAL);
+        CHECK(st == nullptr);
+        EXPECT_STATUS(fvsr_stream_begin(nullptr), FVSR_EINVAL);
+        EXPECT_STATUS(fvsr_stream_destroy(nullptr), FVSR_OK);
+    }
     return g_failed;
 }
 
@@ -229,6 +260,58 @@ static int run_gpu() {
         cudaMemcpy(hc2.data(), kcnt2, hc.size() * 4, cudaMemcpyDeviceToHost);
         CHECK(hc == hc2);
         EXPECT_STATUS(fvsr_kv_cache_destroy(cache), FVSR_OK);
+    }
+    // streaming driver: two chunks of one block from token-order linear outputs (q, k, v reused as such)
+    {
+        fvsr_stream* drv = nullptr;
+        const int out_h = p.bh * 128, out_w = p.bw * 128;
+        EXPECT_STATUS(fvsr_stream_create(p.heads, out_h, out_w, 1, FVSR_BF16, 0.0, 2.0, p.local_range, &drv), FVSR_OK);
+        size_t dws = 0;
+        if (drv) EXPECT_STATUS(fvsr_stream_workspace_size(drv, &dws), FVSR_OK);
+        void* dw = nullptr;
+        uint16_t *qwin = nullptr, *tout = nullptr;
+        int32_t* tcnt = nullptr;
+        const size_t l0 = (size_t)3 * s * 128;  // chunk 0: three slices
+        cudaMalloc(&dw, dws);
+        cudaMalloc(&qwin, l0 * C * 2);
+        cudaMalloc(&tout, l0 * C * 2);
+        cudaMalloc(&tcnt, sizeof(int32_t) * p.heads * 3 * s);
+        CHECK(drv && dw && qwin && tout && tcnt);
+        uint16_t* q0 = to_device(bf16_values(l0 * C, 11));
+        uint16_t* k0 = to_device(bf16_values(l0 * C, 12));
+        uint16_t* v0 = to_device(bf16_values(l0 * C, 13));
+        EXPECT_STATUS(fvsr_stream_layer(drv, 0, q0, k0, v0, nullptr, nullptr, 1e-6f, qwin, tout, nullptr, tcnt, dw, dws,
+                                        fs),
+                      FVSR_EINVAL);  // no chunk started
+        EXPECT_STATUS(fvsr_stream_begin(drv), FVSR_OK);
+        EXPECT_STATUS(fvsr_stream_start_chunk(drv, 1, fs), FVSR_EINVAL);  // chunks run in order
+        for (int chunk = 0; chunk < 2; ++chunk) {
+            EXPECT_STATUS(fvsr_stream_start_chunk(drv, chunk, fs), FVSR_OK);
+            EXPECT_STATUS(fvsr_stream_layer(drv, 0, q0, k0, v0, nullptr, nullptr, 1e-6f, qwin, tout, nullptr, tcnt, dw,
+                                            dws, fs),
+                          FVSR_OK);
+            EXPECT_STATUS(fvsr_stream_layer(drv, 1, q0, k0, v0, nullptr, nullptr, 1e-6f, qwin, tout, nullptr, tcnt, dw,
+                                            dws, fs),
+                          FVSR_EINVAL);  // one block only
+            EXPECT_STATUS(fvsr_device_check(fs), FVSR_OK);
+            const size_t rows = (size_t)(chunk == 0 ? 3 : 1) * s * 128;
+            std::vector<uint16_t> to(rows * C);
+            cudaMemcpy(to.data(), tout, to.size() * 2, cudaMemcpyDeviceToHost);
+            for (size_t i = 0; i < to.size(); i += 89) {
+                const uint32_t bits = (uint32_t)to[i] << 16;
+                float f;
+                std::memcpy(&f, &bits, 4);
+                CHECK(std::isfinite(f) && std::fabs(f) <= 2.0f);
+            }
+        }
+        EXPECT_STATUS(fvsr_stream_destroy(drv), FVSR_OK);
+        cudaFree(dw);
+        cudaFree(qwin);
+        cudaFree(tout);
+        cudaFree(tcnt);
+        cudaFree(q0);
+        cudaFree(k0);
+        cudaFree(v0);
     }
     cudaStreamDestroy(st);
     cudaFree(q);
