@@ -68,6 +68,12 @@ const char* fvsr_last_error(void);
  * Metal kernel has no waits); this is the host side of the library's bounded device waits. */
 fvsr_status fvsr_device_check(fvsr_stream_t stream);
 
+/* Diagnostic of the failure path, no reference counterpart: launches one kernel whose single thread runs the
+ * library's bounded device wait (the one every attention wait uses) on a barrier that nothing completes, with a limit
+ * of limit_us microseconds (1 .. 4,000,000). The wait gives up, records the device timeout and the kernel returns;
+ * the next fvsr_device_check reports FVSR_ETIMEOUT and the context stays usable. Nothing faults or hangs. */
+fvsr_status fvsr_wait_probe(uint32_t limit_us, fvsr_stream_t stream);
+
 /* Bytes of workspace that fvsr_lcsa_select, fvsr_lcsa_attention_mask and fvsr_lcsa_forward need for `p`
  * (the maximum of the three). */
 fvsr_status fvsr_lcsa_workspace_size(const fvsr_lcsa_params* p, size_t* bytes);

@@ -25,7 +25,8 @@ FVSR_OK, FVSR_EINVAL, FVSR_ECUDA, FVSR_ETIMEOUT, FVSR_ENOMEM, FVSR_EUNSUPPORTED 
 FVSR_F32, FVSR_BF16 = 0, 1
 
 EXPORTED = [
-    "fvsr_version", "fvsr_status_string", "fvsr_last_error", "fvsr_device_check", "fvsr_lcsa_workspace_size",
+    "fvsr_version", "fvsr_status_string", "fvsr_last_error", "fvsr_device_check", "fvsr_wait_probe",
+    "fvsr_lcsa_workspace_size",
     "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
@@ -75,6 +76,7 @@ def lib() -> ctypes.CDLL:
         "fvsr_status_string": ([ctypes.c_int], ctypes.c_char_p),
         "fvsr_last_error": ([], ctypes.c_char_p),
         "fvsr_device_check": ([P], ctypes.c_int),
+        "fvsr_wait_probe": ([ctypes.c_uint32, P], ctypes.c_int),
         "fvsr_lcsa_workspace_size": ([PP, ctypes.POINTER(SZ)], ctypes.c_int),
         "fvsr_lcsa_pool": ([PP, P, I64, P, P], ctypes.c_int),
         "fvsr_lcsa_select": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
@@ -670,6 +672,12 @@ class Stream:
                                        _ptr(q_win), _ptr(out), _ptr(kidx), _ptr(kcnt), _ptr(self.workspace),
                                        self.workspace.numel(), _stream(stream)))
         return out
+
+
+def wait_probe(limit_us: int, stream=None) -> None:
+    """Runs one bounded device wait that nothing completes (fvsr_wait_probe); the next device_check raises
+    FVSRError(FVSR_ETIMEOUT). The failure path of the attention kernels' waits, exercised without a fault."""
+    _check(lib().fvsr_wait_probe(int(limit_us), _stream(stream)))
 
 
 def device_check(stream=None) -> None:

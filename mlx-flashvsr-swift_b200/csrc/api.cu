@@ -259,6 +259,14 @@ fvsr_status fvsr_device_check(fvsr_stream_t stream) {
     return flag ? fail(FVSR_ETIMEOUT, "a device-side wait hit its limit; the kernel returned early") : FVSR_OK;
 }
 
+fvsr_status fvsr_wait_probe(uint32_t limit_us, fvsr_stream_t stream) {
+    if (limit_us < 1 || limit_us > 4000000) return fail(FVSR_EINVAL, "limit_us must be in [1, 4000000]");
+    fvsr_status s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    FVSR_CU(launch_wait_probe((uint64_t)limit_us * 1000u, reinterpret_cast<cudaStream_t>(stream)), "wait probe launch");
+    return FVSR_OK;
+}
+
 fvsr_status fvsr_lcsa_workspace_size(const fvsr_lcsa_params* p, size_t* bytes) {
     Dims d;
     fvsr_status s = check_params(p, &d);

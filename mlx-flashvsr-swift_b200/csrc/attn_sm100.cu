@@ -396,6 +396,32 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     return launch_pdl(attn_bf16_sm100_kernel, dim3(item_count), dim3(kThreads), smem, st, mq, mk, mv, a);
 }
 
+namespace {
+
+// The failure path of the bounded waits, without a fault: one thread waits, with mbar_wait and the attention kernel's
+// timeout word, on an mbarrier whose single expected arrival never comes. The wait gives up after limit_ns, raises
+// the CTA abort word and the device timeout word, and the kernel returns normally.
+__global__ void wait_probe_kernel(uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t abort_word;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_word = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        mbar_wait(smem_u32(&bar), 0, reinterpret_cast<volatile uint32_t*>(&abort_word), &g_fvsr_timeout, limit_ns);
+    __syncthreads();
+}
+
+}  // namespace
+
+cudaError_t launch_wait_probe(uint64_t limit_ns, cudaStream_t st) {
+    wait_probe_kernel<<<1, 32, 0, st>>>(limit_ns);
+    return cudaGetLastError();
+}
+
 cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st) {
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return e;

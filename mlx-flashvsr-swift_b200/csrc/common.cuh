@@ -142,6 +142,8 @@ cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int i
                               cudaStream_t st);
 // Reads and clears the persistent kernel's timeout word of the current device.
 cudaError_t read_and_clear_persist_error(int* flag);
+// One bounded wait that runs out (fvsr_wait_probe): sets the device timeout word after limit_ns, faults nothing.
+cudaError_t launch_wait_probe(uint64_t limit_ns, cudaStream_t st);
 // Reads and clears the device-side timeout words of the current device (1 if a wait gave up since the last read).
 cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st);
 

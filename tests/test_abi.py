@@ -122,3 +122,9 @@ def test_token_order_entry_points_check_arguments_on_host(fvsr):
     assert L.fvsr_lcsa_prepare(ctypes.byref(p), *bad) == fvsr.FVSR_EINVAL
     assert L.fvsr_lcsa_forward_tokens(ctypes.byref(p), fake, fake, fake, None, None, ctypes.c_float(1e-6), None, None,
                                       None, fake, fake, None, None, fake, 1 << 20, None) == fvsr.FVSR_EINVAL
+
+
+def test_wait_probe_limit_checked_on_host(fvsr):
+    L = fvsr.lib()
+    assert L.fvsr_wait_probe(0, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_wait_probe(4_000_001, None) == fvsr.FVSR_EINVAL
