@@ -428,29 +428,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-bool make_map_p(CUtensorMap* map, const void* base, int64_t rows, int64_t channels) {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return false;
-        fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)channels * 2};
-    const cuuint32_t box[2] = {64, 128};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 cudaError_t read_and_clear_persist_error(int* flag) {
@@ -471,8 +448,8 @@ cudaError_t launch_attn_bf16_persist(const void* q, const void* k, const void* v
     if (!L.persistent) return cudaErrorInvalidValue;  // the buffer holds no persistent partition
     CUtensorMap mq, mk, mv;
     const int64_t channels = (int64_t)heads * kD;
-    if (!make_map_p(&mq, q, (int64_t)nq * kBlock, channels) || !make_map_p(&mk, k, kv_rows, channels) ||
-        !make_map_p(&mv, v, kv_rows, channels))
+    if (!make_tile_map(&mq, q, (int64_t)nq * kBlock, channels) || !make_tile_map(&mk, k, kv_rows, channels) ||
+        !make_tile_map(&mv, v, kv_rows, channels))
         return cudaErrorInvalidValue;
     cudaError_t e =
         cudaFuncSetAttribute(attn_bf16_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);

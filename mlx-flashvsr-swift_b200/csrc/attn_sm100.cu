@@ -21,8 +21,6 @@
 // Shared memory: Q 32 KB + K 3 × 32 KB + V 2 × 32 KB, each tile as two 128-row × 64-column boxes in the 128-byte
 // swizzled layout that TMA writes and the MMA descriptors read.
 // Every wait is bounded (4 s); on expiry the kernel raises a device timeout word that fvsr_device_check reports.
-#include <mutex>
-
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -335,36 +333,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
-// 2-D map over a (rows, channels) bf16 matrix, box = 128 rows × 64 channels, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t channels) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)channels, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)channels * 2};
-    const cuuint32_t box[2] = {64, 128};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 size_t attn_bf16_smem_bytes(int nk) { return 1024 + kOffList + sizeof(int32_t) * (size_t)nk; }
@@ -375,8 +343,8 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     if (item_count <= 0) return cudaSuccess;
     CUtensorMap mq, mk, mv;
     const int64_t channels = (int64_t)heads * kD;
-    if (!make_map(&mq, q, (int64_t)nq * kBlock, channels) || !make_map(&mk, k, kv_rows, channels) ||
-        !make_map(&mv, v, kv_rows, channels))
+    if (!make_tile_map(&mq, q, (int64_t)nq * kBlock, channels) || !make_tile_map(&mk, k, kv_rows, channels) ||
+        !make_tile_map(&mv, v, kv_rows, channels))
         return cudaErrorInvalidValue;
     const size_t smem = attn_bf16_smem_bytes(nk);
     cudaError_t e = cudaFuncSetAttribute(attn_bf16_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
