@@ -537,6 +537,8 @@ def _token_inputs(geom: Geometry, q_lin, k_lin, v_lin, norm_q, norm_k, rope):
     for t in ts:
         if t.shape != (rows, geom.channels):
             raise FVSRError(FVSR_EINVAL, f"linear outputs must be ({rows}, {geom.channels}), got {tuple(t.shape)}")
+        if _dtype_code(t) != geom.dtype:
+            raise FVSRError(FVSR_EINVAL, "q, k and v must all be in the geometry's dtype")
     for wt in (norm_q, norm_k):
         if wt is not None and (wt.dtype != ts[0].dtype or tuple(wt.shape) != (geom.channels,) or not wt.is_contiguous()
                                or not wt.is_cuda):
