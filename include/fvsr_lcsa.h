@@ -16,8 +16,8 @@
  *   - All pointers are device pointers unless stated; the caller owns every buffer.
  *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = the legacy default stream) and never
  *     synchronises, except where noted.
- *   - No call allocates device memory except fvsr_kv_cache_create. Scratch comes from a caller-provided workspace
- *     whose size fvsr_lcsa_workspace_size reports.
+ *   - No call allocates device memory except fvsr_kv_cache_create and fvsr_stream_create. Scratch comes from a
+ *     caller-provided workspace whose size fvsr_lcsa_workspace_size (fvsr_stream_workspace_size) reports.
  *   - Errors are returned, never trapped: FVSR_EINVAL for bad shapes / NULL pointers (checked on the host before any
  *     launch), FVSR_ECUDA for a failed launch, FVSR_ETIMEOUT when a device-side wait gave up (reported by
  *     fvsr_device_check). fvsr_last_error() returns a message for the calling thread's last failure.
