@@ -58,6 +58,8 @@ def linear_outputs(g, dtype, seed):
     ("bf16", 16, 2, 2, 1, False, True),
     ("bf16", 2, 3, 2, 2, False, False),
     ("f32", 8, 2, 2, 1, True, True),
+    ("f32", 16, 2, 2, 1, True, True),     # the 16-head fp32 instantiation
+    ("bf16", 12, 2, 3, 3, True, True),    # a chunk-0 shape: three temporal slices
 ])
 def test_prepare_matches_oracle(fvsr, orc, dev, dtype, heads, bh, bw, q_slices, norm, rope):
     g = fvsr.Geometry(heads=heads, bh=bh, bw=bw, q_slices=q_slices, kv_slices=q_slices, local_range=11,
