@@ -215,6 +215,8 @@ __global__ void __launch_bounds__(256) select_scores_kernel(const float* __restr
         }
     }
     __syncthreads();
+    // a warp covers tile rows [8·warp, 8·warp + 8): past the last query block it has nothing to write
+    if (i0 + 8 * (tid >> 5) >= nq) return;
     const int ty = tid >> 4, tx = tid & 15;
     float acc[4][4];
 #pragma unroll
