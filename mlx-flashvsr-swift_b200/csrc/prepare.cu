@@ -9,14 +9,15 @@
 // K and V go to the arena blocks a KvPages table names: the pages of a window cache (the append of DiT.swift:508-511
 // fused into this pass) or one contiguous window-ordered buffer.
 //
-// HBM-bound: algorithmic bytes per window = 3·128·C·elt read + 3·128·C·elt written + 2·128·64·8 rotation tables read
-// (q and k) + 2·C·4 pooled written.
+// HBM-bound in bytes: per window 3·128·C·elt read + 3·128·C·elt written + 128·64·8 rotation-table bytes (read by the
+// q and the k CTA) + 2·C·4 pooled written. With few windows (135 at 1920×1152) it is latency-bound instead: 4 warps per
+// CTA, each walking its tokens in order.
 // Layout: CTA = one window of one tensor (blockIdx.y: 0 q, 1 k, 2 v); warp g walks tokens [32g, 32g + 32) of the
-// window in window order; lane l holds channels 128·i + 4l + e (e = 0..3) of every head i, so one token's sum of
-// squares is a lane partial — four chains s_e over the heads, combined (s0 + s1) + (s2 + s3) — plus a five-step
-// butterfly (every lane ends with the same value: a + b = b + a), both rotation
-// pairs of a lane use the lane's two table entries j = 2l, 2l + 1, and a warp moves 256 contiguous bytes (bf16) of a
-// head per instruction.
+// window in window order, loading the next token's row while it computes the current one; lane l holds channels
+// 128·i + 4l + e (e = 0..3) of every head i, so one token's sum of squares is a lane partial — four chains s_e over
+// the heads, combined (s0 + s1) + (s2 + s3) — plus a five-step butterfly (every lane ends with the same value:
+// a + b = b + a), both rotation pairs of a lane use the lane's two table entries j = 2l, 2l + 1, and a warp moves 256
+// contiguous bytes (bf16) of a head per instruction.
 #include "common.cuh"
 
 namespace fvsr {
