@@ -12,7 +12,7 @@ Swift/MLX, Sources/FlashVSRMLX/DiT.swift:158-174), so these hold a float64 numpy
 operation by operation (mean, matmul / sqrt(d), local mask, softmax, sort, strict threshold). They cross-check the
 oracle's fixed-order fp32 restatement on inputs whose pooled scores are well separated (config-2 style block offsets).
 
-Usage:  python tests/golden/make_golden.py [--reference PATH_TO_REFERENCE_TREE]
+Usage:  python tests/golden/make_golden.py --reference PATH_TO_REFERENCE_TREE
 """
 from __future__ import annotations
 
@@ -103,7 +103,7 @@ def allowed_per_row(bh, bw, q_slices, kv_slices, r):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="the xocialize/mlx-flashvsr-swift source tree")
     args = ap.parse_args()
     spec = importlib.util.spec_from_file_location("ref_block_sparse_attn",
                                                   Path(args.reference) / "oracle" / "block_sparse_attn.py")
