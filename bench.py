@@ -753,14 +753,16 @@ def graph_time_us(fn, n, warmup):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", type=int, default=3)
-    ap.add_argument("--layers", type=int, default=30)
-    ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gpus", type=int, default=1, help="GPUs of the run (one process per GPU under torchrun)")
+    ap.add_argument("--steps", type=int, default=5, help="timed steps (one step = one 30-layer chunk)")
+    ap.add_argument("--warmup", type=int, default=3, help="untimed warm-up steps (at least 3)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"],
+                    help="ours: the CUDA path; reference: the CPU arm (the oracle port on the host cores)")
+    ap.add_argument("--config", type=int, default=3, help="workload 1-5 (configs.py); 3 = the metric's chunk")
+    ap.add_argument("--layers", type=int, default=30, help="layer calls per step")
+    ap.add_argument("--e2e-steps", type=int, default=2,
+                    help="steps of the end-to-end measurement through the C ABI with host buffers (0 = skip)")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip timing the CPU oracle on a sample")
     ap.add_argument("--as-rank", default=None, metavar="R/N",
                     help="development: one GPU times rank R's share of an N-way sharded run (no process group)")
     ap.add_argument("--no-split", action="store_true",
