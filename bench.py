@@ -484,7 +484,9 @@ def run_ours(args):
                        **({"schedule": "persistent equal shares" if persistent else "longest-first items"}
                           if shard else {})},
             "ms_per_layer": ms / layers,
-            "breakdown_ms_per_layer": {"attention": att_avg, "pool+select": sel_ms},
+            # "rest" = step time per layer minus the attention kernel timed alone: pooling, selection and the
+            # dependency gaps between the kernels of the graph
+            "breakdown_ms_per_layer": {"attention": att_avg, "rest (pool, select, gaps)": sel_ms},
             "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
                          "unit": "TFLOP/s", "frac": att_tflops / peak, "peak_kind": f"{peak_kind} bf16 burst",
                          "traffic": (tr or {}).get("bytes_per_launch"),
