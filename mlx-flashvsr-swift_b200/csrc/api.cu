@@ -65,20 +65,28 @@ fvsr_status check_params(const fvsr_lcsa_params* p, Dims* d, bool need_kv = true
     if (p->local_range < 1) return fail(FVSR_EINVAL, "local_range must be >= 1, got %d", p->local_range);
     if (p->topk < 0) return fail(FVSR_EINVAL, "topk must be >= 0, got %d", p->topk);
     if (p->dtype != FVSR_F32 && p->dtype != FVSR_BF16) return fail(FVSR_EINVAL, "dtype must be FVSR_F32 or FVSR_BF16");
+    // block counts in 64 bits: a 32-bit product of large grid sizes could wrap around and pass the bounds below
+    const int64_t s64 = (int64_t)p->bh * p->bw;
+    const int64_t nq64 = s64 <= 65535 ? (int64_t)p->q_slices * s64 : INT64_MAX;
+    const int64_t nk64 = !need_kv ? 0 : s64 <= 65535 ? (int64_t)p->kv_slices * s64 : INT64_MAX;
+    if (nk64 > kMaxNk) return fail(FVSR_EUNSUPPORTED, "Nk = %lld key blocks exceeds the supported %d", (long long)nk64, kMaxNk);
+    if (nq64 > 65535 || (int64_t)p->heads * nq64 > (1ll << 30))
+        return fail(FVSR_EUNSUPPORTED, "Nq = %lld query blocks is too large", (long long)nq64);
     d->heads = p->heads;
-    d->s = p->bh * p->bw;
-    d->nq = p->q_slices * d->s;
+    d->s = (int)s64;
+    d->nq = (int)nq64;
     d->q_slices = p->q_slices;
-    d->nk = need_kv ? p->kv_slices * d->s : 0;
+    d->nk = (int)nk64;
     d->channels = (int64_t)p->heads * 128;
     d->elt = p->dtype == FVSR_BF16 ? 2 : 4;
-    if (d->nk > kMaxNk) return fail(FVSR_EUNSUPPORTED, "Nk = %d key blocks exceeds the supported %d", d->nk, kMaxNk);
-    if (d->nq > 65535 || (int64_t)d->heads * d->nq > (1ll << 30))
-        return fail(FVSR_EUNSUPPORTED, "Nq = %d query blocks is too large", d->nq);
     return FVSR_OK;
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Buffers of 4-byte elements (index lists, counts, orders, probabilities, fp32 masks, pooled rows, norm weights read
+// as 32-bit words) need that alignment; NULL passes (presence is checked separately).
+bool aligned4(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3u) == 0; }
 
 size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -111,6 +119,19 @@ Workspace layout(const Dims& d, void* base) {
     w.order = reinterpret_cast<int32_t*>(take((size_t)d.heads * d.nq * 4));
     w.bytes = off;
     return w;
+}
+
+// The caller's workspace: large enough for the layout, and 16-byte aligned (pooled rows are read as float4).
+fvsr_status check_workspace(const Workspace& w, const void* workspace, size_t workspace_bytes) {
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    if (!aligned16(workspace)) return fail(FVSR_EINVAL, "workspace must be 16-byte aligned");
+    return FVSR_OK;
+}
+
+fvsr_status check_lists(const int32_t* kidx, const int32_t* kcnt) {
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
+    return FVSR_OK;
 }
 
 // A contiguous K/V buffer: one page holding all nk blocks, so logical block j is physical block j.
@@ -217,6 +238,7 @@ fvsr_status check_prepare_inputs(const fvsr_lcsa_params* p, const Dims& d, const
     if (rope_cos && (!aligned16(rope_cos) || !aligned16(rope_sin)))
         return fail(FVSR_EINVAL, "rope_cos and rope_sin must be 16-byte aligned");
     if ((norm_q || norm_k) && !(eps >= 0.0f && eps < 1e30f)) return fail(FVSR_EINVAL, "eps must be finite and >= 0");
+    if (!aligned4(norm_q) || !aligned4(norm_k)) return fail(FVSR_EINVAL, "norm_q and norm_k must be 4-byte aligned");
     *a = PrepArgs{};
     a->x[0] = q_lin;
     a->x[1] = k_lin;
@@ -298,9 +320,12 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
     if (!q || (!k && !pooled_k) || !kidx || !kcnt) return fail(FVSR_EINVAL, "q, k (or pooled_k), kidx and kcnt are required");
     if (!aligned16(q) || (k && !aligned16(k)) || (pooled_k && !aligned16(pooled_k)))
         return fail(FVSR_EINVAL, "q, k and pooled_k must be 16-byte aligned");
+    s = check_lists(kidx, kcnt);
+    if (s != FVSR_OK) return s;
+    if (!aligned4(probs)) return fail(FVSR_EINVAL, "probs must be 4-byte aligned");
     Workspace w = layout(d, workspace);
-    if (!workspace || workspace_bytes < w.bytes)
-        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    s = check_workspace(w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const float* pk = pooled_k ? pooled_k : w.pooled_k;
     FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, pooled_k ? nullptr : k, pooled_k ? 0 : d.nk, w.pooled_k, p->dtype,
@@ -317,6 +342,8 @@ fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const 
     if (!q || !k || !v || !kidx || !kcnt || !out) return fail(FVSR_EINVAL, "q, k, v, kidx, kcnt and out are required");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
         return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
+    s = check_lists(kidx, kcnt);
+    if (s != FVSR_OK) return s;
     return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out,
                          reinterpret_cast<cudaStream_t>(stream));
 }
@@ -327,6 +354,7 @@ fvsr_status fvsr_lcsa_item_order(const fvsr_lcsa_params* p, const int32_t* kcnt,
     fvsr_status s = check_params(p, &d);
     if (s != FVSR_OK) return s;
     if (!kcnt || !order) return fail(FVSR_EINVAL, "kcnt and order are required");
+    if (!aligned4(kcnt) || !aligned4(order)) return fail(FVSR_EINVAL, "kcnt and order must be 4-byte aligned");
     const int64_t items = (int64_t)d.heads * d.nq;
     if (item_begin < 0 || item_count < 0 || (int64_t)item_begin + item_count > items)
         return fail(FVSR_EINVAL, "item range [%d, %d) is outside [0, %lld)", item_begin, item_begin + item_count,
@@ -345,6 +373,9 @@ fvsr_status fvsr_lcsa_attention_range(const fvsr_lcsa_params* p, const void* q, 
     if (!q || !k || !v || !kidx || !kcnt || !out) return fail(FVSR_EINVAL, "q, k, v, kidx, kcnt and out are required");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
         return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
+    s = check_lists(kidx, kcnt);
+    if (s != FVSR_OK) return s;
+    if (!aligned4(order)) return fail(FVSR_EINVAL, "order must be 4-byte aligned");
     const int64_t items = (int64_t)d.heads * d.nq;
     if (item_begin < 0 || item_count < 0 || (int64_t)item_begin + item_count > items)
         return fail(FVSR_EINVAL, "item range [%d, %d) is outside [0, %lld)", item_begin, item_begin + item_count,
@@ -387,12 +418,14 @@ fvsr_status fvsr_lcsa_schedule_size(const fvsr_lcsa_params* p, int32_t item_coun
 
 fvsr_status fvsr_lcsa_schedule(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin, int32_t item_count,
                                void* schedule, size_t schedule_bytes, fvsr_stream_t stream) {
+    // pointer checks first: the geometry query below reads the device
+    if (!kcnt || !schedule) return fail(FVSR_EINVAL, "kcnt and schedule are required");
+    if (!aligned16(schedule)) return fail(FVSR_EINVAL, "schedule must be 16-byte aligned");
+    if (!aligned4(kcnt)) return fail(FVSR_EINVAL, "kcnt must be 4-byte aligned");
     Dims d;
     fvsr::SchedLayout L;
     fvsr_status s = sched_geometry(p, &d, item_begin, item_count, &L);
     if (s != FVSR_OK) return s;
-    if (!kcnt || !schedule) return fail(FVSR_EINVAL, "kcnt and schedule are required");
-    if (!aligned16(schedule)) return fail(FVSR_EINVAL, "schedule must be 16-byte aligned");
     if (schedule_bytes < L.bytes)
         return fail(FVSR_ENOMEM, "schedule of %zu bytes is smaller than the %zu required", schedule_bytes, L.bytes);
     if (item_count == 0) return FVSR_OK;
@@ -408,14 +441,17 @@ fvsr_status fvsr_lcsa_attention_scheduled(const fvsr_lcsa_params* p, const void*
                                           const int32_t* kidx, const int32_t* kcnt, void* out, int32_t item_begin,
                                           int32_t item_count, const void* schedule, size_t schedule_bytes,
                                           fvsr_stream_t stream) {
-    Dims d;
-    fvsr::SchedLayout L;
-    fvsr_status s = sched_geometry(p, &d, item_begin, item_count, &L);
-    if (s != FVSR_OK) return s;
+    // pointer checks first: the geometry query below reads the device
     if (!q || !k || !v || !kidx || !kcnt || !out || !schedule)
         return fail(FVSR_EINVAL, "q, k, v, kidx, kcnt, out and schedule are required");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(schedule))
         return fail(FVSR_EINVAL, "q, k, v, out and schedule must be 16-byte aligned");
+    fvsr_status s = check_lists(kidx, kcnt);
+    if (s != FVSR_OK) return s;
+    Dims d;
+    fvsr::SchedLayout L;
+    s = sched_geometry(p, &d, item_begin, item_count, &L);
+    if (s != FVSR_OK) return s;
     if (schedule_bytes < L.bytes)
         return fail(FVSR_ENOMEM, "schedule of %zu bytes is smaller than the %zu required", schedule_bytes, L.bytes);
     if (item_count == 0) return FVSR_OK;
@@ -443,9 +479,10 @@ fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, c
     fvsr_status s = check_params(p, &d);
     if (s != FVSR_OK) return s;
     if (!block_mask) return fail(FVSR_EINVAL, "block_mask is required");
+    if (!aligned4(block_mask)) return fail(FVSR_EINVAL, "block_mask must be 4-byte aligned");
     Workspace w = layout(d, workspace);
-    if (!workspace || workspace_bytes < w.bytes)
-        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    s = check_workspace(w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     FVSR_CU(launch_mask_to_lists(block_mask, d.heads, d.nq, d.nk, w.kidx, w.kcnt, st), "mask to lists launch");
     FVSR_CU(launch_item_order(w.kcnt, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
@@ -569,14 +606,15 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
         return fail(FVSR_EINVAL, "params do not match the cache geometry");
     if (!q || !out) return fail(FVSR_EINVAL, "q and out are required");
     if (!aligned16(q) || !aligned16(out)) return fail(FVSR_EINVAL, "q and out must be 16-byte aligned");
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
     fvsr_lcsa_params pp = *p;
     pp.kv_slices = (int32_t)cache->pages.size() + p->q_slices;
     Dims d;
     fvsr_status s = check_params(&pp, &d);
     if (s != FVSR_OK) return s;
     Workspace w = layout(d, workspace);
-    if (!workspace || workspace_bytes < w.bytes)
-        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    s = check_workspace(w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     s = fvsr_kv_cache_append(cache, k_new, v_new, p->q_slices, stream);
     if (s != FVSR_OK) return s;
@@ -611,6 +649,7 @@ fvsr_status fvsr_lcsa_prepare(const fvsr_lcsa_params* p, const void* q_lin, cons
     if (!q_win || !k_win || !v_win) return fail(FVSR_EINVAL, "q_win, k_win and v_win are required");
     if (!aligned16(q_win) || !aligned16(k_win) || !aligned16(v_win))
         return fail(FVSR_EINVAL, "q_win, k_win and v_win must be 16-byte aligned");
+    if (!aligned4(pooled_q) || !aligned4(pooled_k)) return fail(FVSR_EINVAL, "pooled_q and pooled_k must be 4-byte aligned");
     s = check_device_sm100();
     if (s != FVSR_OK) return s;
     a.q_out = q_win;
@@ -634,6 +673,7 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
         return fail(FVSR_EINVAL, "params do not match the cache geometry");
     if (!q_win || !out) return fail(FVSR_EINVAL, "q_win and out are required");
     if (!aligned16(q_win) || !aligned16(out)) return fail(FVSR_EINVAL, "q_win and out must be 16-byte aligned");
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
     if (p->q_slices < 1 || (int)cache->pages.size() + p->q_slices > cache->capacity)
         return fail(FVSR_EINVAL, "appending %d slices to %zu exceeds the capacity %d", p->q_slices, cache->pages.size(),
                     cache->capacity);
@@ -646,8 +686,8 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
     s = check_prepare_inputs(&pp, d, q_lin, k_lin, v_lin, norm_q, norm_k, eps, rope_cos, rope_sin, &a);
     if (s != FVSR_OK) return s;
     Workspace w = layout(d, workspace);
-    if (!workspace || workspace_bytes < w.bytes)
-        return fail(FVSR_ENOMEM, "workspace of %zu bytes is smaller than the %zu required", workspace_bytes, w.bytes);
+    s = check_workspace(w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
     s = check_device_sm100();
     if (s != FVSR_OK) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

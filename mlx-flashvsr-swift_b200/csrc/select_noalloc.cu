@@ -64,6 +64,15 @@ extern "C" fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const
         set_last_error("q, k (or pooled_k), kidx, kcnt and probs are required");
         return FVSR_EINVAL;
     }
+    auto misaligned = [](const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) != 0; };
+    if (misaligned(q, 16) || misaligned(k, 16) || misaligned(pooled_k, 16)) {
+        set_last_error("q, k and pooled_k must be 16-byte aligned");
+        return FVSR_EINVAL;
+    }
+    if (misaligned(kidx, 4) || misaligned(kcnt, 4) || misaligned(probs, 4)) {
+        set_last_error("kidx, kcnt and probs must be 4-byte aligned");
+        return FVSR_EINVAL;
+    }
     const int s_blocks = p->bh * p->bw;
     const int64_t nq = (int64_t)p->q_slices * s_blocks, nk = (int64_t)p->kv_slices * s_blocks;
     const int64_t channels = (int64_t)p->heads * 128;

@@ -84,6 +84,53 @@ def test_misaligned_pointer_rejected(fvsr):
     assert b"aligned" in L.fvsr_last_error()
 
 
+@pytest.mark.parametrize("bh,bw,q_slices", [(65536, 65536, 1), (1 << 16, 1 << 15, 1), (2, 2, 2**31 - 1)])
+def test_huge_geometry_rejected_without_overflow(fvsr, bh, bw, q_slices):
+    """Block counts are formed in 64 bits: grids whose 32-bit product wraps (to zero or a negative count) are
+    rejected as unsupported, not accepted as tiny problems."""
+    g = fvsr.Geometry(heads=12, bh=bh, bw=bw, q_slices=q_slices, kv_slices=1, local_range=11, topk=10)
+    p = g.params()
+    n = ctypes.c_size_t(0)
+    assert fvsr.lib().fvsr_lcsa_workspace_size(ctypes.byref(p), ctypes.byref(n)) == 5   # FVSR_EUNSUPPORTED
+    assert b"too large" in fvsr.lib().fvsr_last_error() or b"exceeds" in fvsr.lib().fvsr_last_error()
+
+
+def test_misaligned_buffers_rejected_by_every_entry_point(fvsr):
+    """Every pointer a kernel dereferences is checked for its access width on the host: 16 bytes for rows, the
+    workspace and schedules; 4 bytes for index lists, counts, orders, probabilities, masks, pooled rows and norm weights.
+    The addresses are never dereferenced: each call fails its host check before any device call."""
+    L = fvsr.lib()
+    g = fvsr.Geometry(heads=2, bh=2, bw=2, q_slices=1, kv_slices=2, local_range=3, topk=3, dtype=fvsr.FVSR_BF16)
+    p = ctypes.byref(g.params())
+    ok = ctypes.c_void_p(1 << 20)
+    odd2 = ctypes.c_void_p((1 << 20) + 2)    # not 4-byte aligned
+    odd4 = ctypes.c_void_p((1 << 20) + 4)    # 4- but not 16-byte aligned
+    big = 1 << 30
+    n = g.heads * g.nq
+    eps = ctypes.c_float(1e-6)
+    calls = {
+        "select kidx": lambda: L.fvsr_lcsa_select(p, ok, ok, None, odd2, ok, None, None, ok, big, None),
+        "select probs": lambda: L.fvsr_lcsa_select(p, ok, ok, None, ok, ok, None, odd2, ok, big, None),
+        "select workspace": lambda: L.fvsr_lcsa_select(p, ok, ok, None, ok, ok, None, None, odd4, big, None),
+        "attention kcnt": lambda: L.fvsr_lcsa_attention(p, ok, ok, ok, ok, odd2, ok, None),
+        "range order": lambda: L.fvsr_lcsa_attention_range(p, ok, ok, ok, ok, ok, ok, 0, n, odd2, None),
+        "item order kcnt": lambda: L.fvsr_lcsa_item_order(p, odd2, 0, n, ok, None),
+        "schedule kcnt": lambda: L.fvsr_lcsa_schedule(p, odd2, 0, n, ok, big, None),
+        "scheduled kidx": lambda: L.fvsr_lcsa_attention_scheduled(p, ok, ok, ok, odd2, ok, ok, 0, n, ok, big, None),
+        "mask form mask": lambda: L.fvsr_lcsa_attention_mask(p, ok, ok, ok, odd2, ok, ok, big, None),
+        "mask form workspace": lambda: L.fvsr_lcsa_attention_mask(p, ok, ok, ok, ok, ok, odd4, big, None),
+        "noalloc kcnt": lambda: L.fvsr_lcsa_select_noalloc(p, ok, ok, None, ok, odd2, None, ok, None),
+        "noalloc q": lambda: L.fvsr_lcsa_select_noalloc(p, odd4, ok, None, ok, ok, None, ok, None),
+        "prepare norm": lambda: L.fvsr_lcsa_prepare(p, ok, ok, ok, odd2, None, eps, None, None, ok, ok, ok, None, None,
+                                                    None),
+        "prepare pooled": lambda: L.fvsr_lcsa_prepare(p, ok, ok, ok, None, None, eps, None, None, ok, ok, ok, odd2,
+                                                      None, None),
+    }
+    for name, call in calls.items():
+        assert call() == fvsr.FVSR_EINVAL, name
+        assert b"aligned" in L.fvsr_last_error(), (name, L.fvsr_last_error())
+
+
 def test_topk_formula_and_allowed_counts(fvsr):
     """DiT.swift:482 and the per-row allowed counts the configs translate their keep fractions with."""
     assert fvsr.Geometry.topk_from_ratio(60, 2.0) == 7199
