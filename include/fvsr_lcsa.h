@@ -14,6 +14,9 @@
  *
  * Conventions:
  *   - All pointers are device pointers unless stated; the caller owns every buffer.
+ *   - Alignment (checked on the host, FVSR_EINVAL otherwise): 16 bytes for token rows (q, k, v, out and their
+ *     token-order forms), pooled keys passed in, RoPE tables, the workspace and the schedule; 4 bytes for index lists,
+ *     counts, orders, probabilities, fp32 block masks, pooled rows written out and the RMSNorm weights.
  *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = the legacy default stream) and never
  *     synchronises, except where noted.
  *   - No call allocates device memory except fvsr_kv_cache_create and fvsr_stream_create. Scratch comes from a
