@@ -756,7 +756,9 @@ def graph_time_us(fn, n, warmup):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1, help="GPUs of the run (one process per GPU under torchrun)")
-    ap.add_argument("--steps", type=int, default=5, help="timed steps (one step = one 30-layer chunk)")
+    ap.add_argument("--steps", type=int, default=20,
+                    help="timed steps (one step = one 30-layer chunk; 20 keep the clock sampler inside the region "
+                         "for about ten samples)")
     ap.add_argument("--warmup", type=int, default=3, help="untimed warm-up steps (at least 3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"],
                     help="ours: the CUDA path; reference: the CPU arm (the oracle port on the host cores)")
