@@ -72,6 +72,13 @@ fvsr_status check_params(const fvsr_lcsa_params* p, Dims* d, bool need_kv = true
     if (nk64 > kMaxNk) return fail(FVSR_EUNSUPPORTED, "Nk = %lld key blocks exceeds the supported %d", (long long)nk64, kMaxNk);
     if (nq64 > 65535 || (int64_t)p->heads * nq64 > (1ll << 30))
         return fail(FVSR_EUNSUPPORTED, "Nq = %lld query blocks is too large", (long long)nq64);
+    // the selection pools the query and key blocks in one launch whose grid rows are blocks, and runs its radix
+    // passes with one grid row per (head, query slice): both at most 65535
+    if (nq64 + nk64 > 65535)
+        return fail(FVSR_EUNSUPPORTED, "Nq + Nk = %lld blocks is too large for one selection", (long long)(nq64 + nk64));
+    if (need_kv && (int64_t)p->heads * p->q_slices > 65535)
+        return fail(FVSR_EUNSUPPORTED, "heads x q_slices = %lld selection rows is too large",
+                    (long long)p->heads * p->q_slices);
     d->heads = p->heads;
     d->s = (int)s64;
     d->nq = (int)nq64;

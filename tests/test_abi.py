@@ -84,7 +84,8 @@ def test_misaligned_pointer_rejected(fvsr):
     assert b"aligned" in L.fvsr_last_error()
 
 
-@pytest.mark.parametrize("bh,bw,q_slices", [(65536, 65536, 1), (1 << 16, 1 << 15, 1), (2, 2, 2**31 - 1)])
+@pytest.mark.parametrize("bh,bw,q_slices", [(65536, 65536, 1), (1 << 16, 1 << 15, 1), (2, 2, 2**31 - 1),
+                                             (1, 1, 65535), (1, 1, 6000)])
 def test_huge_geometry_rejected_without_overflow(fvsr, bh, bw, q_slices):
     """Block counts are formed in 64 bits: grids whose 32-bit product wraps (to zero or a negative count) are
     rejected as unsupported, not accepted as tiny problems."""
@@ -93,6 +94,9 @@ def test_huge_geometry_rejected_without_overflow(fvsr, bh, bw, q_slices):
     n = ctypes.c_size_t(0)
     assert fvsr.lib().fvsr_lcsa_workspace_size(ctypes.byref(p), ctypes.byref(n)) == 5   # FVSR_EUNSUPPORTED
     assert b"too large" in fvsr.lib().fvsr_last_error() or b"exceeds" in fvsr.lib().fvsr_last_error()
+    if q_slices == 65535:   # Nq + Nk = 65536: too many for one selection; Nq alone is allowed where no key blocks are
+        g.kv_slices = 0     # involved (pooling, cache, prepare)
+        assert fvsr.lib().fvsr_lcsa_pool(ctypes.byref(g.params()), None, 0, None, None) == fvsr.FVSR_OK
 
 
 def test_misaligned_buffers_rejected_by_every_entry_point(fvsr):
