@@ -251,3 +251,47 @@ def test_prepare_matches_the_reference_formulas(orc, dtype, heads):
         # a one-ulp difference of a normalised value, carried through the rotation's cancellations
         rel = np.abs(got - ref).max(axis=1) / np.abs(ref).max(axis=1)
         assert rel.max() <= 8 * np.finfo(np.float32).eps, rel.max()
+
+
+# --- DiT.swift:163-173: invariants of the selection rule on random geometries -----------------------------------
+def test_select_invariants_over_random_geometries(orc):
+    """Seeded random geometries (grid, slices, locality range, top-k from 0 past the row length):
+    - kept entries are locality-allowed;
+    - each query block's probabilities sum to one over its allowed key blocks, and are zero elsewhere;
+    - each (head, query slice) row keeps at most k = min(n − 1, topk) entries, every kept one strictly above every
+      dropped one;
+    - kcnt counts the mask, and kidx lists its kept key blocks ascending, then −1."""
+    rng = np.random.default_rng(77)
+    for case in range(24):
+        heads, bh, bw = int(rng.integers(1, 4)), int(rng.integers(1, 5)), int(rng.integers(1, 5))
+        qs = int(rng.integers(1, 3))
+        ks = int(rng.integers(qs, qs + 3))
+        r = int(rng.integers(1, 8))
+        s = bh * bw
+        nq, nk = qs * s, ks * s
+        n = s * nk
+        topk = int(rng.integers(0, n + 2))
+        pq = rng.standard_normal((nq, heads * 128)).astype(np.float32)
+        pk = rng.standard_normal((nk, heads * 128)).astype(np.float32)
+        loc = orc.local_block_mask(bh, bw, r)
+        probs, mask, kidx, kcnt = orc.select(pq, pk, heads, qs, s, loc, topk)
+        m = mask.astype(bool)
+        allowed = np.tile(loc, (qs, ks))                               # [i, j] = loc[i mod s, j mod s]
+        tag = f"case {case}: H={heads} {bh}x{bw} qs={qs} ks={ks} R={r} topk={topk}"
+        assert not (m & ~allowed[None]).any(), tag
+        assert (probs[:, ~allowed] == 0).all(), tag
+        np.testing.assert_allclose(probs.sum(axis=2), 1.0, rtol=0, atol=2e-6, err_msg=tag)
+        k = min(n - 1, topk)
+        for h in range(heads):
+            for sl in range(qs):
+                p = probs[h, sl * s:(sl + 1) * s].reshape(-1)
+                kept = m[h, sl * s:(sl + 1) * s].reshape(-1)
+                assert kept.sum() <= k, tag
+                if kept.any() and (~kept).any():
+                    assert p[kept].min() > p[~kept].max(), tag
+        np.testing.assert_array_equal(kcnt, m.sum(axis=2), err_msg=tag)
+        for h in range(heads):
+            for i in range(nq):
+                want = np.flatnonzero(m[h, i])
+                np.testing.assert_array_equal(kidx[h, i, :len(want)], want, err_msg=tag)
+                assert (kidx[h, i, len(want):] == -1).all(), tag
