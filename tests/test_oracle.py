@@ -295,3 +295,44 @@ def test_select_invariants_over_random_geometries(orc):
                 want = np.flatnonzero(m[h, i])
                 np.testing.assert_array_equal(kidx[h, i, :len(want)], want, err_msg=tag)
                 assert (kidx[h, i, len(want):] == -1).all(), tag
+
+
+# --- DiT.swift:279-313 semantics: properties of attention over kept blocks --------------------------------------
+def test_attention_properties(orc):
+    """Size-independent properties of attention over kept blocks, checked on the oracle that judges every path:
+    - linear in V;
+    - a V constant over keys passes through every non-empty query row, and query blocks with no kept key block give
+      zero rows;
+    - scaling a head's V columns scales that head's output columns;
+    - adding one vector u to every key of a head shifts each query row's scores by the constant q·u, which the
+      softmax cancels: the output is unchanged."""
+    rng = np.random.default_rng(11)
+    heads, nq, nk = 2, 3, 5
+    q = rng.standard_normal((nq * 128, heads * 128)).astype(np.float32)
+    k = rng.standard_normal((nk * 128, heads * 128)).astype(np.float32)
+    v1 = rng.standard_normal((nk * 128, heads * 128)).astype(np.float32)
+    v2 = rng.standard_normal((nk * 128, heads * 128)).astype(np.float32)
+    mask = rng.random((heads, nq, nk)) < 0.5
+    mask[1, 2] = False                                           # one empty query block
+    mask[0, 0] = True                                            # one full one
+    kidx, kcnt = orc.mask_to_lists(mask)
+    att = lambda v: orc.attention(q, k, v, kidx, kcnt, heads).astype(np.float64)  # noqa: E731
+    a, b = 0.75, -1.25
+    mix = (a * v1.astype(np.float64) + b * v2.astype(np.float64)).astype(np.float32)
+    lin = a * att(v1) + b * att(v2)
+    np.testing.assert_allclose(att(mix), lin, rtol=0, atol=1e-6 * np.abs(lin).max())
+    row = rng.standard_normal((1, heads * 128)).astype(np.float32)
+    const = att(np.repeat(row, nk * 128, axis=0))
+    for h in range(heads):
+        for i in range(nq):
+            blk = const[i * 128:(i + 1) * 128, h * 128:(h + 1) * 128]
+            if kcnt[h, i] == 0:
+                assert not blk.any()
+            else:
+                np.testing.assert_allclose(blk, np.broadcast_to(row[:, h * 128:(h + 1) * 128], blk.shape),
+                                           rtol=0, atol=1e-6 * np.abs(row).max())
+    scale = np.repeat(rng.uniform(0.5, 2.0, heads), 128).astype(np.float32)
+    np.testing.assert_allclose(att(v1 * scale), att(v1) * scale, rtol=0, atol=1e-6 * np.abs(att(v1)).max())
+    u = np.tile(0.5 * rng.standard_normal((1, heads * 128)).astype(np.float32), (nk * 128, 1))
+    shifted = orc.attention(q, k + u, v1, kidx, kcnt, heads).astype(np.float64)
+    np.testing.assert_allclose(shifted, att(v1), rtol=0, atol=1e-6 * np.abs(att(v1)).max())
