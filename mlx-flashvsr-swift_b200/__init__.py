@@ -8,6 +8,8 @@ The reference (xocialize/mlx-flashvsr-swift) exposes the path as Swift functions
 This module offers the same operations, with the same argument meaning, on CUDA torch tensors, by calling the C ABI of
 ``include/fvsr_lcsa.h`` (``libfvsr_lcsa.so``, hand-written sm_100a kernels) through ctypes. torch is used only for
 device memory and the current stream. There is no fallback: if the library is missing, importing this package fails.
+(The reference's two study lanes of FlashVSRAttentionOps, `dense` and `gathered`, are restated with torch's attention
+in ``lanes.py`` for probes; the product path never calls them.)
 
 Where the reference traps on a bad shape (``precondition``), these functions raise ``FVSRError`` carrying the C
 status and message.
@@ -416,11 +418,26 @@ def kernel_block_attention(q, k, v, block_mask, heads: int, workspace=None, stre
 
 
 class FlashVSRAttentionOps:
-    """Public entry points of SparseAttention.swift:190-201. Only the kernel lane exists on B200: the dense and
-    gathered lanes are the reference's CPU / study paths, restated by the test oracle, not the product."""
+    """Public entry points of SparseAttention.swift:190-201, one meaning in three lanes. `kernel` is the product (the
+    sm_100a kernels). `dense` and `gathered` are the reference's study lanes, restated with torch's attention in
+    `lanes.py` for probes that compare lanes (Sources/Smoke/Diag.swift:86-121); they are not the hot path."""
 
     @staticmethod
-    def kernel(q, k, v, block_mask, heads: int):
+    def dense(q, k, v, block_mask, heads: int):
+        from .lanes import dense_block_attention
+        return dense_block_attention(q, k, v, block_mask, heads)
+
+    @staticmethod
+    def gathered(q, k, v, block_mask, heads: int):
+        from .lanes import gathered_block_attention
+        return gathered_block_attention(q, k, v, block_mask, heads)
+
+    @staticmethod
+    def kernel(q, k, v, block_mask, heads: int, simdgroups: int | None = None):
+        """`simdgroups` is the Metal kernel's threadgroup size (SparseAttention.swift:169-170); it has no B200
+        counterpart (one tcgen05 CTA per work item) and is accepted for call compatibility only."""
+        if simdgroups is not None and simdgroups < 1:
+            raise FVSRError(FVSR_EINVAL, "simdgroups must be >= 1")
         return kernel_block_attention(q, k, v, block_mask, heads)
 
 
