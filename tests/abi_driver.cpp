@@ -102,6 +102,21 @@ static int run_cpu() {
                   FVSR_ENOMEM);
     EXPECT_STATUS(fvsr_lcsa_attention(&p, nullptr, ok_ptr, ok_ptr, (int32_t*)ok_ptr, (int32_t*)ok_ptr, ok_ptr, nullptr),
                   FVSR_EINVAL);
+    // each buffer at its access width: index lists 4 bytes, the workspace 16
+    EXPECT_STATUS(fvsr_lcsa_select(&p, ok_ptr, ok_ptr, nullptr, (int32_t*)(fake + 2), (int32_t*)ok_ptr, nullptr, nullptr,
+                                   ok_ptr, bytes, nullptr),
+                  FVSR_EINVAL);
+    EXPECT_STATUS(fvsr_lcsa_select(&p, ok_ptr, ok_ptr, nullptr, (int32_t*)ok_ptr, (int32_t*)ok_ptr, nullptr, nullptr,
+                                   fake + 4, bytes, nullptr),
+                  FVSR_EINVAL);
+    // block counts that wrap in 32 bits are refused, not taken for a small problem
+    {
+        fvsr_lcsa_params b = p;
+        b.bh = 1 << 16;
+        b.bw = 1 << 16;
+        EXPECT_STATUS(fvsr_lcsa_workspace_size(&b, &bytes), FVSR_EUNSUPPORTED);
+        EXPECT_STATUS(fvsr_lcsa_workspace_size(&p, &bytes), FVSR_OK);
+    }
     // item ranges outside the H·Nq items
     const int32_t items = p.heads * p.q_slices * p.bh * p.bw;
     EXPECT_STATUS(fvsr_lcsa_attention_range(&p, ok_ptr, ok_ptr, ok_ptr, (int32_t*)ok_ptr, (int32_t*)ok_ptr, ok_ptr,
