@@ -466,7 +466,8 @@ def run_ours(args):
 
     if rank == 0:
         peak, hbm, peak_kind = peaks()
-        tr = profiled_traffic()
+        # the committed ncu figure is one config-3 launch over all items; other workloads have no capture behind them
+        tr = profiled_traffic() if args.config == 3 and not shard else None
         value = flops_all_ranks / (ms * 1e-3) / 1e12
         line = {
             "metric": f"block-sparse attn effective TFLOP/s (+ ms per 30-layer chunk), config {args.config}",

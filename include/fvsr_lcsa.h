@@ -6,7 +6,7 @@
  *   draftBlockMaskAndProbs(qW:kW:heads:qSlices:spatialBlocks:local:topk:)   Sources/FlashVSRMLX/DiT.swift:158-174
  *   kernelBlockAttention(q:k:v:blockMask:heads:simdgroups:)                 Sources/FlashVSRMLX/SparseAttention.swift:169-187
  * and keeps the window K/V cache in blockForward (DiT.swift:507-511, 532-538). The entry points below replace those
- * with device-resident calls on plain pointers; a thin Swift shim binds them (the binding is shown in INTEGRATION.md).
+ * with device-resident calls on plain pointers; a thin Swift shim over this header binds them.
  *
  * Tensor layout (identical to the Swift side): window-ordered tokens, row-major (L, H·128). Token t of window w is
  * row w·128 + t; head h owns columns [h·128, h·128 + 128). Query block i = window i of the chunk; key block j =
@@ -107,10 +107,11 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
  * Same arguments and results as fvsr_lcsa_select, except that probs is required (an output, as in the reference) and
  * the scratch (pooled queries/keys, selection histograms) comes from one fixed FVSR_NOALLOC_SCRATCH_BYTES array
  * inside the library. Calls needing more scratch than that fail with FVSR_EUNSUPPORTED; nothing is allocated.
- * The first call on a device looks the array's address up (cudaGetSymbolAddress) with that device current, so make
- * that first call before any stream capture. All calls on a device share the array and it keeps the last call's
- * contents (what must start at zero is cleared by each call); calls that overlap on the GPU race, so order them on
- * one stream. No counterpart in the reference: it is an addition for hosts without an allocator. */
+ * Outside a stream capture every call looks the array's address up in the calling thread's current CUDA context
+ * (cudaGetSymbolAddress); inside a capture the address found by that context's last uncaptured call is used, so make
+ * one call in each context before capturing (a captured call in a context without one fails with FVSR_EINVAL).
+ * All calls on a device share the array and it keeps the last call's contents (what must start at zero is cleared
+ * by each call); calls that overlap on the GPU race, so order them on one stream. No counterpart in the reference: it is an addition for hosts without an allocator. */
 fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const void* q, const void* k, const float* pooled_k,
                                      int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs, fvsr_stream_t stream);
 

@@ -8,8 +8,8 @@ The reference (xocialize/mlx-flashvsr-swift) exposes the path as Swift functions
 This module offers the same operations, with the same argument meaning, on CUDA torch tensors, by calling the C ABI of
 ``include/fvsr_lcsa.h`` (``libfvsr_lcsa.so``, hand-written sm_100a kernels) through ctypes. torch is used only for
 device memory and the current stream. There is no fallback: if the library is missing, importing this package fails.
-(The reference's two study lanes of FlashVSRAttentionOps, `dense` and `gathered`, are restated with torch's attention
-in ``lanes.py`` for probes; the product path never calls them.)
+Of FlashVSRAttentionOps only the `kernel` lane is offered; the reference's `dense` and `gathered` study lanes are
+probe code, not part of this path.
 
 Where the reference traps on a bad shape (``precondition``), these functions raise ``FVSRError`` carrying the C
 status and message.
@@ -418,19 +418,9 @@ def kernel_block_attention(q, k, v, block_mask, heads: int, workspace=None, stre
 
 
 class FlashVSRAttentionOps:
-    """Public entry points of SparseAttention.swift:190-201, one meaning in three lanes. `kernel` is the product (the
-    sm_100a kernels). `dense` and `gathered` are the reference's study lanes, restated with torch's attention in
-    `lanes.py` for probes that compare lanes (Sources/Smoke/Diag.swift:86-121); they are not the hot path."""
-
-    @staticmethod
-    def dense(q, k, v, block_mask, heads: int):
-        from .lanes import dense_block_attention
-        return dense_block_attention(q, k, v, block_mask, heads)
-
-    @staticmethod
-    def gathered(q, k, v, block_mask, heads: int):
-        from .lanes import gathered_block_attention
-        return gathered_block_attention(q, k, v, block_mask, heads)
+    """The public kernel entry point of SparseAttention.swift:190-201. The reference offers the same meaning in three
+    lanes; `kernel` is the one this path replaces (the sm_100a kernels). Its `dense` and `gathered` lanes are study
+    code (Sources/Smoke/Diag.swift:86-121 compares them) and are not offered here."""
 
     @staticmethod
     def kernel(q, k, v, block_mask, heads: int, simdgroups: int | None = None):

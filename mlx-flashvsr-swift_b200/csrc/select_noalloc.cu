@@ -10,9 +10,11 @@
 // The array is shared by every call on a device and keeps the previous call's contents; what must start at zero
 // (the histograms) is cleared on the stream by each call. Calls whose work overlaps on the GPU — on two streams
 // at once, or from two threads — race on it, so one caller must order its calls on one stream.
+#include <cuda.h>
+
 #include <cstdio>
+#include <map>
 #include <mutex>
-#include <vector>
 
 #include "../../include/fvsr_lcsa.h"
 #include "common.cuh"
@@ -25,23 +27,49 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratch
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Device address of the array for the current device. The address is looked up once per device, on that device's
-// first call, with that device current; host code never dereferences the symbol itself.
-cudaError_t scratch_address(void** out) {
+// The calling thread's current CUDA context (the driver's cuCtxGetCurrent, resolved once through the runtime), or
+// NULL when it cannot be read. A __device__ array's address belongs to a context, not to a device number: a host
+// that runs its own driver-API context, or one that reset the device, sees a new address.
+CUcontext current_context() {
+    typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    if (!fn || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
+
+// Device address of the array in the current context, with the context current; host code never dereferences the
+// symbol itself. Outside stream capture it is looked up afresh on every call (a cheap query), so a context that was
+// destroyed and re-created, or a host-owned context, always gets its own address. Inside a capture no lookup is made
+// (it could load the module, which a capture forbids); the address recorded by this context's last call outside a
+// capture is used, and a context with no such call is refused.
+cudaError_t scratch_address(cudaStream_t st, void** out) {
     static std::mutex mu;
-    static std::vector<void*> addr(256, nullptr);
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static std::map<CUcontext, void*> addr;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cs);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= (int)addr.size()) return cudaErrorInvalidDevice;
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (cs == cudaStreamCaptureStatusNone) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
-        addr[dev] = p;
+        if (ctx) addr[ctx] = p;
+        *out = p;
+        return cudaSuccess;
     }
-    *out = addr[dev];
+    const auto it = ctx ? addr.find(ctx) : addr.end();
+    if (it == addr.end()) return cudaErrorStreamCaptureUnsupported;
+    *out = it->second;
     return cudaSuccess;
 }
 
@@ -86,23 +114,32 @@ extern "C" fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const
         set_last_error(msg);
         return FVSR_EUNSUPPORTED;
     }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     void* base = nullptr;
-    if (scratch_address(&base) != cudaSuccess) {
-        set_last_error("cudaGetSymbolAddress of the scratch array failed");
+    const cudaError_t ea = scratch_address(st, &base);
+    if (ea == cudaErrorStreamCaptureUnsupported) {
+        set_last_error("the first call in a CUDA context must come before any stream capture (it looks the scratch "
+                       "array's address up)");
+        return FVSR_EINVAL;
+    }
+    if (ea != cudaSuccess) {
+        snprintf(msg, sizeof(msg), "looking up the scratch array's address failed: %s", cudaGetErrorString(ea));
+        set_last_error(msg);
         return FVSR_ECUDA;
     }
     unsigned char* b = static_cast<unsigned char*>(base);
     float* pq = reinterpret_cast<float*>(b);
     float* pk = pooled_k ? const_cast<float*>(pooled_k) : reinterpret_cast<float*>(b + bq);
     uint32_t* hist = reinterpret_cast<uint32_t*>(b + bq + bk);
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     KvPages pages{};
     pages.s = (int32_t)nk;
+    // the pooling launch also clears the histograms (the scratch keeps the previous call's counts), as in
+    // fvsr_lcsa_select, so the kernels chain by programmatic dependent launch with no memset in between
     cudaError_t e = launch_pool2(q, nq, pq, nullptr, pooled_k ? nullptr : k, pooled_k ? 0 : nk, pk, p->dtype,
-                                 (int)channels, st);
+                                 (int)channels, st, hist, select_hist_bytes(p->heads, p->q_slices) / 4);
     if (e == cudaSuccess)
         e = launch_select_scores(pq, pk, pages, p->heads, (int)nq, (int)nk, p->bh, p->bw, p->local_range, p->q_slices,
-                                 p->topk, probs, hist, st);  // clears the histograms on the stream first
+                                 p->topk, probs, hist, st, /*clear_hist=*/false);
     if (e == cudaSuccess)
         e = launch_select_threshold(probs, p->heads, (int)nq, (int)nk, p->q_slices, p->topk, hist, kidx, kcnt, mask, st);
     if (e != cudaSuccess) {

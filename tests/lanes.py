@@ -1,14 +1,16 @@
-"""The reference's two study lanes of block-masked attention, for probes that compare lanes.
+"""The reference's two study lanes of block-masked attention, restated with torch for tests that compare lanes.
+
+TEST INFRASTRUCTURE ONLY: the product package does not import this module.
 
 ``FlashVSRAttentionOps`` (Sources/FlashVSRMLX/SparseAttention.swift:190-201) offers three lanes with one meaning: per
 head, softmax(q·kᵀ/√128) over the key tokens of the kept key blocks, times v; query blocks with no kept key block
 give zero rows. The reference's probes check the kernel lane against the dense one (Sources/Smoke/Diag.swift:86-121).
 
-- ``kernel`` is the product: the sm_100a kernels behind the C ABI (``kernel_block_attention``).
+- ``kernel`` is the product: the sm_100a kernels behind the C ABI (``FlashVSRAttentionOps.kernel`` in the package).
 - ``dense`` (blockMaskedAttention, DiT.swift:279-313) and ``gathered`` (gatheredBlockAttention, DiT.swift:219-273)
   are the reference's other two algorithms. They are restated here with torch's scaled-dot-product attention (library
-  arithmetic, on whatever device the tensors are on), keeping the reference's grouping rules and budgets. They are
-  probe lanes, not the hot path, and nothing in the product calls them.
+  arithmetic, on whatever device the tensors are on), keeping the reference's grouping rules and budgets, so a test
+  can hold the kernel lane against them as the reference's probes do.
 """
 from __future__ import annotations
 

@@ -1,5 +1,5 @@
 """The reference's study lanes of FlashVSRAttentionOps (dense, gathered; SparseAttention.swift:190-201) as restated in
-the package's ``lanes.py``, checked on the CPU against the oracle with the reference's probe recipe
+``tests/lanes.py``, checked on the CPU against the oracle with the reference's probe recipe
 (Sources/Smoke/Diag.swift:86-121: random block masks of density 0.3-0.6 with forced empty query blocks, fp32 and
 bf16 against fp32), and their grouping rules (score and gather budgets) against one group."""
 from __future__ import annotations
@@ -16,8 +16,8 @@ REL_BF16 = 1e-2
 
 
 @pytest.fixture(scope="module")
-def lanes(fvsr):
-    return importlib.import_module("fvsr_b200.lanes")
+def lanes():
+    return importlib.import_module("lanes")
 
 
 def probe_inputs(seed, heads=2, nq=4, nk=6, density=0.45):
@@ -38,7 +38,7 @@ def test_lane_matches_oracle(fvsr, orc, lanes, lane, seed, density):
     q, k, v, mask = probe_inputs(seed, heads=heads, density=density)
     kidx, kcnt = orc.mask_to_lists(mask)
     ref = orc.attention(q, k, v, kidx, kcnt, heads)
-    fn = getattr(fvsr.FlashVSRAttentionOps, lane)
+    fn = getattr(lanes, f"{lane}_block_attention")
     bm = torch.from_numpy(mask.astype(np.float32))
     got = fn(torch.from_numpy(q)[None], torch.from_numpy(k)[None], torch.from_numpy(v)[None], bm, heads)
     assert got.shape == (1, q.shape[0], q.shape[1])

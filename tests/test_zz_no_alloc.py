@@ -24,15 +24,16 @@ def cfgs(fvsr):
     return importlib.import_module("fvsr_b200.configs")
 
 
-def _noalloc(fvsr, g, q, k):
+def _noalloc(fvsr, g, q, k, pooled_k=None):
     dev = q.device
     kidx = torch.full((g.heads, g.nq, g.nk), 7, dtype=torch.int32, device=dev)
     kcnt = torch.full((g.heads, g.nq), 7, dtype=torch.int32, device=dev)
     mask = torch.full((g.heads, g.nq, g.nk), 7, dtype=torch.uint8, device=dev)
     probs = torch.full((g.heads, g.nq, g.nk), 7.0, dtype=torch.float32, device=dev)
     p = g.params()
-    st = fvsr.lib().fvsr_lcsa_select_noalloc(ctypes.byref(p), fvsr._ptr(q), fvsr._ptr(k), None, fvsr._ptr(kidx),
-                                             fvsr._ptr(kcnt), fvsr._ptr(mask), fvsr._ptr(probs), fvsr._stream())
+    st = fvsr.lib().fvsr_lcsa_select_noalloc(ctypes.byref(p), fvsr._ptr(q), fvsr._ptr(k), fvsr._ptr(pooled_k),
+                                             fvsr._ptr(kidx), fvsr._ptr(kcnt), fvsr._ptr(mask), fvsr._ptr(probs),
+                                             fvsr._stream())
     assert st == fvsr.FVSR_OK, fvsr.lib().fvsr_last_error()
     return {"kidx": kidx, "kcnt": kcnt, "mask": mask, "probs": probs}
 
@@ -48,6 +49,50 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row(fvsr, cfgs):
         for key in ("kidx", "kcnt", "mask"):
             assert torch.equal(got[key], want[key]), (cfg_id, key)
         assert torch.equal(got["probs"].view(torch.int32), want["probs"].view(torch.int32)), cfg_id
+    fvsr.device_check()
+
+
+def _same(got, want, tag):
+    for key in ("kidx", "kcnt", "mask"):
+        assert torch.equal(got[key], want[key]), (tag, key)
+    assert torch.equal(got["probs"].view(torch.int32), want["probs"].view(torch.int32)), tag
+
+
+def test_noalloc_with_pooled_keys_matches(fvsr, cfgs):
+    """The streaming caller's form: pooled keys passed in (the cache keeps them), so no key scratch is reserved and
+    the histograms sit at another offset of the array. Bit-exact against fvsr_lcsa_select given the same keys."""
+    cfg = cfgs.CONFIGS[2]
+    g = cfg.geometry()
+    q, k, _ = cfgs.synth_qkv(cfg, g, 33)
+    pk = fvsr.pool(k, g)
+    got = _noalloc(fvsr, g, q, None, pooled_k=pk)
+    want = fvsr.draft_block_mask_and_probs(q, None, g, pooled_k=pk)
+    torch.cuda.synchronize()
+    _same(got, want, "pooled keys")
+    fvsr.device_check()
+
+
+def test_noalloc_call_recorded_in_a_graph(fvsr, cfgs):
+    """A call made inside a stream capture uses the address found by the context's uncaptured calls; the replayed
+    graph gives the same result as the direct entry point on new inputs copied into the captured buffers."""
+    cfg = cfgs.CONFIGS[2]
+    g = cfg.geometry()
+    q, k, _ = cfgs.synth_qkv(cfg, g, 34)
+    _noalloc(fvsr, g, q, k)                       # an uncaptured call in this context first
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        got = _noalloc(fvsr, g, q, k)
+    q2, k2, _ = cfgs.synth_qkv(cfg, g, 35)
+    q.copy_(q2)
+    k.copy_(k2)
+    graph.replay()
+    want = fvsr.draft_block_mask_and_probs(q2, k2, g)
+    torch.cuda.synchronize()
+    _same(got, want, "graph replay")
+    del graph
     fvsr.device_check()
 
 
