@@ -232,6 +232,43 @@ def compare(got: np.ndarray, ref: np.ndarray) -> dict:
     return {"max_abs": max_abs, "ref_max": ref_max, "rel": max_abs / peak, "psnr": psnr}
 
 
+def pool_f64(x: np.ndarray, chunk_blocks: int = 256) -> np.ndarray:
+    """DiT.swift:161-162 in float64: x (N·128, C) fp32 or bf16 bits → (N, C) float64 block means, a chunk of blocks
+    at a time (a float64 copy of a whole config-5 key tensor would take over 1 GB)."""
+    x = np.ascontiguousarray(x)
+    if x.dtype == np.uint16:
+        x = bf16_bits_to_f32(x).reshape(x.shape)
+    n, c = x.shape[0] // BLOCK, x.shape[1]
+    out = np.empty((n, c), np.float64)
+    for b0 in range(0, n, chunk_blocks):
+        b1 = min(n, b0 + chunk_blocks)
+        out[b0:b1] = x[b0 * BLOCK:b1 * BLOCK].reshape(b1 - b0, BLOCK, c).astype(np.float64).mean(axis=1)
+    return out
+
+
+def select_f64(q: np.ndarray, k: np.ndarray, heads: int, q_slices: int, s: int, local: np.ndarray, topk: int,
+               pooled: tuple | None = None):
+    """draftBlockMaskAndProbs (DiT.swift:158-174) evaluated in float64, one step per reference line, with the exact
+    (k+1)-th largest of each (head, slice) row from a full partition — an order-independent reference for the fp32
+    mask. q (Lq, C), k (Lk, C) window order (or pooled = (pq, pk) float64 block means). Returns (mask (H,Nq,Nk) bool,
+    probs (H,Nq,Nk) float64)."""
+    pq, pk = pooled if pooled is not None else (pool_f64(q), pool_f64(k))                            # 161-162
+    nq, nk = pq.shape[0], pk.shape[0]
+    d = pq.shape[1] // heads
+    pqh = pq.reshape(nq, heads, d).transpose(1, 0, 2)
+    pkh = pk.reshape(nk, heads, d).transpose(1, 0, 2)
+    scores = np.matmul(pqh, pkh.transpose(0, 2, 1)) / np.sqrt(d)                                      # 163
+    lm = np.where(np.asarray(local, bool), 0.0, -np.inf)                                              # 165
+    scores = scores + np.broadcast_to(lm.reshape(1, s, 1, s), (nq // s, s, nk // s, s)).reshape(nq, nk)  # 166-167
+    e = np.exp(scores - scores.max(axis=-1, keepdims=True))
+    probs = e / e.sum(axis=-1, keepdims=True)                                                         # 168
+    flat = probs.reshape(heads * q_slices, (nq // q_slices) * nk)                                     # 169
+    n = flat.shape[1]
+    kk = min(n - 1, topk)                                                                             # 171
+    thr = np.partition(flat, n - 1 - kk, axis=1)[:, n - 1 - kk:n - kk]                               # 172
+    return (flat > thr).reshape(heads, nq, nk), probs                                                 # 173
+
+
 def mask_flip_report(mine: np.ndarray, other: np.ndarray, probs: np.ndarray, q_slices: int) -> dict:
     """Sources/Smoke/Gates.swift:242-277: count mask flips and classify each as a near-tie — probability within 1e-3
     (relative) of its nearest sorted neighbour in the (head, slice) row, or below 1e-30."""

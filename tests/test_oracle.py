@@ -336,3 +336,37 @@ def test_attention_properties(orc):
     u = np.tile(0.5 * rng.standard_normal((1, heads * 128)).astype(np.float32), (nk * 128, 1))
     shifted = orc.attention(q, k + u, v1, kidx, kcnt, heads).astype(np.float64)
     np.testing.assert_allclose(shifted, att(v1), rtol=0, atol=1e-6 * np.abs(att(v1)).max())
+
+
+# --- mask flips against float64 at the configs' full spatial sizes ---------------------------------------------
+FLIP_CASES = [  # (config, bh, bw, q_slices, kv_slices, keep, distribution)
+    (3, 9, 15, 1, 3, 0.30, "normal"),
+    (4, 6, 10, 3, 3, 0.60, "c2"),
+    (5, 12, 20, 1, 3, 0.25, "c2"),
+]
+
+
+@pytest.mark.parametrize("case", FLIP_CASES, ids=[f"config{c[0]}" for c in FLIP_CASES])
+def test_select_flips_against_f64_at_full_size(orc, case):
+    """The fixed-order fp32 selection against the order-independent float64 evaluation (exact threshold) of
+    DiT.swift:158-174 at a config's full spatial size, two heads (selection rows are per head, so two are as
+    representative as twelve): every flip must be a near-tie by the reference's classifier (Gates.swift:239-277).
+    Inputs are seeded PCG64 normals rounded to bf16 (a property check, so no fixed bit stream is needed)."""
+    cfg_id, bh, bw, qs, kvs, keep, dist = case
+    heads, s = 2, bh * bw
+    nq, nk, c = qs * s, kvs * s, heads * 128
+    rng = np.random.default_rng(7000 + cfg_id)
+    std = 0.5 if dist == "c2" else 1.0
+    q = rng.standard_normal((nq * 128, c), dtype=np.float32) * np.float32(std)
+    k = rng.standard_normal((nk * 128, c), dtype=np.float32) * np.float32(std)
+    if dist == "c2":
+        off = rng.standard_normal((nk, 1, c), dtype=np.float32) * np.float32(0.3)
+        k = (k.reshape(nk, 128, c) + off).reshape(-1, c)
+    loc = local_mask(bh, bw, 11)
+    topk = int(round(keep * int(loc.sum()) * kvs))
+    qb, kb = orc.f32_to_bf16_bits(q), orc.f32_to_bf16_bits(k)
+    probs, m, _, kcnt = orc.draft_block_mask_and_probs(qb, kb, heads, qs, s, loc, topk)
+    m64, _ = orc.select_f64(qb, kb, heads, qs, s, loc, topk)
+    rep = orc.mask_flip_report(m, m64, probs, qs)
+    assert rep["worst_gap"] <= 1e-3, rep
+    assert int(kcnt.sum()) == topk * heads * qs
