@@ -248,26 +248,38 @@ def run_ours(args):
         g_loc, item_begin, item_count, torch.cuda.get_device_properties(dev).multi_processor_count)
     sched = torch.empty(pkg.schedule_size(g_loc, item_count) if use_split else 1, dtype=torch.uint8, device=dev)
 
-    def attention_call(q, k, v, out):
-        """Sharded: the balanced unit schedule (long key lists split, partials merged) and the attention over it.
-        Otherwise: the longest-first item order, then the attention over the rank's items."""
+    def order_call():
+        """The work order of the rank's items: the balanced unit schedule when sharded (long key lists split,
+        partials merged), else the longest-first item order."""
         if use_split:
             pkg._check(L.fvsr_lcsa_schedule(ctypes.byref(p), pkg._ptr(kcnt), item_begin, item_count, pkg._ptr(sched),
                                             sched.numel(), pkg._stream()))
+        else:
+            pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p), pkg._ptr(kcnt), item_begin, item_count,
+                                              pkg._ptr(order), pkg._stream()))
+
+    def attention_only(q, k, v, out):
+        if use_split:
             pkg._check(L.fvsr_lcsa_attention_scheduled(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
                                                        pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(out), item_begin,
                                                        item_count, pkg._ptr(sched), sched.numel(), pkg._stream()))
             return
-        pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p), pkg._ptr(kcnt), item_begin, item_count, pkg._ptr(order),
-                                          pkg._stream()))
         pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
                                                pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(out), item_begin, item_count,
                                                pkg._ptr(order), pkg._stream()))
 
+    def attention_call(q, k, v, out):
+        order_call()
+        attention_only(q, k, v, out)
+
     def layer_call(l, out):
-        """One layer through the C ABI: fvsr_lcsa_select (pool Q, pool K, scores + softmax, threshold + lists),
-        then the attention over this rank's work items."""
+        """One layer through the C ABI. Unsharded: fvsr_lcsa_layer (pooling, the one-launch selection that also
+        orders the items, the attention). Sharded: fvsr_lcsa_select, then the attention over this rank's items."""
         q, k, v = inputs[l]
+        if not shard:
+            pkg._check(L.fvsr_lcsa_layer(ctypes.byref(p), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v), pkg._ptr(out),
+                                         pkg._ptr(kidx), pkg._ptr(kcnt), pkg._ptr(ws), ws.numel(), pkg._stream()))
+            return
         select_call(q, k)
         attention_call(q, k, v, out)
 
@@ -289,7 +301,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     run_step = step
     if not args.no_graph:
-        # the 30 layer calls of a step (7 kernels + 1 memset each) replayed as one CUDA graph: the C ABI calls make no
+        # the 30 layer calls of a step (3 kernels each unsharded) replayed as one CUDA graph: the C ABI calls make no
         # host synchronisation and no allocation, so they capture as they are
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -323,9 +335,10 @@ def run_ours(args):
     for l in range(layers):
         q, k, v = inputs[l]
         select_call(q, k)
+        order_call()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record(stream)
-        attention_call(q, k, v, outs[0])
+        attention_only(q, k, v, outs[0])
         a1.record(stream)
         a1.synchronize()
         att_ms.append(a0.elapsed_time(a1))
@@ -493,9 +506,9 @@ def run_ours(args):
                          "traffic": (tr or {}).get("bytes_per_launch"),
                          "traffic_source": (tr or {}).get("source")},
             "clocks": clk,
-            # per layer: pool, scores, softmax, 2 histogram passes, finish, order (or schedule), attention, and the
-            # combine step when the range runs the persistent kernel
-            "gpu_launches": (9 if persistent else 8) * layers * args.steps,
+            # per layer, unsharded: pool, selection (which orders the items), attention; sharded: pool, selection,
+            # order (or schedule), attention, and the combine step when the range runs the persistent kernel
+            "gpu_launches": (3 if not shard else (5 if persistent else 4)) * layers * args.steps,
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:

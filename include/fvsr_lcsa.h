@@ -122,6 +122,15 @@ fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const void* q, c
 fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
                                 const int32_t* kidx, const int32_t* kcnt, void* out, fvsr_stream_t stream);
 
+/* One LCSA layer on window-ordered q (Nq·128, H·128) and k, v (Nk·128, H·128) without a cache: the selection of
+ * fvsr_lcsa_select, then the attention of fvsr_lcsa_attention over every (head, query block) item, longest key list
+ * first — the two calls FlashVSRAttention makes per layer (DiT.swift:512-527: draftBlockMaskAndProbs, then
+ * kernelBlockAttention). kidx / kcnt are optional outputs (NULL → kept in the workspace). Same workspace as
+ * fvsr_lcsa_select. Three kernel launches: pooling, selection (which also orders the items), attention. */
+fvsr_status fvsr_lcsa_layer(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v, void* out,
+                            int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                            fvsr_stream_t stream);
+
 /* Work items are the (head, query block) pairs, item = h·Nq + qb (head-major). */
 
 /* Longest-first schedule of the items [item_begin, item_begin + item_count): order receives the non-empty item ids

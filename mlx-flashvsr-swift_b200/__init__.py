@@ -29,7 +29,8 @@ FVSR_F32, FVSR_BF16 = 0, 1
 EXPORTED = [
     "fvsr_version", "fvsr_status_string", "fvsr_last_error", "fvsr_device_check", "fvsr_wait_probe",
     "fvsr_lcsa_workspace_size",
-    "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_attention_mask", "fvsr_kv_cache_create",
+    "fvsr_lcsa_pool", "fvsr_lcsa_select", "fvsr_lcsa_attention", "fvsr_lcsa_layer", "fvsr_lcsa_attention_mask",
+    "fvsr_kv_cache_create",
     "fvsr_kv_cache_destroy", "fvsr_kv_cache_reset", "fvsr_kv_cache_slices", "fvsr_kv_cache_append",
     "fvsr_kv_cache_trim", "fvsr_kv_cache_gather", "fvsr_kv_cache_state", "fvsr_lcsa_forward",
     "fvsr_lcsa_select_noalloc", "fvsr_lcsa_attention_range", "fvsr_lcsa_item_order", "fvsr_lcsa_schedule_size",
@@ -83,6 +84,7 @@ def lib() -> ctypes.CDLL:
         "fvsr_lcsa_pool": ([PP, P, I64, P, P], ctypes.c_int),
         "fvsr_lcsa_select": ([PP, P, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_lcsa_attention": ([PP, P, P, P, P, P, P, P], ctypes.c_int),
+        "fvsr_lcsa_layer": ([PP, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_lcsa_attention_mask": ([PP, P, P, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_kv_cache_create": ([PP, I32, I32, ctypes.POINTER(P)], ctypes.c_int),
         "fvsr_kv_cache_destroy": ([P], ctypes.c_int),
@@ -271,6 +273,23 @@ def block_sparse_attention(q, k, v, kidx, kcnt, geom: Geometry, out=None, stream
     p = g.params()
     _check(lib().fvsr_lcsa_attention(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(kidx), _ptr(kcnt),
                                      _ptr(out), _stream(stream)))
+    return out.reshape(shape)
+
+
+def lcsa_layer(q, k, v, geom: Geometry, out=None, kidx=None, kcnt=None, workspace=None, stream=None):
+    """One layer without a cache (DiT.swift:512-527): draftBlockMaskAndProbs then kernelBlockAttention in one call —
+    pooling, the selection (which also orders the items longest first) and the attention. q (Nq·128, H·128), k / v
+    (Nk·128, H·128) window order; returns out like q."""
+    torch = _torch()
+    shape = q.shape
+    q2, k2, v2 = _rows(q), _rows(k), _rows(v)
+    g = Geometry(**{**geom.__dict__, "dtype": _dtype_code(q2)})
+    if out is None:
+        out = torch.empty_like(q2)
+    ws = workspace if workspace is not None else make_workspace(g, q2.device)
+    p = g.params()
+    _check(lib().fvsr_lcsa_layer(ctypes.byref(p), _ptr(q2), _ptr(k2), _ptr(v2), _ptr(_rows(out)), _ptr(kidx),
+                                 _ptr(kcnt), _ptr(ws), ws.numel(), _stream(stream)))
     return out.reshape(shape)
 
 

@@ -165,14 +165,14 @@ fvsr_status check_device_sm100() {
     return ok ? FVSR_OK : fail(FVSR_EUNSUPPORTED, "device %d is sm_%d%d, the kernels need sm_100a", dev, major, minor);
 }
 
+// The selection on pooled inputs (one cooperative launch); with `order` non-NULL it also writes the longest-first
+// item order the attention takes. The histograms in `hist` were cleared by the pooling or prepare launch before it.
 fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* pooled_q, const float* pooled_k,
                        const KvPages& pk_pages, int32_t* kidx, int32_t* kcnt, uint8_t* mask, float* probs,
-                       uint32_t* hist, cudaStream_t st) {
-    FVSR_CU(launch_select_scores(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range,
-                                 p->q_slices, p->topk, probs, hist, st, /*clear_hist=*/false),
-            "select scores launch");
-    FVSR_CU(launch_select_threshold(probs, d.heads, d.nq, d.nk, p->q_slices, p->topk, hist, kidx, kcnt, mask, st),
-            "select threshold launch");
+                       uint32_t* hist, int32_t* order, cudaStream_t st) {
+    FVSR_CU(launch_select(pooled_q, pooled_k, pk_pages, d.heads, d.nq, d.nk, p->bh, p->bw, p->local_range, p->q_slices,
+                          p->topk, probs, hist, kidx, kcnt, mask, order, st),
+            "selection launch");
     return FVSR_OK;
 }
 
@@ -338,7 +338,8 @@ fvsr_status fvsr_lcsa_select(const fvsr_lcsa_params* p, const void* q, const voi
     FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, pooled_k ? nullptr : k, pooled_k ? 0 : d.nk, w.pooled_k, p->dtype,
                          (int)d.channels, st, w.hist, select_hist_bytes(d.heads, d.q_slices) / 4),
             "pool launch");
-    return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, w.hist, st);
+    return run_select(p, d, w.pooled_q, pk, identity_pages(d.nk), kidx, kcnt, mask, probs ? probs : w.probs, w.hist,
+                      nullptr, st);
 }
 
 fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v,
@@ -353,6 +354,33 @@ fvsr_status fvsr_lcsa_attention(const fvsr_lcsa_params* p, const void* q, const 
     if (s != FVSR_OK) return s;
     return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), kidx, kcnt, out,
                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+fvsr_status fvsr_lcsa_layer(const fvsr_lcsa_params* p, const void* q, const void* k, const void* v, void* out,
+                            int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                            fvsr_stream_t stream) {
+    Dims d;
+    fvsr_status s = check_params(p, &d);
+    if (s != FVSR_OK) return s;
+    if (!q || !k || !v || !out) return fail(FVSR_EINVAL, "q, k, v and out are required");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
+    Workspace w = layout(d, workspace);
+    s = check_workspace(w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
+    s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int32_t* li = kidx ? kidx : w.kidx;
+    int32_t* lc = kcnt ? kcnt : w.kcnt;
+    FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, k, d.nk, w.pooled_k, p->dtype, (int)d.channels, st, w.hist,
+                         select_hist_bytes(d.heads, d.q_slices) / 4),
+            "pool launch");
+    s = run_select(p, d, w.pooled_q, w.pooled_k, identity_pages(d.nk), li, lc, nullptr, w.probs, w.hist, w.order, st);
+    if (s != FVSR_OK) return s;
+    return run_attention(p, d, q, k, v, (int64_t)d.nk * 128, identity_pages(d.nk), li, lc, out, st, 0, d.heads * d.nq,
+                         w.order);
 }
 
 fvsr_status fvsr_lcsa_item_order(const fvsr_lcsa_params* p, const int32_t* kcnt, int32_t item_begin, int32_t item_count,
@@ -634,9 +662,8 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, nullptr, 0, nullptr, pp.dtype, (int)d.channels, st, w.hist,
                          select_hist_bytes(d.heads, d.q_slices) / 4),
             "pool q launch");
-    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, st);
+    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, w.order, st);
     if (s != FVSR_OK) return s;
-    FVSR_CU(launch_item_order(lc, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
     s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
                       out, st, 0, d.heads * d.nq, w.order);
     if (s != FVSR_OK) return s;
@@ -717,9 +744,8 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
         pages.page_block[i] = (i < (int)cache->pages.size() ? cache->pages[i] : 0) * d.s;
     int32_t* li = kidx ? kidx : w.kidx;
     int32_t* lc = kcnt ? kcnt : w.kcnt;
-    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, st);
+    s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, w.order, st);
     if (s != FVSR_OK) return s;
-    FVSR_CU(launch_item_order(lc, d.nq, 0, d.heads * d.nq, w.order, st), "item order launch");
     OutRows rows;
     rows.bh = pp.bh;
     rows.bw = pp.bw;

@@ -77,13 +77,17 @@ cudaError_t launch_append(const void* k_new, const void* v_new, int dtype, int64
 cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst, const void* x2, int64_t n2,
                          float* out2, int dtype, int channels, cudaStream_t st, uint32_t* zero = nullptr,
                          size_t zero_words = 0);
-cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
-                                 int bh, int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist,
-                                 cudaStream_t st, bool clear_hist = true);
-cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
-                                    uint32_t* hist, int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st);
-size_t select_scores_smem_bytes(int nk);
+// The whole selection on pooled inputs in one cooperative launch (select.cu): scores, softmax (probs, in place),
+// the exact per-(head, query slice) threshold, kidx / kcnt / optional mask, and with `order` non-NULL the
+// longest-first order of all H·nq items. `hist` (select_hist_bytes) must have been cleared by an earlier launch on
+// the stream (the pooling or prepare launch clears it).
+cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk, int bh,
+                          int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist, int32_t* kidx,
+                          int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st);
+size_t select_smem_bytes();
 size_t select_hist_bytes(int heads, int q_slices);
+// Reads and clears the selection's grid-barrier timeout word of the current device.
+cudaError_t read_and_clear_select_error(int* flag);
 size_t attn_bf16_smem_bytes(int nk);
 cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
                                  cudaStream_t st);

@@ -1,16 +1,18 @@
 // select.cu — LCSA block selection (draftBlockMaskAndProbs, DiT.swift:158-174) on pooled fp32 Q/K.
 //
-// Kernels (in launch order):
-//   select_scores_kernel    block scores pq·pk / sqrt(d) (fixed-order fmaf dot over 128 dims) with the spatial locality
-//                           mask (DiT.swift:130-145, computed from (bh, bw, R) instead of a table; −inf outside),
-//                           one 32 × 64 (query block × key block) tile per CTA → scores (H, Nq, Nk).
-//   select_softmax_kernel   one warp per (head, query block) row: softmax over key blocks, in place → probs, and
-//                           pass 1 of the radix select's histogram.
-//   select_hist_kernel ×2   passes 2 and 3 of an MSB-first radix select (11 + 11 + 10 bits of the fp32 patterns —
-//                           probabilities are ≥ 0, so unsigned order = float order; no sort) that finds, per
-//                           (head, query slice) row of n = (Nq/q_slices)·Nk entries, the exact
-//                           (min(n−1, topk)+1)-th largest probability, spread over many CTAs per row.
-//   select_finish_kernel    compaction of p > threshold into ascending kidx lists, kcnt and the optional 0/1 mask.
+// One cooperative launch (select_fused_kernel, every CTA resident; phases separated by bounded grid barriers):
+//   1. score tiles       block scores pq·pk / sqrt(d) (fixed-order fmaf dot over 128 dims) with the spatial locality
+//                        mask (DiT.swift:130-145, computed from (bh, bw, R) instead of a table; −inf outside), one
+//                        64 × 64 (query block × key block) tile at a time → scores (H, Nq, Nk).
+//   2. softmax           one warp per (head, query block) row: softmax over key blocks, in place → probs, and pass 1
+//                        of the radix select's histograms.
+//   3, 4. radix passes   passes 2 and 3 of an MSB-first radix select (11 + 11 + 10 bits of the fp32 patterns —
+//                        probabilities are ≥ 0, so unsigned order = float order; no sort) that finds, per
+//                        (head, query slice) row of n = (Nq/q_slices)·Nk entries, the exact (min(n−1, topk)+1)-th
+//                        largest probability; the entries are spread evenly over all CTAs.
+//   5. compaction        p > threshold into ascending kidx lists, kcnt and the optional 0/1 mask.
+//   6. item order        (optional) the longest-first order of the (head, query block) items for the attention.
+// The six steps used to be six launches; in one launch they pay no launch gaps and no tail of a small grid.
 //
 // Bit-exactness. Every floating-point operation is an explicit round-to-nearest intrinsic (never contracted) in the
 // order that the CPU restatement fixes: dot = fmaf chain over e = 0..127; score = dot / sqrtf(128); softmax
@@ -18,6 +20,10 @@
 // reduction, and p_j = e_j / sum. fvsr_exp is Cody–Waite range reduction (W. J. Cody, W. Waite, 1980) with a
 // degree-7 Taylor polynomial — the same function, constant for constant, as the CPU restatement.
 #include <math.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
@@ -28,7 +34,6 @@ namespace {
 constexpr int kTI = 64;   // query blocks per score tile
 constexpr int kTJ = 64;   // key blocks per score tile
 constexpr int kPS = 132;  // padded fp32 row stride of the staged pooled rows
-constexpr int kSoftRows = 4;  // (head, query block) rows per softmax CTA, one per warp
 
 __device__ __forceinline__ float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
 
@@ -66,14 +71,12 @@ __device__ __forceinline__ float fvsr_exp(float x) {
 // unsigned order of the bits is the float order): pass 1 bins bits [31:21] (2048 bins), pass 2 bits [20:10] (2048),
 // pass 3 bits [9:0] (1024). Each pass only counts the entries whose higher bits equal the bins chosen so far.
 constexpr int kBins1 = 2048, kBins2 = 2048, kBins3 = 1024;
-// Per-row workspace words: the three histograms, then completion counters and the radix state after each pass.
-// The last CTA of a pass (threadfence-and-count, no waiting) turns that pass's histogram into the next state.
-constexpr int kOffCounter = kBins1 + kBins2 + kBins3;  // 3 counters (pass 1 counts per head, in the head's first row)
+// Per-row workspace words (all cleared before each selection): the three histograms, four counter words, and the
+// radix state after each pass. Row 0's last counter word is the grid-barrier counter and its word kOffState + 9 the
+// abort word of the selection launch.
+constexpr int kOffCounter = kBins1 + kBins2 + kBins3;
 constexpr int kOffState = kOffCounter + 4;             // state after pass p at kOffState + 3·(p−1): prefix, mask, rank
 constexpr int kHistPerRow = kOffState + 12;
-constexpr int kHistPer = 16;                  // entries per thread per histogram CTA
-constexpr int kHistChunk = 256 * kHistPer;    // entries of one selection row per histogram CTA
-constexpr int kFinishRows = 8;                // query blocks compacted per finishing CTA
 
 // Warp-aggregated shared-memory histogram increment (bins repeat heavily: probabilities share exponents).
 __device__ __forceinline__ void hist_add(uint32_t* h, uint32_t key, bool valid) {
@@ -132,172 +135,226 @@ __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uin
     __syncthreads();
 }
 
-// Called by the last CTA of pass `pass` for row `hrow`: folds that pass's histogram into the radix state.
-__device__ void advance_state(uint32_t* __restrict__ hrow, int pass, uint32_t rank0) {
-    uint32_t prefix = 0, pmask = 0, rank = rank0;
+// Radix state after a pass: the bits fixed so far (prefix under mask) and the descending rank still to find among the
+// entries that carry them.
+struct RadixState {
+    uint32_t prefix, mask, rank;
+};
+
+// The state of selection row `hrow` after pass `pass`: from the state after the previous pass (stored by the phase that
+// computed it; rank0 before pass 1) and this pass's complete histogram. Every thread of the CTA calls it and receives
+// the result; thread 0 also stores it for the next phase (all CTAs that compute a row's state store the same words).
+__device__ RadixState compute_state(uint32_t* __restrict__ hrow, int pass, uint32_t rank0) {
+    RadixState r{0u, 0u, rank0};
     if (pass > 1) {
         const uint32_t* st = hrow + kOffState + 3 * (pass - 2);
-        prefix = __ldcg(st);
-        pmask = __ldcg(st + 1);
-        rank = __ldcg(st + 2);
+        r.prefix = __ldcg(st);
+        r.mask = __ldcg(st + 1);
+        r.rank = __ldcg(st + 2);
     }
     const int off = pass == 1 ? 0 : (pass == 2 ? kBins1 : kBins1 + kBins2);
     const int nb = pass == 3 ? kBins3 : kBins1;
     uint32_t b;
-    block_find_bin(hrow + off, nb, rank, &b, &rank);
+    block_find_bin(hrow + off, nb, r.rank, &b, &r.rank);
     if (pass == 1) {
-        prefix = b << 21;
-        pmask = 0xFFE00000u;
+        r.prefix = b << 21;
+        r.mask = 0xFFE00000u;
     } else if (pass == 2) {
-        prefix |= b << 10;
-        pmask |= 0x001FFC00u;
+        r.prefix |= b << 10;
+        r.mask |= 0x001FFC00u;
     } else {
-        prefix |= b;
-        pmask = 0xFFFFFFFFu;
+        r.prefix |= b;
+        r.mask = 0xFFFFFFFFu;
     }
     if (threadIdx.x == 0) {
         uint32_t* st = hrow + kOffState + 3 * (pass - 1);
-        st[0] = prefix;
-        st[1] = pmask;
-        st[2] = rank;
+        st[0] = r.prefix;
+        st[1] = r.mask;
+        st[2] = r.rank;
     }
+    return r;
 }
 
-// True in every thread of the CTA that completes `counter` (threadfence reduction: each CTA publishes its histogram
-// atomics, fences, then counts itself; the CTA that sees total − 1 runs after all others' atomics are visible).
-__device__ bool last_cta(uint32_t* counter, uint32_t total) {
-    __shared__ uint32_t s_last;
-    __threadfence();
+// Set when a grid barrier of the selection gave up (fvsr_device_check reports it).
+__device__ int g_select_timeout = 0;
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+constexpr uint64_t kBarrierLimitNs = 4000000000ull;
+
+// Grid-wide barrier of the cooperative selection launch (all CTAs are resident at once). Each CTA publishes its
+// writes (fence), adds one to `counter` (zeroed with the histograms before the launch) and waits until the count
+// reaches `target` = phase · gridDim.x. The wait is bounded: after kBarrierLimitNs it raises `abort_word` (so every
+// other CTA stops waiting at its next poll) and the device timeout word, and returns false; the CTA then returns.
+__device__ bool grid_barrier(uint32_t* counter, uint32_t* abort_word, uint32_t target) {
+    __shared__ uint32_t s_ok;
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(counter, 1u) == total - 1 ? 1u : 0u;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(counter, 1u);
+        uint32_t ok = 1;
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 0; ld_acquire_u32(counter) < target; ++it) {
+            if (*reinterpret_cast<volatile uint32_t*>(abort_word)) {
+                ok = 0;
+                break;
+            }
+            if ((it & 31u) == 31u && globaltimer_ns() - t0 > kBarrierLimitNs) {
+                atomicExch(abort_word, 1u);
+                atomicExch(&g_select_timeout, 1);
+                ok = 0;
+                break;
+            }
+            __nanosleep(32);
+        }
+        __threadfence();
+        s_ok = ok;
+    }
     __syncthreads();
-    const bool last = s_last != 0;
-    if (last) __threadfence();
-    return last;
+    return s_ok != 0;
 }
 
 __device__ __forceinline__ uint32_t row_rank0(int64_t n, int topk) {
     return (uint32_t)((int64_t)topk < n - 1 ? (int64_t)topk : n - 1);
 }
 
-// Score tile: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 4 micro-tile of rows
-// 4·ty + a and keys tx + 16·u, each score a sequential fmaf chain over e = 0..127.
-__global__ void __launch_bounds__(256) select_scores_kernel(const float* __restrict__ pq, const float* __restrict__ pk,
-                                                            KvPages pages, int heads, int nq, int nk, int bh, int bw,
-                                                            int local_range, float sqrt_d, float* __restrict__ scores) {
-    griddep_wait_then_release();
-    extern __shared__ float4 score_smem[];
-    float* sq = reinterpret_cast<float*>(score_smem);  // [kTI][kPS]
-    float* sk = sq + kTI * kPS;                         // [kTJ][kPS]
-    const int h = blockIdx.z;
-    const int i0 = blockIdx.y * kTI, j0 = blockIdx.x * kTJ;
-    const int64_t ld = (int64_t)heads * kD;
+constexpr int kSelThreads = 256;
+constexpr int kSelWarps = kSelThreads / 32;
+
+struct SelArgs {
+    const float* pq;   // pooled queries (Nq, H·128) fp32
+    const float* pk;   // pooled keys, logical block j at physical block kv_phys_block(pages, j)
+    KvPages pages;
+    int heads, nq, nk, bh, bw, local_range, q_slices, topk;
+    float sqrt_d;
+    float* probs;      // (H, Nq, Nk): scores, then probabilities in place
+    uint32_t* hist;    // per selection row: histograms, radix states; row 0 also holds the barrier words
+    int32_t* kidx;
+    int32_t* kcnt;
+    uint8_t* mask;     // optional
+    int32_t* order;    // optional longest-first order of all H·Nq items
+};
+
+// Phase 1 unit — score tile `tile`: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 4
+// micro-tile of rows 4·ty + a and keys tx + 16·u, each score a sequential fmaf chain over e = 0..127, then / sqrt(128)
+// (IEEE division), −inf outside the locality window (DiT.swift:130-145, computed from (bh, bw, R)).
+__device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __restrict__ sq) {
+    float* sk = sq + kTI * kPS;
+    const int ntj = (a.nk + kTJ - 1) / kTJ, nti = (a.nq + kTI - 1) / kTI;
+    const int h = tile / (nti * ntj), rem = tile - h * nti * ntj;
+    const int i0 = (rem / ntj) * kTI, j0 = (rem % ntj) * kTJ;
+    const int64_t ld = (int64_t)a.heads * kD;
     const int tid = threadIdx.x;
     {  // stage the tile's pooled rows: all 16 loads of a thread in flight before the first store
-        constexpr int kPer = (kTI * 32) / 256;
-        static_assert(kTI == kTJ && (kTI * 32) % 256 == 0, "staging layout");
+        constexpr int kPer = (kTI * 32) / kSelThreads;
+        static_assert(kTI == kTJ && (kTI * 32) % kSelThreads == 0, "staging layout");
         float4 vq[kPer], vk[kPer];
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
-            const int idx = tid + 256 * k, r = idx >> 5, e4 = idx & 31;
+            const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31;
             const int i = i0 + r, j = j0 + r;
-            vq[k] = i < nq ? __ldg(reinterpret_cast<const float4*>(pq + i * ld + h * kD) + e4)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-            vk[k] = j < nk ? __ldg(reinterpret_cast<const float4*>(pk + (int64_t)kv_phys_block(pages, j) * ld + h * kD) +
-                                   e4)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            vq[k] = i < a.nq ? __ldg(reinterpret_cast<const float4*>(a.pq + i * ld + h * kD) + e4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            vk[k] = j < a.nk ? __ldg(reinterpret_cast<const float4*>(a.pk + (int64_t)kv_phys_block(a.pages, j) * ld +
+                                                                     h * kD) + e4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
-            const int idx = tid + 256 * k, r = idx >> 5, e4 = idx & 31;
+            const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31;
             *reinterpret_cast<float4*>(sq + r * kPS + e4 * 4) = vq[k];
             *reinterpret_cast<float4*>(sk + r * kPS + e4 * 4) = vk[k];
         }
     }
     __syncthreads();
-    // a warp covers tile rows [8·warp, 8·warp + 8): past the last query block it has nothing to write
-    if (i0 + 8 * (tid >> 5) >= nq) return;
-    const int ty = tid >> 4, tx = tid & 15;
-    float acc[4][4];
+    // a warp covers tile rows [8·warp, 8·warp + 8): past the last query block it has nothing to write (warp-uniform)
+    if (i0 + 8 * (tid >> 5) < a.nq) {
+        const int ty = tid >> 4, tx = tid & 15;
+        float acc[4][4];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+        for (int x = 0; x < 4; ++x)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[a][u] = 0.0f;
+            for (int u = 0; u < 4; ++u) acc[x][u] = 0.0f;
 #pragma unroll 2
-    for (int e4 = 0; e4 < 32; ++e4) {
-        float4 x[4], y[4];
+        for (int e4 = 0; e4 < 32; ++e4) {
+            float4 x[4], y[4];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) x[a] = reinterpret_cast<const float4*>(sq + (4 * ty + a) * kPS)[e4];
+            for (int r = 0; r < 4; ++r) x[r] = reinterpret_cast<const float4*>(sq + (4 * ty + r) * kPS)[e4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) y[u] = reinterpret_cast<const float4*>(sk + (tx + 16 * u) * kPS)[e4];
+            for (int u = 0; u < 4; ++u) y[u] = reinterpret_cast<const float4*>(sk + (tx + 16 * u) * kPS)[e4];
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+            for (int r = 0; r < 4; ++r)
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                acc[a][u] = __fmaf_rn(x[a].x, y[u].x, acc[a][u]);
-                acc[a][u] = __fmaf_rn(x[a].y, y[u].y, acc[a][u]);
-                acc[a][u] = __fmaf_rn(x[a].z, y[u].z, acc[a][u]);
-                acc[a][u] = __fmaf_rn(x[a].w, y[u].w, acc[a][u]);
-            }
-    }
-    // locality window of each of the 4 rows and grid position of each of the 4 keys, computed once
-    const int s = bh * bw, half = local_range / 2;
-    int lo_r[4], lo_c[4], kr[4], kc[4];
+                for (int u = 0; u < 4; ++u) {
+                    acc[r][u] = __fmaf_rn(x[r].x, y[u].x, acc[r][u]);
+                    acc[r][u] = __fmaf_rn(x[r].y, y[u].y, acc[r][u]);
+                    acc[r][u] = __fmaf_rn(x[r].z, y[u].z, acc[r][u]);
+                    acc[r][u] = __fmaf_rn(x[r].w, y[u].w, acc[r][u]);
+                }
+        }
+        const int sblk = a.bh * a.bw, half = a.local_range / 2;
+        int lo_r[4], lo_c[4], kr[4], kc[4];
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int qi = (i0 + 4 * ty + a) % s;
-        lo_r[a] = qi / bw - half;
-        lo_c[a] = qi % bw - half;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int kj = (j0 + tx + 16 * u) % s;
-        kr[u] = kj / bw;
-        kc[u] = kj % bw;
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int i = i0 + 4 * ty + a;
-        if (i >= nq) continue;
-        float* out = scores + ((int64_t)h * nq + i) * nk;
+        for (int r = 0; r < 4; ++r) {
+            const int qi = (i0 + 4 * ty + r) % sblk;
+            lo_r[r] = qi / a.bw - half;
+            lo_c[r] = qi % a.bw - half;
+        }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const int j = j0 + tx + 16 * u;
-            if (j >= nk) continue;
-            const bool allowed = kr[u] >= lo_r[a] && kr[u] <= lo_r[a] + local_range - 1 && kc[u] >= lo_c[a] &&
-                                 kc[u] <= lo_c[a] + local_range - 1;
-            out[j] = allowed ? __fdiv_rn(acc[a][u], sqrt_d) : -INFINITY;
+            const int kj = (j0 + tx + 16 * u) % sblk;
+            kr[u] = kj / a.bw;
+            kc[u] = kj % a.bw;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int i = i0 + 4 * ty + r;
+            if (i >= a.nq) continue;
+            float* out = a.probs + ((int64_t)h * a.nq + i) * a.nk;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + tx + 16 * u;
+                if (j >= a.nk) continue;
+                const bool allowed = kr[u] >= lo_r[r] && kr[u] <= lo_r[r] + a.local_range - 1 && kc[u] >= lo_c[r] &&
+                                     kc[u] <= lo_c[r] + a.local_range - 1;
+                out[j] = allowed ? __fdiv_rn(acc[r][u], a.sqrt_d) : -INFINITY;
+            }
         }
     }
+    __syncthreads();  // the next tile restages the shared rows
 }
 
-// Softmax over the key blocks of one (head, query block) row per warp, in place (scores → probs), plus the pass-1
-// histogram of each (head, query slice) row. A CTA's rows lie in at most two slices whenever Nq/q_slices ≥ 8; rows
-// of any further slice go straight to global atomics.
-// NCH > 0: the row (at most NCH·256 key blocks) stays in registers between the three passes; NCH = 0 re-reads it.
+// Phase 2 — rows [r0, r1) of the (H·Nq, Nk) score matrix, one warp per row: softmax in place (scores → probs) and
+// pass 1 of the radix select's histograms. The range's first two selection rows count in shared memory, any further
+// one straight into global memory. NCH > 0: the row (at most NCH·256 key blocks) stays in registers between the
+// three sweeps; NCH = 0 re-reads it.
 template <int NCH>
-__global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* __restrict__ probs, int nq, int nk,
-                                                                       int q_slices, int topk,
-                                                                       uint32_t* __restrict__ hist) {
-    griddep_wait_then_release();
-    __shared__ uint32_t shist[2][kBins1];
-    const int h = blockIdx.y;
-    const int i0 = blockIdx.x * kSoftRows;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nqs = nq / q_slices;
-    const int slice0 = i0 / nqs;
-    for (int i = tid; i < 2 * kBins1; i += kSoftRows * 32) (&shist[0][0])[i] = 0;
+__device__ __forceinline__ void softmax_rows(const SelArgs& a, int64_t r0, int64_t r1, uint32_t* __restrict__ shist) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nqs = a.nq / a.q_slices, nk = a.nk;
+    const int64_t sr0 = r0 / nqs;
+    const int64_t nsel = (int64_t)a.heads * a.q_slices;
+    for (int i = threadIdx.x; i < 2 * kBins1; i += kSelThreads) shist[i] = 0;
     __syncthreads();
-    const int i = i0 + warp;
-    if (i < nq) {  // warp-uniform
-        float* row = probs + ((int64_t)h * nq + i) * nk;
+    for (int64_t rr = r0 + warp; rr < r1; rr += kSelWarps) {  // warp-uniform
+        float* row = a.probs + rr * nk;
         constexpr int kR = NCH > 0 ? NCH * 8 : 1;
         float rv[kR];
-        if (NCH > 0) {  // all loads in flight at once
+        if (NCH > 0) {
 #pragma unroll
             for (int c = 0; c < kR; ++c) {
                 const int j = 256 * (c >> 3) + 32 * (c & 7) + lane;
-                rv[c] = j < nk ? row[j] : -INFINITY;
+                rv[c] = j < nk ? __ldcg(row + j) : -INFINITY;
             }
         }
         float m = -INFINITY;
@@ -310,7 +367,7 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     const int j = jb + 32 * u + lane;
-                    v[u] = j < nk ? row[j] : -INFINITY;
+                    v[u] = j < nk ? __ldcg(row + j) : -INFINITY;
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) m = fmaxf(m, v[u]);
@@ -318,8 +375,8 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float part = 0.0f;
-        if (NCH > 0) {  // same order as below: j ≡ lane (mod 32), increasing j
+        float part = 0.0f;  // lane partial sum over j ≡ lane (mod 32), increasing j
+        if (NCH > 0) {
 #pragma unroll
             for (int c = 0; c < kR; ++c) {
                 const int j = 256 * (c >> 3) + 32 * (c & 7) + lane;
@@ -333,7 +390,7 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     const int j = jb + 32 * u + lane;
-                    v[u] = j < nk ? row[j] : -INFINITY;
+                    v[u] = j < nk ? __ldcg(row + j) : -INFINITY;
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
@@ -348,14 +405,14 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
         }
 #pragma unroll
         for (int o = 16; o >= 1; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
-        const int sl = i / nqs, local = sl - slice0;
-        uint32_t* gh = hist + (int64_t)(h * q_slices + sl) * kHistPerRow;
+        const int64_t sr = rr / nqs, local = sr - sr0;
+        uint32_t* gh = a.hist + sr * kHistPerRow;
         auto emit = [&](int j, float v) {
             const float p = v == 0.0f ? 0.0f : __fdiv_rn(v, part);  // 0 / sum = +0 exactly
             if (j < nk) row[j] = p;
             const uint32_t bin = __float_as_uint(p) >> 21;
             if (local < 2)
-                hist_add(&shist[local][0], bin, j < nk);
+                hist_add(shist + local * kBins1, bin, j < nk);
             else if (j < nk)
                 atomicAdd(gh + bin, 1u);
         };
@@ -368,7 +425,7 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     const int j = jb + 32 * u + lane;
-                    v[u] = j < nk ? row[j] : 0.0f;
+                    v[u] = j < nk ? __ldcg(row + j) : 0.0f;
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) emit(jb + 32 * u + lane, v[u]);
@@ -376,92 +433,189 @@ __global__ void __launch_bounds__(kSoftRows * 32) select_softmax_kernel(float* _
         }
     }
     __syncthreads();
-    for (int x = tid; x < 2 * kBins1; x += kSoftRows * 32) {
-        const uint32_t c = (&shist[0][0])[x];
-        const int sl = slice0 + x / kBins1;
-        if (c && sl < q_slices) atomicAdd(hist + (int64_t)(h * q_slices + sl) * kHistPerRow + (x % kBins1), c);
+    for (int x = threadIdx.x; x < 2 * kBins1; x += kSelThreads) {
+        const uint32_t c = shist[x];
+        const int64_t sr = sr0 + x / kBins1;
+        if (c && sr < nsel) atomicAdd(a.hist + sr * kHistPerRow + (x % kBins1), c);
     }
-    uint32_t* head0 = hist + (int64_t)(h * q_slices) * kHistPerRow;
-    if (last_cta(head0 + kOffCounter, gridDim.x))
-        for (int t = 0; t < q_slices; ++t)
-            advance_state(hist + (int64_t)(h * q_slices + t) * kHistPerRow, 1, row_rank0((int64_t)nqs * nk, topk));
 }
 
-// Passes 2 and 3 of the radix select: one CTA per kHistChunk entries of one (head, query slice) row.
-__global__ void __launch_bounds__(256) select_hist_kernel(const float* __restrict__ probs, int nq, int nk, int q_slices,
-                                                          int topk, uint32_t* __restrict__ hist, int pass) {
-    griddep_wait_then_release();
-    __shared__ uint32_t sh[kBins2];
-    const int row = blockIdx.y;
-    const int h = row / q_slices, t = row % q_slices;
-    const int nqs = nq / q_slices;
-    const int64_t n = (int64_t)nqs * nk;
-    uint32_t* hrow = hist + (int64_t)row * kHistPerRow;
-    const int tid = threadIdx.x;
-    const float* base = probs + ((int64_t)h * nq + (int64_t)t * nqs) * nk;
-    const int64_t e0 = (int64_t)blockIdx.x * kHistChunk;
-    uint32_t u[kHistPer];
-#pragma unroll
-    for (int k = 0; k < kHistPer; ++k) {
-        const int64_t idx = e0 + tid + 256 * k;
-        u[k] = idx < n ? __float_as_uint(base[idx]) : 0xFFFFFFFFu;
-    }
-    for (int i = tid; i < kBins2; i += 256) sh[i] = 0;
-    const uint32_t* st = hrow + kOffState + 3 * (pass - 2);
-    const uint32_t prefix = __ldcg(st), pmask = __ldcg(st + 1);
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kHistPer; ++k) {
-        const int64_t idx = e0 + tid + 256 * k;
-        const bool valid = idx < n && (u[k] & pmask) == prefix;
-        const uint32_t bin = pass == 2 ? (u[k] >> 10) & (kBins2 - 1) : u[k] & (kBins3 - 1);
-        hist_add(sh, bin, valid);
-    }
-    __syncthreads();
-    uint32_t* gh = hrow + (pass == 2 ? kBins1 : kBins1 + kBins2);
+// Phases 3 and 4 — radix pass `pass` (2: bits [20:10], 3: bits [9:0]) over the entries [e0, e1) of the flattened
+// probabilities, where selection row sr = (head, query slice) owns entries [sr·n, (sr + 1)·n), n = (Nq/q_slices)·Nk.
+// Only entries whose higher bits equal the bins chosen so far are counted.
+__device__ __forceinline__ void radix_pass(const SelArgs& a, int pass, int64_t e0, int64_t e1, uint32_t* __restrict__ sh) {
+    const int nqs = a.nq / a.q_slices;
+    const int64_t n = (int64_t)nqs * a.nk;
+    const uint32_t rank0 = row_rank0(n, a.topk);
+    const uint32_t* flat = reinterpret_cast<const uint32_t*>(a.probs);
     const int nb = pass == 2 ? kBins2 : kBins3;
-    for (int i = tid; i < nb; i += 256)
-        if (sh[i]) atomicAdd(gh + i, sh[i]);
-    if (last_cta(hrow + kOffCounter + pass - 1, gridDim.x)) advance_state(hrow, pass, row_rank0(n, topk));
+    for (int64_t sr = e0 / n; e0 < e1 && sr * n < e1; ++sr) {
+        uint32_t* hrow = a.hist + sr * kHistPerRow;
+        const RadixState st = compute_state(hrow, pass - 1, rank0);
+        for (int i = threadIdx.x; i < nb; i += kSelThreads) sh[i] = 0;
+        __syncthreads();
+        const int64_t lo = e0 > sr * n ? e0 : sr * n, hi = e1 < (sr + 1) * n ? e1 : (sr + 1) * n;
+        for (int64_t base = lo; base < hi; base += 4 * kSelThreads) {  // uniform trip count: whole warps in hist_add
+            uint32_t u[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int64_t idx = base + threadIdx.x + k * kSelThreads;
+                u[k] = idx < hi ? __ldcg(flat + idx) : 0xFFFFFFFFu;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int64_t idx = base + threadIdx.x + k * kSelThreads;
+                const bool valid = idx < hi && (u[k] & st.mask) == st.prefix;
+                hist_add(sh, pass == 2 ? (u[k] >> 10) & (kBins2 - 1) : u[k] & (kBins3 - 1), valid);
+            }
+        }
+        __syncthreads();
+        uint32_t* gh = hrow + (pass == 2 ? kBins1 : kBins1 + kBins2);
+        for (int i = threadIdx.x; i < nb; i += kSelThreads)
+            if (sh[i]) atomicAdd(gh + i, sh[i]);
+        __syncthreads();
+    }
 }
 
-// Threshold = the exact (min(n−1, topk)+1)-th largest of the row; compaction of p > threshold into ascending kidx
-// lists (the rest −1), kcnt, and the optional 0/1 mask. One CTA per kFinishRows query blocks of one row.
-__global__ void __launch_bounds__(256) select_finish_kernel(const float* __restrict__ probs, int nq, int nk,
-                                                            int q_slices, int topk, const uint32_t* __restrict__ hist,
-                                                            int32_t* __restrict__ kidx, int32_t* __restrict__ kcnt,
-                                                            uint8_t* __restrict__ mask) {
-    griddep_wait_then_release();
-    const int row = blockIdx.y;
-    const int h = row / q_slices, t = row % q_slices;
-    const int nqs = nq / q_slices;
-    const float thr = __uint_as_float(__ldcg(hist + (int64_t)row * kHistPerRow + kOffState + 6));
+// Phase 5 — rows [r0, r1): threshold = the exact (min(n−1, topk)+1)-th largest entry of the row's selection row;
+// p > threshold compacted into ascending kidx lists (the rest −1), kcnt and the optional 0/1 mask, one warp per row.
+__device__ __forceinline__ void finish_rows(const SelArgs& a, int64_t r0, int64_t r1) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ii = blockIdx.x * kFinishRows + warp;
-    if (ii >= nqs) return;
-    const int64_t qrow = (int64_t)h * nq + (int64_t)t * nqs + ii;
-    const float* p = probs + qrow * nk;
-    int32_t* lst = kidx + qrow * nk;
-    int cnt = 0;
-    for (int jb = 0; jb < nk; jb += 256) {
-        float v[8];
+    const int nqs = a.nq / a.q_slices, nk = a.nk;
+    const uint32_t rank0 = row_rank0((int64_t)nqs * nk, a.topk);
+    for (int64_t sr = r0 / nqs; r0 < r1 && sr * nqs < r1; ++sr) {
+        const float thr = __uint_as_float(compute_state(a.hist + sr * kHistPerRow, 3, rank0).prefix);
+        const int64_t lo = r0 > sr * nqs ? r0 : sr * nqs, hi = r1 < (sr + 1) * nqs ? r1 : (sr + 1) * nqs;
+        for (int64_t rr = lo + warp; rr < hi; rr += kSelWarps) {
+            const float* p = a.probs + rr * nk;
+            int32_t* lst = a.kidx + rr * nk;
+            int cnt = 0;
+            for (int jb = 0; jb < nk; jb += 256) {
+                float v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int j = jb + 32 * u + lane;
-            v[u] = j < nk ? p[j] : 0.0f;
-        }
+                for (int u = 0; u < 8; ++u) {
+                    const int j = jb + 32 * u + lane;
+                    v[u] = j < nk ? __ldcg(p + j) : 0.0f;
+                }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int j = jb + 32 * u + lane;
-            const bool keep = j < nk && v[u] > thr;
-            const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-            if (keep) lst[cnt + __popc(bal & ((1u << lane) - 1u))] = j;
-            if (mask && j < nk) mask[qrow * nk + j] = keep ? 1 : 0;
-            cnt += __popc(bal);
+                for (int u = 0; u < 8; ++u) {
+                    const int j = jb + 32 * u + lane;
+                    const bool keep = j < nk && v[u] > thr;
+                    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+                    if (keep) lst[cnt + __popc(bal & ((1u << lane) - 1u))] = j;
+                    if (a.mask && j < nk) a.mask[rr * nk + j] = keep ? 1 : 0;
+                    cnt += __popc(bal);
+                }
+            }
+            for (int j = cnt + lane; j < nk; j += 32) lst[j] = -1;
+            if (lane == 0) a.kcnt[rr] = cnt;
         }
+        __syncthreads();
     }
-    for (int j = cnt + lane; j < nk; j += 32) lst[j] = -1;
-    if (lane == 0) kcnt[qrow] = cnt;
+}
+
+// Longest-first order of one head segment of the items [item_begin, item_begin + item_count) (see launch_item_order):
+// the non-empty items of each head segment in turn (segments in head order), longest key list first within a segment
+// (ties by id); then every empty item of the range, ascending. Empty items only write zeros, so they go last: placed
+// between heads they would delay the next head's long items. Rank of a non-empty item inside its segment = items of
+// the segment with a longer key list, or an equal one and a smaller id; empty items rank after all non-empty ones, by
+// id. All threads of the CTA call it; sc (4096 words) and cnt (4 words) are shared scratch.
+__device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item_begin, int item_count,
+                              int32_t* __restrict__ order, int seg, int32_t* __restrict__ sc, int* __restrict__ cnt) {
+    const int h = item_begin / nq + seg;
+    const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
+    const int n = s1 - s0;
+    if (n <= 0) return;  // uniform over the CTA
+    if (threadIdx.x < 4) cnt[threadIdx.x] = 0;
+    __syncthreads();
+    {
+        int na = 0, nb = 0, nc = 0, nd = 0;
+        for (int i = threadIdx.x; i < item_count; i += blockDim.x) {
+            const int it = item_begin + i;
+            const bool nz = __ldcg(kcnt + it) > 0;
+            nc += nz;
+            if (it < s0) {
+                na += nz;
+                nb += !nz;
+            } else if (it < s1) {
+                nd += nz;
+            }
+        }
+        atomicAdd(&cnt[0], na);
+        atomicAdd(&cnt[1], nb);
+        atomicAdd(&cnt[2], nc);
+        atomicAdd(&cnt[3], nd);
+    }
+    __syncthreads();
+    const int ne_before = cnt[0], e_before = cnt[1], ne_total = cnt[2], ne_seg = cnt[3];
+    auto place = [&](int i, int rank, bool nz) {  // rank: position inside the segment, non-empty items first
+        const int pos = nz ? ne_before + rank : ne_total + e_before + (rank - ne_seg);
+        order[pos] = s0 + i;
+    };
+    if (n > 4096) {  // no room to rank: each class in ascending id order
+        if (threadIdx.x == 0) {
+            int x = 0, y = 0;
+            for (int i = 0; i < n; ++i) {
+                const bool nz = __ldcg(kcnt + s0 + i) > 0;
+                place(i, nz ? x++ : ne_seg + y++, nz);
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = max(__ldcg(kcnt + s0 + i), 0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int ci = sc[i];
+        int rank = 0;
+        for (int t = 0; t < n; ++t) {
+            const int ct = sc[t];
+            rank += (ct > ci) || (ct == ci && t < i);
+        }
+        place(i, rank, ci > 0);
+    }
+    __syncthreads();
+}
+
+// The whole selection of one call in one cooperative launch (every CTA resident), its phases separated by grid
+// barriers: (1) score tiles, (2) softmax + radix pass 1 per row, (3) radix pass 2, (4) radix pass 3, (5) threshold
+// and compaction per row, and with an order buffer (6) the longest-first item order. Each phase partitions its work
+// evenly over the CTAs; the radix state a phase needs is recomputed by every CTA from the finished histogram (a
+// 2048-bin scan) instead of waiting for one CTA to publish it.
+template <int NCH>
+__global__ void __launch_bounds__(kSelThreads, 3) select_fused_kernel(const __grid_constant__ SelArgs a) {
+    extern __shared__ float4 sel_smem4[];
+    float* smem = reinterpret_cast<float*>(sel_smem4);
+    uint32_t* smem_u = reinterpret_cast<uint32_t*>(sel_smem4);
+    griddep_wait_then_release();
+    const uint32_t G = gridDim.x;
+    uint32_t* bar = a.hist + kOffCounter + 3;
+    uint32_t* abort_word = a.hist + kOffState + 9;
+    const int ntiles = a.heads * ((a.nq + kTI - 1) / kTI) * ((a.nk + kTJ - 1) / kTJ);
+    for (int t = blockIdx.x; t < ntiles; t += (int)G) score_tile(a, t, smem);
+    if (!grid_barrier(bar, abort_word, G)) return;
+
+    const int64_t rows = (int64_t)a.heads * a.nq;
+    const int64_t rpc = (rows + G - 1) / G;
+    const int64_t r0 = min(rows, (int64_t)blockIdx.x * rpc), r1 = min(rows, r0 + rpc);
+    softmax_rows<NCH>(a, r0, r1, smem_u);
+    if (!grid_barrier(bar, abort_word, 2 * G)) return;
+
+    const int64_t ents = rows * a.nk;
+    const int64_t epc = (((ents + G - 1) / G) + 255) & ~int64_t(255);
+    const int64_t e0 = min(ents, (int64_t)blockIdx.x * epc), e1 = min(ents, e0 + epc);
+    radix_pass(a, 2, e0, e1, smem_u);
+    if (!grid_barrier(bar, abort_word, 3 * G)) return;
+    radix_pass(a, 3, e0, e1, smem_u);
+    if (!grid_barrier(bar, abort_word, 4 * G)) return;
+
+    finish_rows(a, r0, r1);
+    if (!a.order) return;
+    if (!grid_barrier(bar, abort_word, 5 * G)) return;
+    const int items = a.heads * a.nq;
+    for (int seg = blockIdx.x; seg < a.heads; seg += (int)G)
+        order_segment(a.kcnt, a.nq, 0, items, a.order, seg, reinterpret_cast<int32_t*>(smem_u),
+                      reinterpret_cast<int*>(smem_u + 4096));
 }
 
 __global__ void __launch_bounds__(256) mask_to_lists_kernel(const float* __restrict__ mask, int rows, int nk,
@@ -483,49 +637,97 @@ __global__ void __launch_bounds__(256) mask_to_lists_kernel(const float* __restr
     if (lane == 0) kcnt[warp] = cnt;
 }
 
+// One CTA per head segment of the range (order_segment).
+__global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restrict__ kcnt, int nq, int item_begin,
+                                                         int item_count, int32_t* __restrict__ order) {
+    griddep_wait_then_release();
+    __shared__ int32_t sc[4096];
+    __shared__ int cnt[4];
+    order_segment(kcnt, nq, item_begin, item_count, order, blockIdx.x, sc, cnt);
+}
+
 }  // namespace
 
-size_t select_scores_smem_bytes(int) { return sizeof(float) * (size_t)(kTI + kTJ) * kPS; }
+// Shared memory of the fused selection: the two staged pooled tiles of a score tile (the largest phase).
+size_t select_smem_bytes() { return sizeof(float) * (size_t)(kTI + kTJ) * kPS; }
 
 size_t select_hist_bytes(int heads, int q_slices) { return sizeof(uint32_t) * (size_t)heads * q_slices * kHistPerRow; }
 
-cudaError_t launch_select_scores(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk,
-                                 int bh, int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist,
-                                 cudaStream_t st, bool clear_hist) {
-    cudaError_t e = cudaSuccess;
-    if (clear_hist && (e = cudaMemsetAsync(hist, 0, select_hist_bytes(heads, q_slices), st)) != cudaSuccess) return e;
-    const int smem = (int)select_scores_smem_bytes(nk);
-    e = cudaFuncSetAttribute(select_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk, int bh,
+                          int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist, int32_t* kidx,
+                          int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st) {
+    SelArgs a;
+    a.pq = pq;
+    a.pk = pk;
+    a.pages = pk_pages;
+    a.heads = heads;
+    a.nq = nq;
+    a.nk = nk;
+    a.bh = bh;
+    a.bw = bw;
+    a.local_range = local_range;
+    a.q_slices = q_slices;
+    a.topk = topk;
+    a.sqrt_d = sqrtf((float)kD);
+    a.probs = probs;
+    a.hist = hist;
+    a.kidx = kidx;
+    a.kcnt = kcnt;
+    a.mask = mask;
+    a.order = order;
+    const int nch = nk <= 256 ? 1 : nk <= 512 ? 2 : nk <= 768 ? 3 : nk <= 1024 ? 4 : 0;
+    void (*kernels[5])(SelArgs) = {select_fused_kernel<0>, select_fused_kernel<1>, select_fused_kernel<2>,
+                                   select_fused_kernel<3>, select_fused_kernel<4>};
+    auto kernel = kernels[nch];
+    const int smem = (int)select_smem_bytes();
+    // grid = every CTA the device holds at once (the grid barriers need all of them resident), looked up once per
+    // device and variant
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const float sqrt_d = sqrtf((float)kD);
-    dim3 grid((nk + kTJ - 1) / kTJ, (nq + kTI - 1) / kTI, heads);
-    e = launch_pdl(select_scores_kernel, grid, dim3(256), (size_t)smem, st, pq, pk, pk_pages, heads, nq, nk, bh, bw,
-                   local_range, sqrt_d, probs);
-    if (e != cudaSuccess) return e;
-    dim3 sgrid((nq + kSoftRows - 1) / kSoftRows, heads);
-    auto soft = [&](auto kernel) {
-        return launch_pdl(kernel, sgrid, dim3(kSoftRows * 32), 0, st, probs, nq, nk, q_slices, topk, hist);
-    };
-    if (nk <= 256) return soft(select_softmax_kernel<1>);
-    if (nk <= 512) return soft(select_softmax_kernel<2>);
-    if (nk <= 768) return soft(select_softmax_kernel<3>);
-    if (nk <= 1024) return soft(select_softmax_kernel<4>);
-    return soft(select_softmax_kernel<0>);
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, int> grid_of;
+    int grid = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = grid_of.find({dev, nch});
+        if (it != grid_of.end()) {
+            grid = it->second;
+        } else {
+            int nsm = 0, per_sm = 0;
+            if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
+                return e;
+            if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+            if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSelThreads, smem)) != cudaSuccess)
+                return e;
+            if (per_sm < 1) return cudaErrorLaunchOutOfResources;
+            grid = per_sm * nsm;
+            grid_of[{dev, nch}] = grid;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kSelThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
-cudaError_t launch_select_threshold(const float* probs, int heads, int nq, int nk, int q_slices, int topk,
-                                    uint32_t* hist, int32_t* kidx, int32_t* kcnt, uint8_t* mask, cudaStream_t st) {
-    const int rows = heads * q_slices;
-    const int64_t n = (int64_t)(nq / q_slices) * nk;
-    dim3 hgrid((unsigned)((n + kHistChunk - 1) / kHistChunk), rows);
-    for (int pass = 2; pass <= 3; ++pass) {
-        const cudaError_t e =
-            launch_pdl(select_hist_kernel, hgrid, dim3(256), 0, st, probs, nq, nk, q_slices, topk, hist, pass);
-        if (e != cudaSuccess) return e;
+cudaError_t read_and_clear_select_error(int* flag) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_select_timeout, sizeof(int));
+    if (e != cudaSuccess) return e;
+    if (v) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_select_timeout, &zero, sizeof(int));
     }
-    dim3 fgrid((nq / q_slices + kFinishRows - 1) / kFinishRows, rows);
-    return launch_pdl(select_finish_kernel, fgrid, dim3(256), 0, st, probs, nq, nk, q_slices, topk, hist, kidx, kcnt,
-                      mask);
+    *flag = v;
+    return e;
 }
 
 cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, int32_t* kidx, int32_t* kcnt,
@@ -534,77 +736,6 @@ cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, i
     return launch_pdl(mask_to_lists_kernel, dim3((rows * 32 + 255) / 256), dim3(256), 0, st, mask, rows, nk, kidx,
                       kcnt);
 }
-
-}  // namespace fvsr
-
-namespace fvsr {
-
-namespace {
-
-// One CTA per head segment of the range. The order is: the non-empty items of each head segment in turn (segments in
-// head order), longest key list first within a segment (ties by id); then every empty item of the range, ascending.
-// Empty items only write zeros, so they go last: placed between heads they would delay the next head's long items.
-// Rank of a non-empty item inside its segment = items of the segment with a longer key list, or an equal one and a
-// smaller id; empty items rank after all non-empty ones, by id.
-__global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restrict__ kcnt, int nq, int item_begin,
-                                                         int item_count, int32_t* __restrict__ order) {
-    griddep_wait_then_release();
-    __shared__ int32_t sc[4096];
-    __shared__ int cnt[4];  // non-empty before this segment, empty before it, non-empty in the range, in the segment
-    const int h = item_begin / nq + blockIdx.x;
-    const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
-    const int n = s1 - s0;
-    if (n <= 0) return;
-    if (threadIdx.x < 4) cnt[threadIdx.x] = 0;
-    __syncthreads();
-    {
-        int a = 0, b = 0, c = 0, d = 0;
-        for (int i = threadIdx.x; i < item_count; i += blockDim.x) {
-            const int it = item_begin + i;
-            const bool nz = kcnt[it] > 0;
-            c += nz;
-            if (it < s0) {
-                a += nz;
-                b += !nz;
-            } else if (it < s1) {
-                d += nz;
-            }
-        }
-        atomicAdd(&cnt[0], a);
-        atomicAdd(&cnt[1], b);
-        atomicAdd(&cnt[2], c);
-        atomicAdd(&cnt[3], d);
-    }
-    __syncthreads();
-    const int ne_before = cnt[0], e_before = cnt[1], ne_total = cnt[2], ne_seg = cnt[3];
-    auto place = [&](int i, int rank, bool nz) {  // rank: position inside the segment, non-empty items first
-        const int pos = nz ? ne_before + rank : ne_total + e_before + (rank - ne_seg);
-        order[pos] = s0 + i;
-    };
-    if (n > 4096) {  // no room to rank: each class in ascending id order
-        if (threadIdx.x == 0) {
-            int a = 0, b = 0;
-            for (int i = 0; i < n; ++i) {
-                const bool nz = kcnt[s0 + i] > 0;
-                place(i, nz ? a++ : ne_seg + b++, nz);
-            }
-        }
-        return;
-    }
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = max(kcnt[s0 + i], 0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int ci = sc[i];
-        int rank = 0;
-        for (int t = 0; t < n; ++t) {
-            const int ct = sc[t];
-            rank += (ct > ci) || (ct == ci && t < i);
-        }
-        place(i, rank, ci > 0);
-    }
-}
-
-}  // namespace
 
 cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int item_count, int32_t* order,
                               cudaStream_t st) {

@@ -134,14 +134,12 @@ extern "C" fvsr_status fvsr_lcsa_select_noalloc(const fvsr_lcsa_params* p, const
     KvPages pages{};
     pages.s = (int32_t)nk;
     // the pooling launch also clears the histograms (the scratch keeps the previous call's counts), as in
-    // fvsr_lcsa_select, so the kernels chain by programmatic dependent launch with no memset in between
+    // fvsr_lcsa_select, so no memset runs in between
     cudaError_t e = launch_pool2(q, nq, pq, nullptr, pooled_k ? nullptr : k, pooled_k ? 0 : nk, pk, p->dtype,
                                  (int)channels, st, hist, select_hist_bytes(p->heads, p->q_slices) / 4);
     if (e == cudaSuccess)
-        e = launch_select_scores(pq, pk, pages, p->heads, (int)nq, (int)nk, p->bh, p->bw, p->local_range, p->q_slices,
-                                 p->topk, probs, hist, st, /*clear_hist=*/false);
-    if (e == cudaSuccess)
-        e = launch_select_threshold(probs, p->heads, (int)nq, (int)nk, p->q_slices, p->topk, hist, kidx, kcnt, mask, st);
+        e = launch_select(pq, pk, pages, p->heads, (int)nq, (int)nk, p->bh, p->bw, p->local_range, p->q_slices,
+                          p->topk, probs, hist, kidx, kcnt, mask, nullptr, st);
     if (e != cudaSuccess) {
         snprintf(msg, sizeof(msg), "launch failed: %s", cudaGetErrorString(e));
         set_last_error(msg);

@@ -394,3 +394,22 @@ def test_cache_append_pages(fvsr, heads, dtype):
 
 def test_device_check_clean(fvsr, cfgs):
     fvsr.device_check()
+
+
+@pytest.mark.parametrize("cfg_id", [1, 2])
+def test_layer_entry_equals_select_then_attention(fvsr, cfgs, cfg_id):
+    """fvsr_lcsa_layer (pooling, the one-launch selection that also orders the items, attention) gives the selection
+    and the output of fvsr_lcsa_select followed by fvsr_lcsa_attention, bit for bit."""
+    cfg = cfgs.CONFIGS[cfg_id]
+    g = cfg.geometry()
+    q, k, v = cfgs.synth_qkv(cfg, g, cfgs.seed_of(cfg_id, 0, 5))
+    kidx = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device="cuda")
+    kcnt = torch.empty((g.heads, g.nq), dtype=torch.int32, device="cuda")
+    out = fvsr.lcsa_layer(q, k, v, g, kidx=kidx, kcnt=kcnt)
+    r = fvsr.draft_block_mask_and_probs(q, k, g, want_mask=False, want_probs=False)
+    want = fvsr.block_sparse_attention(q, k, v, r["kidx"], r["kcnt"], g)
+    torch.cuda.synchronize()
+    assert torch.equal(kidx, r["kidx"]) and torch.equal(kcnt, r["kcnt"])
+    assert torch.equal(out.view(torch.int16) if out.dtype == torch.bfloat16 else out.view(torch.int32),
+                       want.view(torch.int16) if want.dtype == torch.bfloat16 else want.view(torch.int32))
+    fvsr.device_check()
