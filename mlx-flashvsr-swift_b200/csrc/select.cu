@@ -86,16 +86,28 @@ __device__ __forceinline__ void hist_add(uint32_t* h, uint32_t key, bool valid) 
     if (valid && lane == __ffs(peers) - 1) atomicAdd(h + key, (uint32_t)__popc(peers));
 }
 
+// A group of kSelThreads threads (eight warps) that works as one unit: the fused selection runs kSelGroups groups per
+// CTA, the stand-alone item-order kernel one group per CTA. Groups synchronise with their own named barrier.
+constexpr int kSelThreads = 256;
+constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kSelGroups = 3;       // groups per CTA of the fused selection (one CTA per SM)
+constexpr int kMiscWords = 64;      // per-group shared scratch words (scan partials, broadcasts)
+
+struct Grp {
+    int id;   // group within the CTA
+    int tid;  // thread within the group
+    __device__ __forceinline__ void sync() const {
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + id), "r"(kSelThreads) : "memory");
+    }
+};
+
 // Finds, among `nbins` histogram bins scanned from the highest, the bin holding the entry of descending rank `rank`
-// (0 = largest). All threads of the block call it (128 to 1024 threads, nbins / blockDim ≤ 16); the result is
-// returned to every thread.
-__device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uint32_t rank, uint32_t* out_bin,
-                               uint32_t* out_rank) {
-    __shared__ uint32_t warp_sums[32];
-    __shared__ uint32_t s_bin, s_rank;
-    const int nt = blockDim.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int per = nbins / nt;
+// (0 = largest). All threads of the group call it (nbins / kSelThreads ≤ 16); the result goes to every thread.
+__device__ void group_find_bin(const uint32_t* __restrict__ hist, int nbins, uint32_t rank, uint32_t* out_bin,
+                               uint32_t* out_rank, const Grp& g, uint32_t* misc) {
+    uint32_t* warp_sums = misc;  // [kSelWarps]
+    const int tid = g.tid, lane = tid & 31, warp = tid >> 5;
+    const int per = nbins / kSelThreads;
     const int top = nbins - 1 - per * tid;  // this thread covers bins top, top−1, …, top−per+1
     uint32_t c[16];
 #pragma unroll
@@ -111,10 +123,10 @@ __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uin
     }
     if (lane == 31) warp_sums[warp] = incl;
     if (tid == 0) {
-        s_bin = 0;
-        s_rank = 0;
+        misc[kSelWarps] = 0;
+        misc[kSelWarps + 1] = 0;
     }
-    __syncthreads();
+    g.sync();
     uint32_t before = 0;
     for (int w = 0; w < warp; ++w) before += warp_sums[w];
     const uint32_t excl = before + incl - local;
@@ -122,17 +134,17 @@ __device__ void block_find_bin(const uint32_t* __restrict__ hist, int nbins, uin
         uint32_t cum = excl;
         for (int i = 0; i < per; ++i) {
             if (rank < cum + c[i]) {
-                s_bin = (uint32_t)(top - i);
-                s_rank = rank - cum;
+                misc[kSelWarps] = (uint32_t)(top - i);
+                misc[kSelWarps + 1] = rank - cum;
                 break;
             }
             cum += c[i];
         }
     }
-    __syncthreads();
-    *out_bin = s_bin;
-    *out_rank = s_rank;
-    __syncthreads();
+    g.sync();
+    *out_bin = misc[kSelWarps];
+    *out_rank = misc[kSelWarps + 1];
+    g.sync();
 }
 
 // Radix state after a pass: the bits fixed so far (prefix under mask) and the descending rank still to find among the
@@ -141,21 +153,19 @@ struct RadixState {
     uint32_t prefix, mask, rank;
 };
 
-// The state of selection row `hrow` after pass `pass`: from the state after the previous pass (stored by the phase that
-// computed it; rank0 before pass 1) and this pass's complete histogram. Every thread of the CTA calls it and receives
-// the result; thread 0 also stores it for the next phase (all CTAs that compute a row's state store the same words).
-__device__ RadixState compute_state(uint32_t* __restrict__ hrow, int pass, uint32_t rank0) {
-    RadixState r{0u, 0u, rank0};
-    if (pass > 1) {
-        const uint32_t* st = hrow + kOffState + 3 * (pass - 2);
-        r.prefix = __ldcg(st);
-        r.mask = __ldcg(st + 1);
-        r.rank = __ldcg(st + 2);
-    }
+__device__ __forceinline__ RadixState load_state(const uint32_t* __restrict__ hrow, int pass) {
+    const uint32_t* st = hrow + kOffState + 3 * (pass - 1);
+    return RadixState{__ldcg(st), __ldcg(st + 1), __ldcg(st + 2)};
+}
+
+// The state of selection row `hrow` after pass `pass`, from the state after the previous pass (rank0 before pass 1)
+// and this pass's complete histogram; thread 0 of the group stores it.
+__device__ void compute_state(uint32_t* __restrict__ hrow, int pass, uint32_t rank0, const Grp& g, uint32_t* misc) {
+    RadixState r = pass > 1 ? load_state(hrow, pass - 1) : RadixState{0u, 0u, rank0};
     const int off = pass == 1 ? 0 : (pass == 2 ? kBins1 : kBins1 + kBins2);
     const int nb = pass == 3 ? kBins3 : kBins1;
     uint32_t b;
-    block_find_bin(hrow + off, nb, r.rank, &b, &r.rank);
+    group_find_bin(hrow + off, nb, r.rank, &b, &r.rank, g, misc);
     if (pass == 1) {
         r.prefix = b << 21;
         r.mask = 0xFFE00000u;
@@ -166,13 +176,32 @@ __device__ RadixState compute_state(uint32_t* __restrict__ hrow, int pass, uint3
         r.prefix |= b;
         r.mask = 0xFFFFFFFFu;
     }
-    if (threadIdx.x == 0) {
+    if (g.tid == 0) {
         uint32_t* st = hrow + kOffState + 3 * (pass - 1);
         st[0] = r.prefix;
         st[1] = r.mask;
         st[2] = r.rank;
     }
-    return r;
+}
+
+// Called by a group once its contributions to selection row sr's pass-`pass` histogram are in global memory: counts
+// the group in (threadfence reduction), and the group that completes the count of the `need` groups that contribute
+// to the row computes the row's state after the pass — once per row, so the next phase only reads three words.
+__device__ void arrive_and_advance(uint32_t* __restrict__ hrow, int pass, uint32_t need, uint32_t rank0, const Grp& g,
+                                   uint32_t* misc) {
+    __threadfence();
+    g.sync();
+    if (g.tid == 0) misc[kSelWarps + 2] = atomicAdd(hrow + kOffCounter + pass - 1, 1u) == need - 1 ? 1u : 0u;
+    g.sync();
+    if (misc[kSelWarps + 2]) {
+        __threadfence();
+        compute_state(hrow, pass, rank0, g, misc);
+    }
+    g.sync();
+}
+
+__device__ __forceinline__ uint32_t row_rank0(int64_t n, int topk) {
+    return (uint32_t)((int64_t)topk < n - 1 ? (int64_t)topk : n - 1);
 }
 
 // Set when a grid barrier of the selection gave up (fvsr_device_check reports it).
@@ -215,7 +244,6 @@ __device__ bool grid_barrier(uint32_t* counter, uint32_t* abort_word, uint32_t t
                 ok = 0;
                 break;
             }
-            __nanosleep(32);
         }
         __threadfence();
         s_ok = ok;
@@ -224,13 +252,6 @@ __device__ bool grid_barrier(uint32_t* counter, uint32_t* abort_word, uint32_t t
     return s_ok != 0;
 }
 
-__device__ __forceinline__ uint32_t row_rank0(int64_t n, int topk) {
-    return (uint32_t)((int64_t)topk < n - 1 ? (int64_t)topk : n - 1);
-}
-
-constexpr int kSelThreads = 256;
-constexpr int kSelWarps = kSelThreads / 32;
-
 struct SelArgs {
     const float* pq;   // pooled queries (Nq, H·128) fp32
     const float* pk;   // pooled keys, logical block j at physical block kv_phys_block(pages, j)
@@ -238,7 +259,7 @@ struct SelArgs {
     int heads, nq, nk, bh, bw, local_range, q_slices, topk;
     float sqrt_d;
     float* probs;      // (H, Nq, Nk): scores, then probabilities in place
-    uint32_t* hist;    // per selection row: histograms, radix states; row 0 also holds the barrier words
+    uint32_t* hist;    // per selection row: histograms, arrival counters, radix states; row 0: the barrier words
     int32_t* kidx;
     int32_t* kcnt;
     uint8_t* mask;     // optional
@@ -248,13 +269,13 @@ struct SelArgs {
 // Phase 1 unit — score tile `tile`: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 4
 // micro-tile of rows 4·ty + a and keys tx + 16·u, each score a sequential fmaf chain over e = 0..127, then / sqrt(128)
 // (IEEE division), −inf outside the locality window (DiT.swift:130-145, computed from (bh, bw, R)).
-__device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __restrict__ sq) {
+__device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __restrict__ sq, const Grp& g) {
     float* sk = sq + kTI * kPS;
     const int ntj = (a.nk + kTJ - 1) / kTJ, nti = (a.nq + kTI - 1) / kTI;
     const int h = tile / (nti * ntj), rem = tile - h * nti * ntj;
     const int i0 = (rem / ntj) * kTI, j0 = (rem % ntj) * kTJ;
     const int64_t ld = (int64_t)a.heads * kD;
-    const int tid = threadIdx.x;
+    const int tid = g.tid;
     {  // stage the tile's pooled rows: all 16 loads of a thread in flight before the first store
         constexpr int kPer = (kTI * 32) / kSelThreads;
         static_assert(kTI == kTJ && (kTI * 32) % kSelThreads == 0, "staging layout");
@@ -276,7 +297,7 @@ __device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __
             *reinterpret_cast<float4*>(sk + r * kPS + e4 * 4) = vk[k];
         }
     }
-    __syncthreads();
+    g.sync();
     // a warp covers tile rows [8·warp, 8·warp + 8): past the last query block it has nothing to write (warp-uniform)
     if (i0 + 8 * (tid >> 5) < a.nq) {
         const int ty = tid >> 4, tx = tid & 15;
@@ -303,49 +324,39 @@ __device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __
                 }
         }
         const int sblk = a.bh * a.bw, half = a.local_range / 2;
-        int lo_r[4], lo_c[4], kr[4], kc[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int qi = (i0 + 4 * ty + r) % sblk;
-            lo_r[r] = qi / a.bw - half;
-            lo_c[r] = qi % a.bw - half;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int kj = (j0 + tx + 16 * u) % sblk;
-            kr[u] = kj / a.bw;
-            kc[u] = kj % a.bw;
-        }
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             const int i = i0 + 4 * ty + r;
             if (i >= a.nq) continue;
+            const int qi = i % sblk, lo_r = qi / a.bw - half, lo_c = qi % a.bw - half;
             float* out = a.probs + ((int64_t)h * a.nq + i) * a.nk;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int j = j0 + tx + 16 * u;
                 if (j >= a.nk) continue;
-                const bool allowed = kr[u] >= lo_r[r] && kr[u] <= lo_r[r] + a.local_range - 1 && kc[u] >= lo_c[r] &&
-                                     kc[u] <= lo_c[r] + a.local_range - 1;
+                const int kj = j % sblk, kr = kj / a.bw, kc = kj % a.bw;
+                const bool allowed = kr >= lo_r && kr <= lo_r + a.local_range - 1 && kc >= lo_c &&
+                                     kc <= lo_c + a.local_range - 1;
                 out[j] = allowed ? __fdiv_rn(acc[r][u], a.sqrt_d) : -INFINITY;
             }
         }
     }
-    __syncthreads();  // the next tile restages the shared rows
+    g.sync();  // the next tile restages the shared rows
 }
 
 // Phase 2 — rows [r0, r1) of the (H·Nq, Nk) score matrix, one warp per row: softmax in place (scores → probs) and
 // pass 1 of the radix select's histograms. The range's first two selection rows count in shared memory, any further
 // one straight into global memory. NCH > 0: the row (at most NCH·256 key blocks) stays in registers between the
-// three sweeps; NCH = 0 re-reads it.
+// three sweeps; NCH = 0 re-reads it. Then the group counts itself in on each selection row it touched.
 template <int NCH>
-__device__ __forceinline__ void softmax_rows(const SelArgs& a, int64_t r0, int64_t r1, uint32_t* __restrict__ shist) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void softmax_rows(const SelArgs& a, int64_t r0, int64_t r1, int64_t rpc,
+                                             uint32_t* __restrict__ shist, const Grp& g, uint32_t* misc) {
+    const int warp = g.tid >> 5, lane = g.tid & 31;
     const int nqs = a.nq / a.q_slices, nk = a.nk;
     const int64_t sr0 = r0 / nqs;
     const int64_t nsel = (int64_t)a.heads * a.q_slices;
-    for (int i = threadIdx.x; i < 2 * kBins1; i += kSelThreads) shist[i] = 0;
-    __syncthreads();
+    for (int i = g.tid; i < 2 * kBins1; i += kSelThreads) shist[i] = 0;
+    g.sync();
     for (int64_t rr = r0 + warp; rr < r1; rr += kSelWarps) {  // warp-uniform
         float* row = a.probs + rr * nk;
         constexpr int kR = NCH > 0 ? NCH * 8 : 1;
@@ -432,18 +443,26 @@ __device__ __forceinline__ void softmax_rows(const SelArgs& a, int64_t r0, int64
             }
         }
     }
-    __syncthreads();
-    for (int x = threadIdx.x; x < 2 * kBins1; x += kSelThreads) {
+    g.sync();
+    for (int x = g.tid; x < 2 * kBins1; x += kSelThreads) {
         const uint32_t c = shist[x];
         const int64_t sr = sr0 + x / kBins1;
         if (c && sr < nsel) atomicAdd(a.hist + sr * kHistPerRow + (x % kBins1), c);
+    }
+    const uint32_t rank0 = row_rank0((int64_t)nqs * nk, a.topk);
+    for (int64_t sr = sr0; r0 < r1 && sr * nqs < r1; ++sr) {
+        // groups whose row range meets selection row sr (ranges of rpc rows each)
+        const uint32_t need = (uint32_t)(((sr + 1) * nqs - 1) / rpc - (sr * nqs) / rpc + 1);
+        arrive_and_advance(a.hist + sr * kHistPerRow, 1, need, rank0, g, misc);
     }
 }
 
 // Phases 3 and 4 — radix pass `pass` (2: bits [20:10], 3: bits [9:0]) over the entries [e0, e1) of the flattened
 // probabilities, where selection row sr = (head, query slice) owns entries [sr·n, (sr + 1)·n), n = (Nq/q_slices)·Nk.
-// Only entries whose higher bits equal the bins chosen so far are counted.
-__device__ __forceinline__ void radix_pass(const SelArgs& a, int pass, int64_t e0, int64_t e1, uint32_t* __restrict__ sh) {
+// Only entries whose higher bits equal the bins chosen so far are counted; the last group to count into a row
+// computes the row's next state.
+__device__ __forceinline__ void radix_pass(const SelArgs& a, int pass, int64_t e0, int64_t e1, int64_t epc,
+                                           uint32_t* __restrict__ sh, const Grp& g, uint32_t* misc) {
     const int nqs = a.nq / a.q_slices;
     const int64_t n = (int64_t)nqs * a.nk;
     const uint32_t rank0 = row_rank0(n, a.topk);
@@ -451,66 +470,63 @@ __device__ __forceinline__ void radix_pass(const SelArgs& a, int pass, int64_t e
     const int nb = pass == 2 ? kBins2 : kBins3;
     for (int64_t sr = e0 / n; e0 < e1 && sr * n < e1; ++sr) {
         uint32_t* hrow = a.hist + sr * kHistPerRow;
-        const RadixState st = compute_state(hrow, pass - 1, rank0);
-        for (int i = threadIdx.x; i < nb; i += kSelThreads) sh[i] = 0;
-        __syncthreads();
+        const RadixState st = load_state(hrow, pass - 1);
+        for (int i = g.tid; i < nb; i += kSelThreads) sh[i] = 0;
+        g.sync();
         const int64_t lo = e0 > sr * n ? e0 : sr * n, hi = e1 < (sr + 1) * n ? e1 : (sr + 1) * n;
         for (int64_t base = lo; base < hi; base += 4 * kSelThreads) {  // uniform trip count: whole warps in hist_add
             uint32_t u[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int64_t idx = base + threadIdx.x + k * kSelThreads;
+                const int64_t idx = base + g.tid + k * kSelThreads;
                 u[k] = idx < hi ? __ldcg(flat + idx) : 0xFFFFFFFFu;
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int64_t idx = base + threadIdx.x + k * kSelThreads;
+                const int64_t idx = base + g.tid + k * kSelThreads;
                 const bool valid = idx < hi && (u[k] & st.mask) == st.prefix;
                 hist_add(sh, pass == 2 ? (u[k] >> 10) & (kBins2 - 1) : u[k] & (kBins3 - 1), valid);
             }
         }
-        __syncthreads();
+        g.sync();
         uint32_t* gh = hrow + (pass == 2 ? kBins1 : kBins1 + kBins2);
-        for (int i = threadIdx.x; i < nb; i += kSelThreads)
+        for (int i = g.tid; i < nb; i += kSelThreads)
             if (sh[i]) atomicAdd(gh + i, sh[i]);
-        __syncthreads();
+        const uint32_t need = (uint32_t)(((sr + 1) * n - 1) / epc - (sr * n) / epc + 1);
+        arrive_and_advance(hrow, pass, need, rank0, g, misc);
     }
 }
 
-// Phase 5 — rows [r0, r1): threshold = the exact (min(n−1, topk)+1)-th largest entry of the row's selection row;
-// p > threshold compacted into ascending kidx lists (the rest −1), kcnt and the optional 0/1 mask, one warp per row.
-__device__ __forceinline__ void finish_rows(const SelArgs& a, int64_t r0, int64_t r1) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Phase 5 — rows [r0, r1): threshold = the exact (min(n−1, topk)+1)-th largest entry of the row's selection row (the
+// state after pass 3); p > threshold compacted into ascending kidx lists (the rest −1), kcnt and the optional 0/1
+// mask, one warp per row.
+__device__ __forceinline__ void finish_rows(const SelArgs& a, int64_t r0, int64_t r1, const Grp& g) {
+    const int warp = g.tid >> 5, lane = g.tid & 31;
     const int nqs = a.nq / a.q_slices, nk = a.nk;
-    const uint32_t rank0 = row_rank0((int64_t)nqs * nk, a.topk);
-    for (int64_t sr = r0 / nqs; r0 < r1 && sr * nqs < r1; ++sr) {
-        const float thr = __uint_as_float(compute_state(a.hist + sr * kHistPerRow, 3, rank0).prefix);
-        const int64_t lo = r0 > sr * nqs ? r0 : sr * nqs, hi = r1 < (sr + 1) * nqs ? r1 : (sr + 1) * nqs;
-        for (int64_t rr = lo + warp; rr < hi; rr += kSelWarps) {
-            const float* p = a.probs + rr * nk;
-            int32_t* lst = a.kidx + rr * nk;
-            int cnt = 0;
-            for (int jb = 0; jb < nk; jb += 256) {
-                float v[8];
+    for (int64_t rr = r0 + warp; rr < r1; rr += kSelWarps) {
+        const float thr = __uint_as_float(load_state(a.hist + (rr / nqs) * kHistPerRow, 3).prefix);
+        const float* p = a.probs + rr * nk;
+        int32_t* lst = a.kidx + rr * nk;
+        int cnt = 0;
+        for (int jb = 0; jb < nk; jb += 256) {
+            float v[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int j = jb + 32 * u + lane;
-                    v[u] = j < nk ? __ldcg(p + j) : 0.0f;
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int j = jb + 32 * u + lane;
-                    const bool keep = j < nk && v[u] > thr;
-                    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-                    if (keep) lst[cnt + __popc(bal & ((1u << lane) - 1u))] = j;
-                    if (a.mask && j < nk) a.mask[rr * nk + j] = keep ? 1 : 0;
-                    cnt += __popc(bal);
-                }
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                v[u] = j < nk ? __ldcg(p + j) : 0.0f;
             }
-            for (int j = cnt + lane; j < nk; j += 32) lst[j] = -1;
-            if (lane == 0) a.kcnt[rr] = cnt;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = jb + 32 * u + lane;
+                const bool keep = j < nk && v[u] > thr;
+                const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+                if (keep) lst[cnt + __popc(bal & ((1u << lane) - 1u))] = j;
+                if (a.mask && j < nk) a.mask[rr * nk + j] = keep ? 1 : 0;
+                cnt += __popc(bal);
+            }
         }
-        __syncthreads();
+        for (int j = cnt + lane; j < nk; j += 32) lst[j] = -1;
+        if (lane == 0) a.kcnt[rr] = cnt;
     }
 }
 
@@ -519,18 +535,19 @@ __device__ __forceinline__ void finish_rows(const SelArgs& a, int64_t r0, int64_
 // (ties by id); then every empty item of the range, ascending. Empty items only write zeros, so they go last: placed
 // between heads they would delay the next head's long items. Rank of a non-empty item inside its segment = items of
 // the segment with a longer key list, or an equal one and a smaller id; empty items rank after all non-empty ones, by
-// id. All threads of the CTA call it; sc (4096 words) and cnt (4 words) are shared scratch.
+// id. All threads of the group call it; sc (4096 words) and cnt (4 words) are shared scratch of the group.
 __device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item_begin, int item_count,
-                              int32_t* __restrict__ order, int seg, int32_t* __restrict__ sc, int* __restrict__ cnt) {
+                              int32_t* __restrict__ order, int seg, int32_t* __restrict__ sc, int* __restrict__ cnt,
+                              const Grp& g) {
     const int h = item_begin / nq + seg;
     const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
     const int n = s1 - s0;
-    if (n <= 0) return;  // uniform over the CTA
-    if (threadIdx.x < 4) cnt[threadIdx.x] = 0;
-    __syncthreads();
+    if (n <= 0) return;  // uniform over the group
+    if (g.tid < 4) cnt[g.tid] = 0;
+    g.sync();
     {
         int na = 0, nb = 0, nc = 0, nd = 0;
-        for (int i = threadIdx.x; i < item_count; i += blockDim.x) {
+        for (int i = g.tid; i < item_count; i += kSelThreads) {
             const int it = item_begin + i;
             const bool nz = __ldcg(kcnt + it) > 0;
             nc += nz;
@@ -546,26 +563,26 @@ __device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item
         atomicAdd(&cnt[2], nc);
         atomicAdd(&cnt[3], nd);
     }
-    __syncthreads();
+    g.sync();
     const int ne_before = cnt[0], e_before = cnt[1], ne_total = cnt[2], ne_seg = cnt[3];
     auto place = [&](int i, int rank, bool nz) {  // rank: position inside the segment, non-empty items first
         const int pos = nz ? ne_before + rank : ne_total + e_before + (rank - ne_seg);
         order[pos] = s0 + i;
     };
     if (n > 4096) {  // no room to rank: each class in ascending id order
-        if (threadIdx.x == 0) {
+        if (g.tid == 0) {
             int x = 0, y = 0;
             for (int i = 0; i < n; ++i) {
                 const bool nz = __ldcg(kcnt + s0 + i) > 0;
                 place(i, nz ? x++ : ne_seg + y++, nz);
             }
         }
-        __syncthreads();
+        g.sync();
         return;
     }
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sc[i] = max(__ldcg(kcnt + s0 + i), 0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = g.tid; i < n; i += kSelThreads) sc[i] = max(__ldcg(kcnt + s0 + i), 0);
+    g.sync();
+    for (int i = g.tid; i < n; i += kSelThreads) {
         const int ci = sc[i];
         int rank = 0;
         for (int t = 0; t < n; ++t) {
@@ -574,48 +591,55 @@ __device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item
         }
         place(i, rank, ci > 0);
     }
-    __syncthreads();
+    g.sync();
 }
 
-// The whole selection of one call in one cooperative launch (every CTA resident), its phases separated by grid
-// barriers: (1) score tiles, (2) softmax + radix pass 1 per row, (3) radix pass 2, (4) radix pass 3, (5) threshold
-// and compaction per row, and with an order buffer (6) the longest-first item order. Each phase partitions its work
-// evenly over the CTAs; the radix state a phase needs is recomputed by every CTA from the finished histogram (a
-// 2048-bin scan) instead of waiting for one CTA to publish it.
+// Shared memory of one group: the two staged pooled tiles of a score tile (the largest phase), then its scratch words.
+constexpr size_t kGroupSmemWords = (size_t)(kTI + kTJ) * kPS;
+
+// The whole selection of one call in one cooperative launch: one CTA per SM, each of kSelGroups groups a worker
+// (worker w = group·gridDim.x + CTA, so consecutive work goes to different SMs). Phases, separated by grid barriers:
+// (1) score tiles, (2) softmax + radix pass 1 per row, (3) radix pass 2, (4) radix pass 3 — after each histogram
+// pass the last worker to count into a selection row computes that row's radix state — (5) threshold and compaction
+// per row, and with an order buffer (6) the longest-first item order. Every phase splits its work evenly over the
+// workers.
 template <int NCH>
-__global__ void __launch_bounds__(kSelThreads, 3) select_fused_kernel(const __grid_constant__ SelArgs a) {
+__global__ void __launch_bounds__(kSelThreads * kSelGroups, 1) select_fused_kernel(const __grid_constant__ SelArgs a) {
     extern __shared__ float4 sel_smem4[];
-    float* smem = reinterpret_cast<float*>(sel_smem4);
-    uint32_t* smem_u = reinterpret_cast<uint32_t*>(sel_smem4);
+    const Grp g{(int)threadIdx.x / kSelThreads, (int)threadIdx.x % kSelThreads};
+    float* gsm = reinterpret_cast<float*>(sel_smem4) + (size_t)g.id * (kGroupSmemWords + kMiscWords);
+    uint32_t* gsm_u = reinterpret_cast<uint32_t*>(gsm);
+    uint32_t* misc = gsm_u + kGroupSmemWords;
     griddep_wait_then_release();
     const uint32_t G = gridDim.x;
+    const int W = kSelGroups * (int)G, w = g.id * (int)G + (int)blockIdx.x;
     uint32_t* bar = a.hist + kOffCounter + 3;
     uint32_t* abort_word = a.hist + kOffState + 9;
     const int ntiles = a.heads * ((a.nq + kTI - 1) / kTI) * ((a.nk + kTJ - 1) / kTJ);
-    for (int t = blockIdx.x; t < ntiles; t += (int)G) score_tile(a, t, smem);
+    for (int t = w; t < ntiles; t += W) score_tile(a, t, gsm, g);
     if (!grid_barrier(bar, abort_word, G)) return;
 
     const int64_t rows = (int64_t)a.heads * a.nq;
-    const int64_t rpc = (rows + G - 1) / G;
-    const int64_t r0 = min(rows, (int64_t)blockIdx.x * rpc), r1 = min(rows, r0 + rpc);
-    softmax_rows<NCH>(a, r0, r1, smem_u);
+    const int64_t rpc = (rows + W - 1) / W;
+    const int64_t r0 = min(rows, (int64_t)w * rpc), r1 = min(rows, r0 + rpc);
+    softmax_rows<NCH>(a, r0, r1, rpc, gsm_u, g, misc);
     if (!grid_barrier(bar, abort_word, 2 * G)) return;
 
     const int64_t ents = rows * a.nk;
-    const int64_t epc = (((ents + G - 1) / G) + 255) & ~int64_t(255);
-    const int64_t e0 = min(ents, (int64_t)blockIdx.x * epc), e1 = min(ents, e0 + epc);
-    radix_pass(a, 2, e0, e1, smem_u);
+    const int64_t epc = (((ents + W - 1) / W) + 255) & ~int64_t(255);
+    const int64_t e0 = min(ents, (int64_t)w * epc), e1 = min(ents, e0 + epc);
+    radix_pass(a, 2, e0, e1, epc, gsm_u, g, misc);
     if (!grid_barrier(bar, abort_word, 3 * G)) return;
-    radix_pass(a, 3, e0, e1, smem_u);
+    radix_pass(a, 3, e0, e1, epc, gsm_u, g, misc);
     if (!grid_barrier(bar, abort_word, 4 * G)) return;
 
-    finish_rows(a, r0, r1);
+    finish_rows(a, r0, r1, g);
     if (!a.order) return;
     if (!grid_barrier(bar, abort_word, 5 * G)) return;
     const int items = a.heads * a.nq;
-    for (int seg = blockIdx.x; seg < a.heads; seg += (int)G)
-        order_segment(a.kcnt, a.nq, 0, items, a.order, seg, reinterpret_cast<int32_t*>(smem_u),
-                      reinterpret_cast<int*>(smem_u + 4096));
+    for (int seg = w; seg < a.heads; seg += W)
+        order_segment(a.kcnt, a.nq, 0, items, a.order, seg, reinterpret_cast<int32_t*>(gsm_u),
+                      reinterpret_cast<int*>(gsm_u + 4096), g);
 }
 
 __global__ void __launch_bounds__(256) mask_to_lists_kernel(const float* __restrict__ mask, int rows, int nk,
@@ -637,19 +661,20 @@ __global__ void __launch_bounds__(256) mask_to_lists_kernel(const float* __restr
     if (lane == 0) kcnt[warp] = cnt;
 }
 
-// One CTA per head segment of the range (order_segment).
-__global__ void __launch_bounds__(256) item_order_kernel(const int32_t* __restrict__ kcnt, int nq, int item_begin,
-                                                         int item_count, int32_t* __restrict__ order) {
+// One 256-thread CTA (one group) per head segment of the range (order_segment).
+__global__ void __launch_bounds__(kSelThreads) item_order_kernel(const int32_t* __restrict__ kcnt, int nq,
+                                                                 int item_begin, int item_count,
+                                                                 int32_t* __restrict__ order) {
     griddep_wait_then_release();
     __shared__ int32_t sc[4096];
     __shared__ int cnt[4];
-    order_segment(kcnt, nq, item_begin, item_count, order, blockIdx.x, sc, cnt);
+    order_segment(kcnt, nq, item_begin, item_count, order, blockIdx.x, sc, cnt, Grp{0, (int)threadIdx.x});
 }
 
 }  // namespace
 
-// Shared memory of the fused selection: the two staged pooled tiles of a score tile (the largest phase).
-size_t select_smem_bytes() { return sizeof(float) * (size_t)(kTI + kTJ) * kPS; }
+// Shared memory of the fused selection CTA: per group the staged score tiles and the group's scratch words.
+size_t select_smem_bytes() { return sizeof(float) * (size_t)kSelGroups * (kGroupSmemWords + kMiscWords); }
 
 size_t select_hist_bytes(int heads, int q_slices) { return sizeof(uint32_t) * (size_t)heads * q_slices * kHistPerRow; }
 
@@ -680,8 +705,8 @@ cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pa
                                    select_fused_kernel<3>, select_fused_kernel<4>};
     auto kernel = kernels[nch];
     const int smem = (int)select_smem_bytes();
-    // grid = every CTA the device holds at once (the grid barriers need all of them resident), looked up once per
-    // device and variant
+    // grid = one CTA per SM (its shared memory admits no second one; the grid barriers need every CTA resident),
+    // checked once per device and variant
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -698,16 +723,17 @@ cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pa
             if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess)
                 return e;
             if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-            if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSelThreads, smem)) != cudaSuccess)
+            if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kSelThreads * kSelGroups, smem)) !=
+                cudaSuccess)
                 return e;
-            if (per_sm < 1) return cudaErrorLaunchOutOfResources;
-            grid = per_sm * nsm;
+            if (per_sm != 1) return cudaErrorLaunchOutOfResources;
+            grid = nsm;
             grid_of[{dev, nch}] = grid;
         }
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kSelThreads);
+    cfg.blockDim = dim3(kSelThreads * kSelGroups);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
