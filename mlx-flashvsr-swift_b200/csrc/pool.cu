@@ -2,7 +2,8 @@
 // of the same rows into a KV-cache page (the cache append of DiT.swift:508-511 reads each key row once).
 //
 // HBM-bound: algorithmic bytes = nblocks·128·C·elt read (+ the same written when copying) + nblocks·C·4 written.
-// Layout: one CTA covers one 128-token block × 512 channels; 4 token groups × 64 channel lanes, 8 channels per lane
+// The inputs are read with evict-first (streaming) loads, so the pass does not push the pooled rows it writes — which
+// the selection reads next — out of L2. Layout: one CTA covers one 128-token block × 512 channels; 4 token groups × 64 channel lanes, 8 channels per lane
 // (one 128-bit load per token for bf16), so a warp reads 512 contiguous bytes of a token row per load. With at most
 // 256 channels (the one or two heads of a sharded rank) the 64 lanes are split into bpc = 64 / lanes groups that
 // pool bpc consecutive blocks at once, each block with exactly the arithmetic of the one-block layout.
@@ -50,7 +51,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
                 uint4 v[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u)
-                    v[u] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) +
+                    v[u] = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) +
                                                                (b * kBlock + t0 + u) * (int64_t)channels + c0));
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
@@ -70,8 +71,8 @@ __global__ void __launch_bounds__(256) pool_kernel(const void* __restrict__ x, i
                 for (int u = 0; u < 8; ++u) {
                     const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(x) +
                                                                         (b * kBlock + t0 + u) * (int64_t)channels + c0);
-                    v[u][0] = __ldg(src);
-                    v[u][1] = __ldg(src + 1);
+                    v[u][0] = __ldcs(src);
+                    v[u][1] = __ldcs(src + 1);
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {

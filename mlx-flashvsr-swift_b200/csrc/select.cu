@@ -3,7 +3,7 @@
 // One cooperative launch (select_fused_kernel, every CTA resident; phases separated by bounded grid barriers):
 //   1. score tiles       block scores pq·pk / sqrt(d) (fixed-order fmaf dot over 128 dims) with the spatial locality
 //                        mask (DiT.swift:130-145, computed from (bh, bw, R) instead of a table; −inf outside), one
-//                        64 × 64 (query block × key block) tile at a time → scores (H, Nq, Nk).
+//                        64 × 32 (query block × key block) tile at a time → scores (H, Nq, Nk).
 //   2. softmax           one warp per (head, query block) row: softmax over key blocks, in place → probs, and pass 1
 //                        of the radix select's histograms.
 //   3, 4. radix passes   passes 2 and 3 of an MSB-first radix select (11 + 11 + 10 bits of the fp32 patterns —
@@ -32,7 +32,7 @@ namespace fvsr {
 namespace {
 
 constexpr int kTI = 64;   // query blocks per score tile
-constexpr int kTJ = 64;   // key blocks per score tile
+constexpr int kTJ = 32;   // key blocks per score tile
 constexpr int kPS = 132;  // padded fp32 row stride of the staged pooled rows
 
 __device__ __forceinline__ float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
@@ -266,34 +266,41 @@ struct SelArgs {
     int32_t* order;    // optional longest-first order of all H·Nq items
 };
 
-// Phase 1 unit — score tile `tile`: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 4
+// Phase 1 unit — score tile `tile`: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 2
 // micro-tile of rows 4·ty + a and keys tx + 16·u, each score a sequential fmaf chain over e = 0..127, then / sqrt(128)
 // (IEEE division), −inf outside the locality window (DiT.swift:130-145, computed from (bh, bw, R)).
 __device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __restrict__ sq, const Grp& g) {
+    static_assert(kTI == 64 && kTJ == 32, "micro-tile layout: 16 × 16 threads of 4 rows × 2 keys");
     float* sk = sq + kTI * kPS;
     const int ntj = (a.nk + kTJ - 1) / kTJ, nti = (a.nq + kTI - 1) / kTI;
     const int h = tile / (nti * ntj), rem = tile - h * nti * ntj;
     const int i0 = (rem / ntj) * kTI, j0 = (rem % ntj) * kTJ;
     const int64_t ld = (int64_t)a.heads * kD;
     const int tid = g.tid;
-    {  // stage the tile's pooled rows: all 16 loads of a thread in flight before the first store
-        constexpr int kPer = (kTI * 32) / kSelThreads;
-        static_assert(kTI == kTJ && (kTI * 32) % kSelThreads == 0, "staging layout");
-        float4 vq[kPer], vk[kPer];
+    {  // stage the tile's pooled rows: all 12 loads of a thread in flight before the first store
+        constexpr int kPerQ = (kTI * 32) / kSelThreads, kPerK = (kTJ * 32) / kSelThreads;
+        float4 vq[kPerQ], vk[kPerK];
 #pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31;
-            const int i = i0 + r, j = j0 + r;
+        for (int k = 0; k < kPerQ; ++k) {
+            const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31, i = i0 + r;
             vq[k] = i < a.nq ? __ldg(reinterpret_cast<const float4*>(a.pq + i * ld + h * kD) + e4)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kPerK; ++k) {
+            const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31, j = j0 + r;
             vk[k] = j < a.nk ? __ldg(reinterpret_cast<const float4*>(a.pk + (int64_t)kv_phys_block(a.pages, j) * ld +
                                                                      h * kD) + e4)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int k = 0; k < kPer; ++k) {
+        for (int k = 0; k < kPerQ; ++k) {
             const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31;
             *reinterpret_cast<float4*>(sq + r * kPS + e4 * 4) = vq[k];
+        }
+#pragma unroll
+        for (int k = 0; k < kPerK; ++k) {
+            const int idx = tid + kSelThreads * k, r = idx >> 5, e4 = idx & 31;
             *reinterpret_cast<float4*>(sk + r * kPS + e4 * 4) = vk[k];
         }
     }
@@ -301,22 +308,22 @@ __device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __
     // a warp covers tile rows [8·warp, 8·warp + 8): past the last query block it has nothing to write (warp-uniform)
     if (i0 + 8 * (tid >> 5) < a.nq) {
         const int ty = tid >> 4, tx = tid & 15;
-        float acc[4][4];
+        float acc[4][2];
 #pragma unroll
         for (int x = 0; x < 4; ++x)
 #pragma unroll
-            for (int u = 0; u < 4; ++u) acc[x][u] = 0.0f;
-#pragma unroll 2
+            for (int u = 0; u < 2; ++u) acc[x][u] = 0.0f;
+#pragma unroll 4
         for (int e4 = 0; e4 < 32; ++e4) {
-            float4 x[4], y[4];
+            float4 x[4], y[2];
 #pragma unroll
             for (int r = 0; r < 4; ++r) x[r] = reinterpret_cast<const float4*>(sq + (4 * ty + r) * kPS)[e4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) y[u] = reinterpret_cast<const float4*>(sk + (tx + 16 * u) * kPS)[e4];
+            for (int u = 0; u < 2; ++u) y[u] = reinterpret_cast<const float4*>(sk + (tx + 16 * u) * kPS)[e4];
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < 2; ++u) {
                     acc[r][u] = __fmaf_rn(x[r].x, y[u].x, acc[r][u]);
                     acc[r][u] = __fmaf_rn(x[r].y, y[u].y, acc[r][u]);
                     acc[r][u] = __fmaf_rn(x[r].z, y[u].z, acc[r][u]);
@@ -331,7 +338,7 @@ __device__ __forceinline__ void score_tile(const SelArgs& a, int tile, float* __
             const int qi = i % sblk, lo_r = qi / a.bw - half, lo_c = qi % a.bw - half;
             float* out = a.probs + ((int64_t)h * a.nq + i) * a.nk;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 2; ++u) {
                 const int j = j0 + tx + 16 * u;
                 if (j >= a.nk) continue;
                 const int kj = j % sblk, kr = kj / a.bw, kc = kj % a.bw;
