@@ -37,6 +37,7 @@ extern "C" {
 #endif
 
 typedef struct CUstream_st* fvsr_stream_t; /* a cudaStream_t */
+typedef struct CUevent_st* fvsr_event_t;   /* a cudaEvent_t */
 
 typedef enum fvsr_status {
     FVSR_OK = 0,
@@ -210,6 +211,37 @@ fvsr_status fvsr_kv_cache_state(const fvsr_kv_cache* cache, int32_t* pages, int3
 fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const void* k_new, const void* v_new,
                               fvsr_kv_cache* cache, void* out, int32_t* kidx, int32_t* kcnt, void* workspace,
                               size_t workspace_bytes, fvsr_stream_t stream);
+
+/* ---- Query-block sharding of one chunk across GPUs ----
+ * The reference runs on one device; this is the B200 partition of one chunk over N GPUs of a node. Rank r holds the
+ * chunk's query blocks (windows) [qb_begin, qb_end) of q, k_new and v_new — what a sequence-split QKV projection
+ * leaves on it. Per layer it pools its shard (fvsr_lcsa_pool), all-gathers the pooled queries and keys of every rank,
+ * all-gathers the current slice's K and V straight into a reserved cache page (the caller's collective, e.g. NCCL),
+ * commits the page, and calls fvsr_lcsa_forward_shard: the full selection (every rank computes the same one) and the
+ * attention of its own query blocks over all heads. */
+
+/* fvsr_kv_cache_create with a page stride of page_blocks ≥ s blocks (at most 2s + 64): a page can then receive N equal
+ * shards of ceil(s / N) blocks each in one all-gather, the blocks past s being padding that is never read. */
+fvsr_status fvsr_kv_cache_create_padded(const fvsr_lcsa_params* p, int32_t kv_len, int32_t max_new_slices,
+                                        int32_t page_blocks, fvsr_kv_cache** cache);
+/* Device pointers to the next free page (one slice): keys and values (page_blocks·128, H·128) in the cache dtype and
+ * pooled keys (page_blocks, H·128) fp32, to be filled by the caller (window w of the slice at row w·128 / pooled
+ * row w). Calling it again before fvsr_kv_cache_commit returns the same page. Host only. */
+fvsr_status fvsr_kv_cache_reserve(fvsr_kv_cache* cache, void** k_page, void** v_page, float** pooled_k_page);
+/* Appends the reserved page as the newest slice (the concat of DiT.swift:508-511 without a copy). Host only. */
+fvsr_status fvsr_kv_cache_commit(fvsr_kv_cache* cache);
+
+/* The layer call of one rank: selection over pooled_q (Nq, H·128) fp32 — every query block of the chunk — and the
+ * cache's pooled keys (the current slice committed), then, after kv_ready (an event recorded once the K/V gather
+ * into the page is complete; NULL = none), the attention of the items (h, qb) with qb in [qb_begin, qb_end), every
+ * head, longest key list first, then the trim (DiT.swift:532-538). q and out hold only those query blocks:
+ * ((qb_end − qb_begin)·128, H·128) window order. kidx / kcnt (H, Nq, Nk) / (H, Nq): optional outputs for all items.
+ * p->q_slices = the chunk's slices; p->kv_slices is taken from the cache. Same workspace as fvsr_lcsa_forward.
+ * The selection is identical on every rank, so the ranks' outputs together equal fvsr_lcsa_forward's. */
+fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, int32_t qb_begin, int32_t qb_end,
+                                    const float* pooled_q, fvsr_kv_cache* cache, fvsr_event_t kv_ready, void* out,
+                                    int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                                    fvsr_stream_t stream);
 
 /* ---- Token-order entry points: the q/k/v side and the output side of blockForward's self-attention ----
  * Token grid of a chunk: (F, Hp, Wp) = (2·q_slices, 8·bh, 8·bw) patches, L = F·Hp·Wp = Nq·128 tokens in token order

@@ -37,6 +37,7 @@ EXPORTED = [
     "fvsr_lcsa_schedule", "fvsr_lcsa_attention_scheduled", "fvsr_lcsa_prepare", "fvsr_lcsa_forward_tokens",
     "fvsr_stream_chunk_geometry", "fvsr_stream_create", "fvsr_stream_destroy", "fvsr_stream_begin",
     "fvsr_stream_workspace_size", "fvsr_stream_start_chunk", "fvsr_stream_rope", "fvsr_stream_layer",
+    "fvsr_kv_cache_create_padded", "fvsr_kv_cache_reserve", "fvsr_kv_cache_commit", "fvsr_lcsa_forward_shard",
 ]
 
 
@@ -114,6 +115,10 @@ def lib() -> ctypes.CDLL:
         "fvsr_stream_start_chunk": ([P, I32, P], ctypes.c_int),
         "fvsr_stream_rope": ([P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(I64)], ctypes.c_int),
         "fvsr_stream_layer": ([P, I32, P, P, P, P, P, ctypes.c_float, P, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_kv_cache_create_padded": ([PP, I32, I32, I32, ctypes.POINTER(P)], ctypes.c_int),
+        "fvsr_kv_cache_reserve": ([P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)], ctypes.c_int),
+        "fvsr_kv_cache_commit": ([P], ctypes.c_int),
+        "fvsr_lcsa_forward_shard": ([PP, P, I32, I32, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -453,13 +458,16 @@ class FlashVSRAttentionOps:
 class KVCache:
     """The window K/V cache of blockForward (DiT.swift:507-511, 532-538) as slice pages appended in place."""
 
-    def __init__(self, geom: Geometry, kv_len: int, max_new_slices: int):
+    def __init__(self, geom: Geometry, kv_len: int, max_new_slices: int, page_blocks: int | None = None):
+        """page_blocks: arena blocks per page (default s); more leaves room for N equal gathered shards."""
         self.geom = geom
         self.kv_len = kv_len
         self.capacity = kv_len + max_new_slices
+        self.page_blocks = page_blocks or geom.s
         h = ctypes.c_void_p()
         p = geom.params()
-        _check(lib().fvsr_kv_cache_create(ctypes.byref(p), kv_len, max_new_slices, ctypes.byref(h)))
+        _check(lib().fvsr_kv_cache_create_padded(ctypes.byref(p), kv_len, max_new_slices, self.page_blocks,
+                                                 ctypes.byref(h)))
         self.handle = h
 
     def close(self):
@@ -488,6 +496,24 @@ class KVCache:
 
     def trim(self):
         _check(lib().fvsr_kv_cache_trim(self.handle))
+
+    def reserve(self):
+        """The next free page as device views (k (page_blocks·128, H·128), v likewise, pooled k (page_blocks, H·128)
+        fp32), for a collective to fill; commit() then appends it as the newest slice."""
+        torch = _torch()
+        k, v, pk = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib().fvsr_kv_cache_reserve(self.handle, ctypes.byref(k), ctypes.byref(v), ctypes.byref(pk)))
+        rows, c = self.page_blocks * 128, self.geom.channels
+        dt, code = (torch.bfloat16, "<i2") if self.geom.dtype == FVSR_BF16 else (torch.float32, "<f4")
+        views = []
+        for ptr, shape, tcode, tdt in ((k, (rows, c), code, dt), (v, (rows, c), code, dt),
+                                       (pk, (self.page_blocks, c), "<f4", torch.float32)):
+            t = torch.as_tensor(_DeviceArray(ptr.value, shape, tcode), device="cuda")
+            views.append(t.view(tdt) if tdt == torch.bfloat16 else t)
+        return tuple(views)
+
+    def commit(self):
+        _check(lib().fvsr_kv_cache_commit(self.handle))
 
     def state(self) -> list[int]:
         n = ctypes.c_int32(0)
@@ -519,6 +545,50 @@ def lcsa_forward(q, k_new, v_new, cache: KVCache, geom: Geometry, out=None, kidx
     p = geom.params()
     _check(lib().fvsr_lcsa_forward(ctypes.byref(p), _ptr(q2), _ptr(_rows(k_new)), _ptr(_rows(v_new)), cache.handle,
                                    _ptr(out), _ptr(kidx), _ptr(kcnt), _ptr(ws), ws.numel(), _stream(stream)))
+    return out
+
+
+@dataclass(frozen=True)
+class QueryShard:
+    """One rank's query blocks of a chunk split across `world` GPUs: [begin, end) of the chunk's nq windows, and the
+    equal padded shard of `width` blocks every rank contributes to a gather (world·width ≥ nq; the last ranks' shards
+    may hold fewer real blocks, and a rank past the end holds none)."""
+    begin: int
+    end: int
+    width: int
+
+    @property
+    def blocks(self) -> int:
+        return self.end - self.begin
+
+
+def query_shard(nq: int, world: int, rank: int) -> QueryShard:
+    """Contiguous split of a chunk's nq query blocks into shards of width = ceil(nq / world) blocks, in rank order —
+    the layout a sequence-split QKV projection leaves, and the one an all-gather of equal shards reassembles."""
+    if world < 1 or not 0 <= rank < world or nq < 1:
+        raise FVSRError(FVSR_EINVAL, f"bad shard request nq={nq} world={world} rank={rank}")
+    width = -(-nq // world)
+    b = min(nq, rank * width)
+    return QueryShard(b, min(nq, b + width), width)
+
+
+def lcsa_forward_shard(q, shard: QueryShard, pooled_q, cache: KVCache, geom: Geometry, out=None, kv_ready=None,
+                       kidx=None, kcnt=None, workspace=None, stream=None):
+    """One rank's layer call (fvsr_lcsa_forward_shard): the full selection over pooled_q (Nq, H·128) fp32 and the
+    cache's pooled keys (the current slice committed), then the attention of the rank's query blocks over every head
+    after `kv_ready` (a torch.cuda.Event recorded when the K/V gather into the page is done), then the trim.
+    q / out: (shard.blocks·128, H·128) window order."""
+    torch = _torch()
+    q2 = _rows(q)
+    if out is None:
+        out = torch.empty_like(q2)
+    full = Geometry(**{**geom.__dict__, "kv_slices": cache.slices})
+    ws = workspace if workspace is not None else make_workspace(full, q2.device)
+    p = geom.params()
+    ev = None if kv_ready is None else ctypes.c_void_p(kv_ready.cuda_event)
+    _check(lib().fvsr_lcsa_forward_shard(ctypes.byref(p), _ptr(q2), shard.begin, shard.end, _ptr(pooled_q),
+                                         cache.handle, ev, _ptr(_rows(out)), _ptr(kidx), _ptr(kcnt), _ptr(ws),
+                                         ws.numel(), _stream(stream)))
     return out
 
 
@@ -630,10 +700,10 @@ def chunk_geometry(k: int, heads: int, out_h: int, out_w: int, dtype: int = FVSR
 
 
 class _DeviceArray:
-    """An fp32 device buffer of the library, seen by torch through __cuda_array_interface__ (copied, never written)."""
+    """A device buffer of the library seen by torch through __cuda_array_interface__ (fp32 "<f4" or 16-bit "<i2")."""
 
-    def __init__(self, ptr: int, shape: tuple):
-        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 2,
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 2,
                                          "strides": None}
 
 

@@ -202,13 +202,22 @@ struct fvsr_kv_cache {
     fvsr_lcsa_params p;
     Dims d;
     int kv_len, capacity;
+    int page_blocks;             // arena blocks per page: s, or more when a page receives N equal gathered shards
     std::vector<int32_t> pages;  // logical slice order, oldest first → arena page
+    int reserved = -1;           // page handed out by fvsr_kv_cache_reserve and not yet committed
     void* k_arena = nullptr;
     void* v_arena = nullptr;
-    float* pk_arena = nullptr;   // pooled keys, (capacity·s, H·128) fp32
+    float* pk_arena = nullptr;   // pooled keys, (capacity·page_blocks, H·128) fp32
     int device = 0;
-    int64_t page_rows() const { return (int64_t)d.s * 128; }
+    int64_t page_rows() const { return (int64_t)page_blocks * 128; }
     int64_t page_bytes() const { return page_rows() * d.channels * d.elt; }
+    int64_t slice_bytes() const { return (int64_t)d.s * 128 * d.channels * d.elt; }
+    KvPages kv_pages() const {  // the logical slices as the kernels read them
+        KvPages pg{};
+        pg.s = d.s;
+        for (int i = 0; i < kMaxPages; ++i) pg.page_block[i] = (i < (int)pages.size() ? pages[i] : 0) * page_blocks;
+        return pg;
+    }
 };
 
 namespace {
@@ -224,9 +233,10 @@ void choose_pages(const fvsr_kv_cache* c, int new_slices, KvPages* dst, std::vec
         for (int cand = 0; cand < c->capacity && page < 0; ++cand) {
             bool used = false;
             for (int32_t u : *pages) used |= (u == cand);
+            used |= (cand == c->reserved);  // a page handed out for a gather and not yet committed
             if (!used) page = cand;
         }
-        dst->page_block[t] = page * c->d.s;
+        dst->page_block[t] = page * c->page_blocks;
         pages->push_back(page);
     }
 }
@@ -530,6 +540,12 @@ fvsr_status fvsr_lcsa_attention_mask(const fvsr_lcsa_params* p, const void* q, c
 
 fvsr_status fvsr_kv_cache_create(const fvsr_lcsa_params* p, int32_t kv_len, int32_t max_new_slices,
                                  fvsr_kv_cache** cache) {
+    if (!p) return fail(FVSR_EINVAL, "params is NULL");
+    return fvsr_kv_cache_create_padded(p, kv_len, max_new_slices, p->bh * p->bw, cache);
+}
+
+fvsr_status fvsr_kv_cache_create_padded(const fvsr_lcsa_params* p, int32_t kv_len, int32_t max_new_slices,
+                                        int32_t page_blocks, fvsr_kv_cache** cache) {
     Dims d;
     fvsr_status s = check_params(p, &d, false);
     if (s != FVSR_OK) return s;
@@ -537,17 +553,23 @@ fvsr_status fvsr_kv_cache_create(const fvsr_lcsa_params* p, int32_t kv_len, int3
     *cache = nullptr;
     if (kv_len < 1 || max_new_slices < 1 || kv_len + max_new_slices > kMaxPages)
         return fail(FVSR_EINVAL, "need kv_len >= 1, max_new_slices >= 1 and kv_len + max_new_slices <= %d", kMaxPages);
+    if (page_blocks < d.s || page_blocks > 2 * d.s + 64)
+        return fail(FVSR_EINVAL, "page_blocks must be in [s, 2s + 64] = [%d, %d], got %d", d.s, 2 * d.s + 64, page_blocks);
     if ((int64_t)(kv_len + max_new_slices) * d.s > kMaxNk)
         return fail(FVSR_EUNSUPPORTED, "cache of %d key blocks exceeds the supported %d", (kv_len + max_new_slices) * d.s, kMaxNk);
+    if ((int64_t)(kv_len + max_new_slices) * page_blocks * 128 > (1ll << 31) - 1)
+        return fail(FVSR_EUNSUPPORTED, "cache arena of %lld rows is too large",
+                    (long long)(kv_len + max_new_slices) * page_blocks * 128);
     fvsr_kv_cache* c = new (std::nothrow) fvsr_kv_cache();
     if (!c) return fail(FVSR_ENOMEM, "host allocation failed");
     c->p = *p;
     c->d = d;
     c->kv_len = kv_len;
     c->capacity = kv_len + max_new_slices;
+    c->page_blocks = page_blocks;
     cudaGetDevice(&c->device);
     const size_t bytes = (size_t)c->capacity * c->page_bytes();
-    const size_t pbytes = (size_t)c->capacity * d.s * d.channels * 4;
+    const size_t pbytes = (size_t)c->capacity * page_blocks * d.channels * 4;
     if (cudaMalloc(&c->k_arena, bytes) != cudaSuccess || cudaMalloc(&c->v_arena, bytes) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&c->pk_arena), pbytes) != cudaSuccess) {
         cudaGetLastError();
@@ -573,6 +595,32 @@ fvsr_status fvsr_kv_cache_destroy(fvsr_kv_cache* c) {
 fvsr_status fvsr_kv_cache_reset(fvsr_kv_cache* c) {
     if (!c) return fail(FVSR_EINVAL, "cache is NULL");
     c->pages.clear();
+    c->reserved = -1;
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_reserve(fvsr_kv_cache* c, void** k_page, void** v_page, float** pooled_k_page) {
+    if (!c || !k_page || !v_page || !pooled_k_page) return fail(FVSR_EINVAL, "cache and the three outputs are required");
+    if (c->reserved < 0) {
+        if ((int)c->pages.size() + 1 > c->capacity)
+            return fail(FVSR_EINVAL, "no free page: %zu slices held, capacity %d", c->pages.size(), c->capacity);
+        KvPages dst{};
+        std::vector<int32_t> pages;
+        choose_pages(c, 1, &dst, &pages);
+        c->reserved = pages.back();
+    }
+    const int64_t off = (int64_t)c->reserved * c->page_bytes();
+    *k_page = static_cast<uint8_t*>(c->k_arena) + off;
+    *v_page = static_cast<uint8_t*>(c->v_arena) + off;
+    *pooled_k_page = c->pk_arena + (int64_t)c->reserved * c->page_blocks * c->d.channels;
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_kv_cache_commit(fvsr_kv_cache* c) {
+    if (!c) return fail(FVSR_EINVAL, "cache is NULL");
+    if (c->reserved < 0) return fail(FVSR_EINVAL, "no page is reserved");
+    c->pages.push_back(c->reserved);
+    c->reserved = -1;
     return FVSR_OK;
 }
 
@@ -613,12 +661,12 @@ fvsr_status fvsr_kv_cache_gather(const fvsr_kv_cache* c, void* k_out, void* v_ou
     for (size_t i = 0; i < c->pages.size(); ++i) {
         const int64_t off = (int64_t)c->pages[i] * c->page_bytes();
         if (k_out)
-            FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(k_out) + i * c->page_bytes(), static_cast<uint8_t*>(c->k_arena) + off,
-                                    c->page_bytes(), cudaMemcpyDeviceToDevice, st),
+            FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(k_out) + i * c->slice_bytes(), static_cast<uint8_t*>(c->k_arena) + off,
+                                    c->slice_bytes(), cudaMemcpyDeviceToDevice, st),
                     "cache gather (keys)");
         if (v_out)
-            FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(v_out) + i * c->page_bytes(), static_cast<uint8_t*>(c->v_arena) + off,
-                                    c->page_bytes(), cudaMemcpyDeviceToDevice, st),
+            FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(v_out) + i * c->slice_bytes(), static_cast<uint8_t*>(c->v_arena) + off,
+                                    c->slice_bytes(), cudaMemcpyDeviceToDevice, st),
                     "cache gather (values)");
     }
     return FVSR_OK;
@@ -653,10 +701,7 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     s = fvsr_kv_cache_append(cache, k_new, v_new, p->q_slices, stream);
     if (s != FVSR_OK) return s;
-    KvPages pages{};
-    pages.s = d.s;
-    for (int i = 0; i < kMaxPages; ++i)
-        pages.page_block[i] = (i < (int)cache->pages.size() ? cache->pages[i] : 0) * d.s;
+    const KvPages pages = cache->kv_pages();
     int32_t* li = kidx ? kidx : w.kidx;
     int32_t* lc = kcnt ? kcnt : w.kcnt;
     FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, nullptr, 0, nullptr, pp.dtype, (int)d.channels, st, w.hist,
@@ -666,6 +711,52 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     if (s != FVSR_OK) return s;
     s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
                       out, st, 0, d.heads * d.nq, w.order);
+    if (s != FVSR_OK) return s;
+    return fvsr_kv_cache_trim(cache);
+}
+
+fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, int32_t qb_begin, int32_t qb_end,
+                                    const float* pooled_q, fvsr_kv_cache* cache, fvsr_event_t kv_ready, void* out,
+                                    int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                                    fvsr_stream_t stream) {
+    if (!cache) return fail(FVSR_EINVAL, "cache is NULL");
+    if (!p) return fail(FVSR_EINVAL, "params is NULL");
+    if (p->heads != cache->p.heads || p->bh != cache->p.bh || p->bw != cache->p.bw || p->dtype != cache->p.dtype)
+        return fail(FVSR_EINVAL, "params do not match the cache geometry");
+    if (cache->reserved >= 0) return fail(FVSR_EINVAL, "a reserved page is not committed");
+    if ((int)cache->pages.size() < p->q_slices)
+        return fail(FVSR_EINVAL, "the cache holds %zu slices, fewer than the chunk's %d", cache->pages.size(), p->q_slices);
+    if (!q || !out || !pooled_q) return fail(FVSR_EINVAL, "q, pooled_q and out are required");
+    if (!aligned16(q) || !aligned16(out) || !aligned16(pooled_q))
+        return fail(FVSR_EINVAL, "q, pooled_q and out must be 16-byte aligned");
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
+    fvsr_lcsa_params pp = *p;
+    pp.kv_slices = (int32_t)cache->pages.size();
+    Dims d;
+    fvsr_status s = check_params(&pp, &d);
+    if (s != FVSR_OK) return s;
+    if (qb_begin < 0 || qb_end < qb_begin || qb_end > d.nq)
+        return fail(FVSR_EINVAL, "query block range [%d, %d) is outside [0, %d)", qb_begin, qb_end, d.nq);
+    if (qb_end == qb_begin) return fvsr_kv_cache_trim(cache);  // a rank past the end of the chunk: nothing to attend
+    Workspace w = layout(d, workspace);
+    s = check_workspace(w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
+    s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const KvPages pages = cache->kv_pages();
+    int32_t* li = kidx ? kidx : w.kidx;
+    int32_t* lc = kcnt ? kcnt : w.kcnt;
+    FVSR_CU(cudaMemsetAsync(w.hist, 0, select_hist_bytes(d.heads, d.q_slices), st), "histogram clear");
+    FVSR_CU(launch_select(pooled_q, cache->pk_arena, pages, d.heads, d.nq, d.nk, pp.bh, pp.bw, pp.local_range,
+                          pp.q_slices, pp.topk, w.probs, w.hist, li, lc, nullptr, w.order, st, qb_begin, qb_end),
+            "selection launch");
+    if (kv_ready) FVSR_CU(cudaStreamWaitEvent(st, reinterpret_cast<cudaEvent_t>(kv_ready), 0), "wait for the K/V gather");
+    OutRows rows;
+    rows.qbase = qb_begin;
+    rows.q_blocks = qb_end - qb_begin;
+    s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages,
+                      li, lc, out, st, 0, d.heads * (qb_end - qb_begin), w.order, rows);
     if (s != FVSR_OK) return s;
     return fvsr_kv_cache_trim(cache);
 }
@@ -738,10 +829,7 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
     a.zero_words = select_hist_bytes(d.heads, d.q_slices) / 4;
     FVSR_CU(launch_prepare(a, pp.dtype, st), "prepare launch");
     cache->pages = new_pages;
-    KvPages pages{};
-    pages.s = d.s;
-    for (int i = 0; i < kMaxPages; ++i)
-        pages.page_block[i] = (i < (int)cache->pages.size() ? cache->pages[i] : 0) * d.s;
+    const KvPages pages = cache->kv_pages();
     int32_t* li = kidx ? kidx : w.kidx;
     int32_t* lc = kcnt ? kcnt : w.kcnt;
     s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, w.order, st);

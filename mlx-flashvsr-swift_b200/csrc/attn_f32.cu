@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(256) attn_f32_kernel(const float* __restrict__
     for (int idx = tid; idx < kBlock * 32; idx += 256) {
         const int rr = idx >> 5, e4 = idx & 31;
         *reinterpret_cast<float4*>(sm.q + rr * kQS + e4 * 4) =
-            __ldg(reinterpret_cast<const float4*>(q + ((int64_t)qb * kBlock + rr) * ld + h * kD) + e4);
+            __ldg(reinterpret_cast<const float4*>(q + (rows.q_row(qb) + rr) * ld + h * kD) + e4);
     }
     const float scale = 1.0f / sqrtf((float)kD);
     float o[64];

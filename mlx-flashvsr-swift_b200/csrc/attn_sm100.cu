@@ -150,8 +150,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const int x0 = h * kD;
             mbar_expect_tx(bar(kBarQ), kTileBytes);
-            tma_load_2d(sbase + kOffQ, &tmQ, x0, qb * kBlock, bar(kBarQ));
-            tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, x0 + 64, qb * kBlock, bar(kBarQ));
+            const int qy = (int)a.rows.q_row(qb);
+            tma_load_2d(sbase + kOffQ, &tmQ, x0, qy, bar(kBarQ));
+            tma_load_2d(sbase + kOffQ + kBoxBytes, &tmQ, x0 + 64, qy, bar(kBarQ));
             auto load_k = [&](int j) -> bool {
                 const int ks = j % kKSlots;
                 if (j >= kKSlots && !wait(kBarSF + ks, (uint32_t)(j / kKSlots - 1))) return false;  // S_{j−3} done
@@ -343,7 +344,8 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     if (item_count <= 0) return cudaSuccess;
     CUtensorMap mq, mk, mv;
     const int64_t channels = (int64_t)heads * kD;
-    if (!make_tile_map(&mq, q, (int64_t)nq * kBlock, channels) || !make_tile_map(&mk, k, kv_rows, channels) ||
+    const int64_t q_rows = (int64_t)(rows.q_blocks > 0 ? rows.q_blocks : nq) * kBlock;
+    if (!make_tile_map(&mq, q, q_rows, channels) || !make_tile_map(&mk, k, kv_rows, channels) ||
         !make_tile_map(&mv, v, kv_rows, channels))
         return cudaErrorInvalidValue;
     const size_t smem = attn_bf16_smem_bytes(nk);

@@ -31,13 +31,16 @@ __host__ __device__ __forceinline__ int64_t token_row(int bh, int bw, int w, int
     return ((int64_t)(2 * nf + wf) * (8 * bh) + 8 * nh + wh) * (8 * bw) + 8 * nw + ww;
 }
 
-// Where the attention writes output row r of query block qb: window order (bw == 0, row qb·128 + r) or token order
-// (windowReverse fused into the epilogue).
+// Where the attention reads query block qb and writes its output row r: window order (bw == 0), with q and out
+// holding the query blocks [qbase, qbase + q_blocks) (a rank's shard; q_blocks = 0 means all of them, qbase 0), or
+// token order (windowReverse fused into the epilogue; whole chunk only).
 struct OutRows {
     int bh = 0, bw = 0;
+    int qbase = 0, q_blocks = 0;
     __device__ __forceinline__ int64_t row(int qb, int r) const {
-        return bw == 0 ? (int64_t)qb * kBlock + r : token_row(bh, bw, qb, r);
+        return bw == 0 ? (int64_t)(qb - qbase) * kBlock + r : token_row(bh, bw, qb, r);
     }
+    __device__ __forceinline__ int64_t q_row(int qb) const { return (int64_t)(qb - qbase) * kBlock; }
 };
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
@@ -81,9 +84,11 @@ cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst
 // the exact per-(head, query slice) threshold, kidx / kcnt / optional mask, and with `order` non-NULL the
 // longest-first order of all H·nq items. `hist` (select_hist_bytes) must have been cleared by an earlier launch on
 // the stream (the pooling or prepare launch clears it).
+// The order covers the items whose query block lies in [order_q0, order_q1) (all heads); order_q1 <= 0 means all.
 cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk, int bh,
                           int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist, int32_t* kidx,
-                          int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st);
+                          int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st, int order_q0 = 0,
+                          int order_q1 = 0);
 size_t select_smem_bytes();
 size_t select_hist_bytes(int heads, int q_slices);
 // Reads and clears the selection's grid-barrier timeout word of the current device.

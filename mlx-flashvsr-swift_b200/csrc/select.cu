@@ -263,7 +263,8 @@ struct SelArgs {
     int32_t* kidx;
     int32_t* kcnt;
     uint8_t* mask;     // optional
-    int32_t* order;    // optional longest-first order of all H·Nq items
+    int32_t* order;    // optional longest-first order of the items whose query block is in [order_q0, order_q1)
+    int order_q0, order_q1;
 };
 
 // Phase 1 unit — score tile `tile`: kTI query blocks × kTJ key blocks of one head. Thread (ty, tx) computes the 4 × 2
@@ -537,17 +538,18 @@ __device__ __forceinline__ void finish_rows(const SelArgs& a, int64_t r0, int64_
     }
 }
 
-// Longest-first order of one head segment of the items [item_begin, item_begin + item_count) (see launch_item_order):
-// the non-empty items of each head segment in turn (segments in head order), longest key list first within a segment
-// (ties by id); then every empty item of the range, ascending. Empty items only write zeros, so they go last: placed
+// Longest-first order of one head segment of a range of items — the items of [item_begin, item_begin + item_count)
+// whose query block lies in [q0, q1) (see launch_item_order; q0 = 0, q1 = nq for a contiguous range): the non-empty
+// items of each head segment in turn (segments in head order), longest key list first within a segment (ties by id);
+// then every empty item of the range, ascending. Empty items only write zeros, so they go last: placed
 // between heads they would delay the next head's long items. Rank of a non-empty item inside its segment = items of
 // the segment with a longer key list, or an equal one and a smaller id; empty items rank after all non-empty ones, by
 // id. All threads of the group call it; sc (4096 words) and cnt (4 words) are shared scratch of the group.
-__device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item_begin, int item_count,
+__device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item_begin, int item_count, int q0, int q1,
                               int32_t* __restrict__ order, int seg, int32_t* __restrict__ sc, int* __restrict__ cnt,
                               const Grp& g) {
     const int h = item_begin / nq + seg;
-    const int s0 = max(item_begin, h * nq), s1 = min(item_begin + item_count, (h + 1) * nq);
+    const int s0 = max(item_begin, h * nq + q0), s1 = min(item_begin + item_count, h * nq + q1);
     const int n = s1 - s0;
     if (n <= 0) return;  // uniform over the group
     if (g.tid < 4) cnt[g.tid] = 0;
@@ -555,7 +557,8 @@ __device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item
     {
         int na = 0, nb = 0, nc = 0, nd = 0;
         for (int i = g.tid; i < item_count; i += kSelThreads) {
-            const int it = item_begin + i;
+            const int it = item_begin + i, qb = it % nq;
+            if (qb < q0 || qb >= q1) continue;
             const bool nz = __ldcg(kcnt + it) > 0;
             nc += nz;
             if (it < s0) {
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(kSelThreads * kSelGroups, 1) select_fused_kern
     if (!grid_barrier(bar, abort_word, 5 * G)) return;
     const int items = a.heads * a.nq;
     for (int seg = w; seg < a.heads; seg += W)
-        order_segment(a.kcnt, a.nq, 0, items, a.order, seg, reinterpret_cast<int32_t*>(gsm_u),
+        order_segment(a.kcnt, a.nq, 0, items, a.order_q0, a.order_q1, a.order, seg, reinterpret_cast<int32_t*>(gsm_u),
                       reinterpret_cast<int*>(gsm_u + 4096), g);
 }
 
@@ -675,7 +678,7 @@ __global__ void __launch_bounds__(kSelThreads) item_order_kernel(const int32_t* 
     griddep_wait_then_release();
     __shared__ int32_t sc[4096];
     __shared__ int cnt[4];
-    order_segment(kcnt, nq, item_begin, item_count, order, blockIdx.x, sc, cnt, Grp{0, (int)threadIdx.x});
+    order_segment(kcnt, nq, item_begin, item_count, 0, nq, order, blockIdx.x, sc, cnt, Grp{0, (int)threadIdx.x});
 }
 
 }  // namespace
@@ -687,7 +690,8 @@ size_t select_hist_bytes(int heads, int q_slices) { return sizeof(uint32_t) * (s
 
 cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk, int bh,
                           int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist, int32_t* kidx,
-                          int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st) {
+                          int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st, int order_q0,
+                          int order_q1) {
     SelArgs a;
     a.pq = pq;
     a.pk = pk;
@@ -707,6 +711,8 @@ cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pa
     a.kcnt = kcnt;
     a.mask = mask;
     a.order = order;
+    a.order_q0 = order_q1 > 0 ? order_q0 : 0;
+    a.order_q1 = order_q1 > 0 ? order_q1 : nq;
     const int nch = nk <= 256 ? 1 : nk <= 512 ? 2 : nk <= 768 ? 3 : nk <= 1024 ? 4 : 0;
     void (*kernels[5])(SelArgs) = {select_fused_kernel<0>, select_fused_kernel<1>, select_fused_kernel<2>,
                                    select_fused_kernel<3>, select_fused_kernel<4>};
