@@ -522,6 +522,259 @@ def run_ours(args):
     ranks.shutdown()
 
 
+def run_chunk(args):
+    """The metric's workload as the reference streams it: one steady-state chunk of config `--config` (default 3, the
+    1920×1152 chunk) = 30 DiT layers, each layer holding its window cache of kvLen = kv_slices − 1 slices and
+    receiving the chunk's q, k_new and v_new (fresh seeded data per layer, resident in HBM). At N = 1 a layer is one
+    fvsr_lcsa_forward call. At N > 1 the chunk's query blocks are split across the ranks (shard.py): each rank holds
+    only its shard of q / k_new / v_new, pools it, all-gathers the pooled rows and the slice's K/V over NVLink (NCCL,
+    inside the timed region), computes the full selection and attends for its own query blocks. Strong scaling: the
+    chunk is the same at every N; time = max over ranks."""
+    import torch
+    pkg, cfgs = load_pkg()
+    import importlib
+    ranks = importlib.import_module("fvsr_b200.ranks")
+    shard_mod = importlib.import_module("fvsr_b200.shard")
+    info = ranks.rank_info()
+    world, rank, local = info.world, info.rank, info.local
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ranks.init(info, "nccl", timeout_s=120, device=dev)
+    cfg = cfgs.CONFIGS[args.config]
+    g_full = cfg.geometry()                       # q_slices = 1, kv_slices = 3: the steady chunk
+    if g_full.q_slices != 1:
+        raise SystemExit(f"config {args.config} has {g_full.q_slices} query slices; the chunk mode takes one")
+    g = pkg.Geometry(**{**g_full.__dict__})
+    kv_len, layers = g.kv_slices - g.q_slices, args.layers
+    srows = g.s * 128
+    comm = None
+    if world > 1:
+        nccl = importlib.import_module("fvsr_b200.nccl")
+        comm = nccl.Comm(rank, world, dev)
+    sc = shard_mod.ShardedChunk(pkg, g, kv_len, layers, rank, world, comm, dev)
+    sh = sc.shard
+    stream = torch.cuda.current_stream()
+    # per layer: the seeded full tensors of the one-GPU problem (q of the chunk, K/V of cache ⊕ current), of which
+    # this rank keeps its query shard, padded K/V shards of the current slice, and the cache prefill
+    qs, ks, vs, full = [], [], [], []
+    for l in range(layers):
+        q, k, v = cfgs.synth_qkv(cfg, g_full, cfgs.seed_of(args.config, 0, l), device=dev)
+        sc.prefill(l, [k[i * srows:(i + 1) * srows] for i in range(kv_len)],
+                   [v[i * srows:(i + 1) * srows] for i in range(kv_len)])
+        qs.append(q[sh.begin * 128:sh.end * 128].clone())
+        kp = torch.zeros((sc.shard_rows(), g.channels), dtype=q.dtype, device=dev)
+        vp = torch.zeros_like(kp)
+        kp[:sh.blocks * 128] = k[kv_len * srows + sh.begin * 128:kv_len * srows + sh.end * 128]
+        vp[:sh.blocks * 128] = v[kv_len * srows + sh.begin * 128:kv_len * srows + sh.end * 128]
+        ks.append(kp)
+        vs.append(vp)
+        if l < args.roofline_layers:
+            full.append((q, k, v))
+        del q, k, v
+    outs = [torch.empty((sh.blocks * 128, g.channels), dtype=qs[0].dtype, device=dev) for _ in range(2)]
+    kcnt = torch.zeros((layers, g.heads, g.nq), dtype=torch.int32, device=dev)
+
+    def step():
+        for l in range(layers):
+            sc.layer(l, qs[l], ks[l], vs[l], outs[l & 1], kcnt=kcnt[l], stream=stream)
+
+    if comm is not None:                          # set NCCL's connections up before any capture
+        comm.group_start()
+        comm.all_gather(sc.pq_send, sc.pq_full, stream)
+        comm.group_end()
+        comm.group_start()
+        comm.all_gather(ks[0], torch.empty((world * ks[0].shape[0], g.channels), dtype=ks[0].dtype, device=dev),
+                        sc.comm_stream)
+        comm.group_end()
+        torch.cuda.synchronize()
+    launch = "CUDA graph of one step (page choices fixed at capture)"
+    run_step = None
+    if not args.no_graph:
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            run_step = graph.replay
+        except Exception as exc:  # a capture the stack refuses: time the same calls eagerly
+            launch = f"eager (graph capture failed: {type(exc).__name__})"
+            run_step = None
+            for c in sc.caches:   # the failed capture left the page tables mid-step: start the caches over
+                c.reset()
+            for l in range(layers):
+                q, k, v = cfgs.synth_qkv(cfg, g_full, cfgs.seed_of(args.config, 0, l), device=dev)
+                sc.prefill(l, [k[i * srows:(i + 1) * srows] for i in range(kv_len)],
+                           [v[i * srows:(i + 1) * srows] for i in range(kv_len)])
+    if run_step is None:
+        if args.no_graph:
+            launch = "eager"
+        run_step = step
+    for _ in range(max(args.warmup, 3)):
+        run_step()
+    torch.cuda.synchronize()
+    kept = int(kcnt.sum().item())                 # the chunk's kept triples (every rank selects the same)
+    ranks.barrier()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = Clocks(uuid)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_begin = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        run_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks.mark(t_begin, time.time())
+    clk = clocks.stop()
+    ms = ranks.max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    pkg.device_check()
+    if comm is not None:
+        comm.check()
+    if run_step is not step:
+        del graph
+    flops = 4.0 * 128 ** 3 * kept
+
+    # the dominant kernel alone: the attention of whole fresh layers (one GPU's problem), CUDA events on its stream
+    L = pkg.lib()
+    ws = pkg.make_workspace(g_full, dev)
+    kidx1 = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device=dev)
+    kcnt1 = torch.empty((g.heads, g.nq), dtype=torch.int32, device=dev)
+    order = torch.empty(g.heads * g.nq, dtype=torch.int32, device=dev)
+    out1 = torch.empty((g.nq * 128, g.channels), dtype=qs[0].dtype, device=dev)
+    p1 = g_full.params()
+    att_ms, att_kept = [], []
+    for (q, k, v) in full:
+        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p1), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx1),
+                                      pkg._ptr(kcnt1), None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+        pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p1), pkg._ptr(kcnt1), 0, g.heads * g.nq, pkg._ptr(order),
+                                          pkg._stream()))
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p1), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
+                                               pkg._ptr(kidx1), pkg._ptr(kcnt1), pkg._ptr(out1), 0, g.heads * g.nq,
+                                               pkg._ptr(order), pkg._stream()))
+        a1.record(stream)
+        a1.synchronize()
+        att_ms.append(a0.elapsed_time(a1))
+        att_kept.append(int(kcnt1.sum().item()))
+    del full
+    att_avg = sum(att_ms) / len(att_ms)
+    att_tflops = 4.0 * 128 ** 3 * (sum(att_kept) / len(att_kept)) / (att_avg * 1e-3) / 1e12
+
+    # end to end through the public API with host buffers: per layer the rank's q, k_new and v_new shards uploaded
+    # from pinned memory (beside the previous layer's compute) and its output rows read back
+    e2e = None
+    if args.e2e_steps > 0:
+        hq = [qs[l % 3].cpu().pin_memory() for l in range(3)]
+        hk = [ks[l % 3].cpu().pin_memory() for l in range(3)]
+        hv = [vs[l % 3].cpu().pin_memory() for l in range(3)]
+        dq = [torch.empty_like(qs[0]) for _ in range(2)]
+        dk = [torch.empty_like(ks[0]) for _ in range(2)]
+        dv = [torch.empty_like(vs[0]) for _ in range(2)]
+        hout = [torch.empty(outs[0].shape, dtype=outs[0].dtype, pin_memory=True) for _ in range(2)]
+        up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        read = [torch.cuda.Event() for _ in range(2)]
+        for ev in free + read:
+            ev.record(stream)
+        kc2 = torch.zeros_like(kcnt)
+
+        def e2e_step():
+            for l in range(layers):
+                b = l & 1
+                with torch.cuda.stream(up):
+                    up.wait_event(free[b])
+                    dq[b].copy_(hq[l % 3], non_blocking=True)
+                    dk[b].copy_(hk[l % 3], non_blocking=True)
+                    dv[b].copy_(hv[l % 3], non_blocking=True)
+                    ready[b].record(up)
+                stream.wait_event(ready[b])
+                stream.wait_event(read[b])
+                sc.layer(l, dq[b], dk[b], dv[b], outs[b], kcnt=kc2[l], stream=stream)
+                free[b].record(stream)
+                done[b].record(stream)
+                with torch.cuda.stream(down):
+                    down.wait_event(done[b])
+                    hout[b].copy_(outs[b], non_blocking=True)
+                    read[b].record(down)
+            stream.wait_stream(down)
+
+        for _ in range(3):                        # the caches reach their steady state (every slice the same data)
+            e2e_step()
+        torch.cuda.synchronize()
+        kept_e2e = int(kc2.sum().item())
+        ranks.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        pkg.device_check()
+        e2e_ms = ranks.max_over_ranks(f0.elapsed_time(f1) / args.e2e_steps, dev)
+        h2d = sum(t.numel() * t.element_size() for t in (hq[0], hk[0], hv[0])) * layers
+        d2h = outs[0].numel() * outs[0].element_size() * layers
+        e2e = {"value": 4.0 * 128 ** 3 * kept_e2e / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "kind": "per layer: this rank's q / k_new / v_new shards from pinned host memory, the layer call "
+                       "(collectives included), its output rows back to the host"}
+
+    if rank == 0:
+        peak, hbm, peak_kind = peaks()
+        sustained = None
+        try:
+            sustained = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops_sustained"])
+        except Exception:
+            pass
+        tr = profiled_traffic() if args.config == 3 else None
+        value = flops / (ms * 1e-3) / 1e12
+        par = "1 GPU" if world == 1 else (f"{world} GPUs: query blocks split ({sh.width} per rank), pooled rows and "
+                                          f"the slice's K/V all-gathered by NCCL inside the step")
+        line = {
+            "metric": f"block-sparse attn effective TFLOP/s (+ ms per 30-layer chunk), config {args.config}",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if cfg.dtype == "bf16" else "f32",
+            "data": "synthetic (seeded normal Q/K/V per layer, window order, resident in HBM)",
+            "config": {"workload": f"config {args.config}: {cfg.name}, one steady-state streamed chunk",
+                       "layers_per_step": layers, "heads": g.heads, "q_blocks": g.nq, "k_blocks": g.nk,
+                       "kv_len": kv_len, "topk": g.topk, "kept_triples_per_layer": kept / layers,
+                       "l2": f"per layer {3 * g.nq * 128 * g.channels * 2 / 1e6:.0f} MB of chunk data + "
+                             f"{2 * kv_len * srows * g.channels * 2 / 1e6:.0f} MB of cache read (> L2), no flush",
+                       "launch": launch, "parallelism": par},
+            "ms_per_layer": ms / layers,
+            "chunk_frac_of_sustained_peak": (value / world / sustained) if sustained else None,
+            "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
+                         "unit": "TFLOP/s", "frac": att_tflops / peak, "peak_kind": f"{peak_kind} bf16 burst",
+                         "ms_alone_per_layer": att_avg, "traffic": (tr or {}).get("bytes_per_launch"),
+                         "traffic_source": (tr or {}).get("source"),
+                         "timed": f"the attention of {len(att_ms)} whole fresh layers alone, CUDA events"},
+            "clocks": clk,
+            # per layer: N = 1 append (+ key pooling), query pooling, selection, attention; N > 1 two pooling
+            # launches, selection, attention (the collectives are NCCL's kernels, not counted)
+            "gpu_launches": 4 * layers * args.steps,
+            "e2e": e2e,
+        }
+        if not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline(args.config)
+                line["cpu_baseline"].pop("seconds", None)
+            except Exception as exc:  # the baseline is reported, never required
+                line["cpu_baseline"] = {"error": str(exc)}
+        print(json.dumps(line), flush=True)
+    ranks.barrier()
+    sc.close()
+    if comm is not None:
+        comm.destroy()
+    ranks.shutdown()
+
+
 def run_kv_append(args):
     """The window cache's in-place append (fvsr_kv_cache_append + trim, DiT.swift:507-511, 532-538) as HBM traffic:
     per chunk the chunk's q_slices new slices of K and V are read and written into their cache pages and the K slices
@@ -790,6 +1043,10 @@ def main():
                     help="split the config's (head, query block) items across the ranks (default for config 5)")
     ap.add_argument("--replicas", dest="shard", action="store_false",
                     help="one independent copy of the config per rank (default except for config 5)")
+    ap.add_argument("--fresh", action="store_true",
+                    help="30 independent layer calls on fresh full Q/K/V (no cache) instead of a streamed chunk")
+    ap.add_argument("--roofline-layers", type=int, default=8,
+                    help="chunk mode: fresh layers whose attention is timed alone for the roofline")
     ap.add_argument("--kv-append", action="store_true",
                     help="measure the window cache's in-place append (HBM GB/s) instead of the layer step")
     ap.add_argument("--prepare", action="store_true",
@@ -810,8 +1067,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    else:
+    elif args.fresh or args.shard is not None or args.as_rank or args.config == 5:
         run_ours(args)
+    else:
+        run_chunk(args)
 
 
 if __name__ == "__main__":
