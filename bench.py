@@ -664,6 +664,7 @@ def run_chunk(args):
     del full
     att_avg = sum(att_ms) / len(att_ms)
     att_tflops = 4.0 * 128 ** 3 * (sum(att_kept) / len(att_kept)) / (att_avg * 1e-3) / 1e12
+    nsm = torch.cuda.get_device_properties(dev).multi_processor_count
 
     # end to end through the public API with host buffers: per layer the rank's q, k_new and v_new shards uploaded
     # from pinned memory (beside the previous layer's compute) and its output rows read back
@@ -749,12 +750,20 @@ def run_chunk(args):
                              f"{2 * kv_len * srows * g.channels * 2 / 1e6:.0f} MB of cache read (> L2), no flush",
                        "launch": launch, "parallelism": par},
             "ms_per_layer": ms / layers,
-            "chunk_frac_of_sustained_peak": (value / world / sustained) if sustained else None,
-            "roofline": {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
-                         "unit": "TFLOP/s", "frac": att_tflops / peak, "peak_kind": f"{peak_kind} bf16 burst",
-                         "ms_alone_per_layer": att_avg, "traffic": (tr or {}).get("bytes_per_launch"),
-                         "traffic_source": (tr or {}).get("source"),
-                         "timed": f"the attention of {len(att_ms)} whole fresh layers alone, CUDA events"},
+            "chunk_frac_of_sustained_peak": (value / world / sustained) if sustained and cfg.dtype == "bf16" else None,
+            "roofline": (
+                {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
+                 "unit": "TFLOP/s", "frac": att_tflops / peak, "peak_kind": f"{peak_kind} bf16 burst",
+                 "ms_alone_per_layer": att_avg, "traffic": (tr or {}).get("bytes_per_launch"),
+                 "traffic_source": (tr or {}).get("source"),
+                 "timed": f"the attention of {len(att_ms)} whole fresh layers alone, CUDA events"}
+                if cfg.dtype == "bf16" else
+                {"kernel": "attn_f32_kernel", "bound": "fp32 FMA", "achieved": att_tflops,
+                 "peak": nsm * 128 * 2 * (clk.get("sm_mhz") or 1965.0) * 1e6 / 1e12, "unit": "TFLOP/s",
+                 "frac": att_tflops / (nsm * 128 * 2 * (clk.get("sm_mhz") or 1965.0) * 1e6 / 1e12),
+                 "peak_kind": f"FFMA: {nsm} SMs x 128 lanes x 2 FLOP x the sampled SM clock",
+                 "ms_alone_per_layer": att_avg, "traffic": None,
+                 "timed": f"the attention of {len(att_ms)} whole fresh layers alone, CUDA events"}),
             "clocks": clk,
             # per layer: N = 1 append (+ key pooling), query pooling, selection, attention; N > 1 two pooling
             # launches, selection, attention (the collectives are NCCL's kernels, not counted)
@@ -773,6 +782,75 @@ def run_chunk(args):
     if comm is not None:
         comm.destroy()
     ranks.shutdown()
+
+
+def run_stream4(args):
+    """Config 4 as BASELINE.json states it: a streamed sequence of 10 chunks at the 1280×768 output (12 heads, 6×10
+    spatial blocks): chunk 0 carries 3 temporal slices, every later chunk one; kvLen 2 (the window attends to the
+    current slice plus two cached ones); 30 DiT layers per chunk, each with its own window cache appended in place and
+    trimmed (DiT.swift:504-538, fvsr_lcsa_forward); Q/K/V seeded per (chunk, layer) and resident in HBM before the
+    timed region. One step = the whole 10-chunk sequence (the caches start empty). Prints one JSON line."""
+    import torch
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[4]
+    layers, chunks, kv_len = args.layers, 10, 2
+    g0 = cfg.geometry(q_slices=3)
+    srows = g0.s * 128
+    data = []                                   # per chunk, per layer: (q, k_new, v_new, geometry)
+    for c in range(chunks):
+        qs_ = 3 if c == 0 else 1
+        row = []
+        for l in range(layers):
+            have = 0 if c == 0 else min(kv_len, 3 + c - 1)
+            g = cfg.geometry(q_slices=qs_, kv_slices=have + qs_)
+            q, k, v = cfgs.synth_qkv(cfg, g, cfgs.seed_of(4, c, l), kv_rows=qs_ * srows)
+            row.append((q, k, v, g))
+        data.append(row)
+    caches = [pkg.KVCache(g0, kv_len, 3) for _ in range(layers)]
+    wsg = pkg.Geometry(**{**g0.__dict__, "kv_slices": kv_len + 3})
+    ws = pkg.make_workspace(wsg)
+    out = [torch.empty((3 * srows, g0.channels), dtype=torch.bfloat16, device="cuda")]
+    kcnt = [torch.zeros((layers, g0.heads, (3 if c == 0 else 1) * g0.s), dtype=torch.int32, device="cuda")
+            for c in range(chunks)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(chunks + 1)]
+
+    def sequence(timed=False):
+        for c in caches:
+            c.reset()
+        if timed:
+            ev[0].record()
+        for c in range(chunks):
+            for l in range(layers):
+                q, k, v, g = data[c][l]
+                pkg.lcsa_forward(q, k, v, caches[l], g, out=out[0][: q.shape[0]], kcnt=kcnt[c][l], workspace=ws)
+            if timed:
+                ev[c + 1].record()
+
+    for _ in range(max(args.warmup, 3)):
+        sequence()
+    torch.cuda.synchronize()
+    per_chunk = []
+    for _ in range(max(args.steps, 1)):
+        sequence(timed=True)
+        torch.cuda.synchronize()
+        per_chunk.append([ev[c].elapsed_time(ev[c + 1]) for c in range(chunks)])
+    pkg.device_check()
+    kept = [int(kcnt[c].sum().item()) for c in range(chunks)]
+    import statistics
+    ms = [statistics.median(x[c] for x in per_chunk) for c in range(chunks)]
+    total_ms = sum(ms)
+    fl = 4.0 * 128 ** 3
+    for c in caches:
+        c.close()
+    print(json.dumps({
+        "metric": "config 4 streamed sequence: effective TFLOP/s over 10 chunks (+ ms per 30-layer chunk)",
+        "value": fl * sum(kept) / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_sequence": total_ms,
+        "ms_per_chunk": {"chunk0 (3 slices)": ms[0], "steady (median of chunks 1-9)": statistics.median(ms[1:])},
+        "tflops_per_chunk": [fl * kept[c] / (ms[c] * 1e-3) / 1e12 for c in range(chunks)],
+        "kept_triples_per_chunk": kept, "steps": args.steps, "warmup": args.warmup, "gpu_launches_per_layer": 4,
+        "launch": "host C-ABI calls (fvsr_lcsa_forward per layer), CUDA events per chunk",
+        "config": {"workload": "config 4: 1280x768, 12 heads, 6x10 blocks, chunk 0 = 3 slices then 1, kvLen 2, "
+                               "30 layers per chunk, R=11, keep 60%", "dtype": "bf16"}}), flush=True)
 
 
 def run_kv_append(args):
@@ -1051,11 +1129,16 @@ def main():
                     help="measure the window cache's in-place append (HBM GB/s) instead of the layer step")
     ap.add_argument("--prepare", action="store_true",
                     help="measure the token-order q/k/v pass (HBM GB/s) and the token-order layer")
+    ap.add_argument("--stream4", action="store_true",
+                    help="config 4 as a streamed sequence: 10 chunks of 1280x768, chunk 0 of 3 slices, kvLen 2")
     ap.add_argument("--stream", action="store_true",
                     help="run whole chunks through the streaming driver (reference chunk loop and defaults)")
     args = ap.parse_args()
     if args.stream:
         run_stream(args)
+        return
+    if args.stream4:
+        run_stream4(args)
         return
     if args.kv_append:
         run_kv_append(args)
