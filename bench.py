@@ -575,8 +575,9 @@ def run_chunk(args):
     kcnt = torch.zeros((layers, g.heads, g.nq), dtype=torch.int32, device=dev)
 
     def step():
+        st = torch.cuda.current_stream()          # the capture stream inside torch.cuda.graph
         for l in range(layers):
-            sc.layer(l, qs[l], ks[l], vs[l], outs[l & 1], kcnt=kcnt[l], stream=stream)
+            sc.layer(l, qs[l], ks[l], vs[l], outs[l & 1], kcnt=kcnt[l], stream=st)
 
     if comm is not None:                          # set NCCL's connections up before any capture
         comm.group_start()
