@@ -636,7 +636,10 @@ def run_chunk(args):
     if comm is not None:
         comm.check()
     if run_step is not step:
+        run_step = None                           # the bound replay holds the graph (and its NCCL work) alive
+        graph.reset()
         del graph
+    torch.cuda.synchronize()
     flops = 4.0 * 128 ** 3 * kept
 
     # the dominant kernel alone: the attention of whole fresh layers (one GPU's problem), CUDA events on its stream
@@ -779,8 +782,9 @@ def run_chunk(args):
                 line["cpu_baseline"] = {"error": str(exc)}
         print(json.dumps(line), flush=True)
     ranks.barrier()
+    torch.cuda.synchronize()
     sc.close()
-    if comm is not None:
+    if comm is not None:                          # no graph holds NCCL work any more: the teardown cannot wait
         comm.destroy()
     ranks.shutdown()
 
