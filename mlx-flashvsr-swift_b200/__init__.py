@@ -38,6 +38,7 @@ EXPORTED = [
     "fvsr_stream_chunk_geometry", "fvsr_stream_create", "fvsr_stream_destroy", "fvsr_stream_begin",
     "fvsr_stream_workspace_size", "fvsr_stream_start_chunk", "fvsr_stream_rope", "fvsr_stream_layer",
     "fvsr_kv_cache_create_padded", "fvsr_kv_cache_reserve", "fvsr_kv_cache_commit", "fvsr_lcsa_forward_shard",
+    "fvsr_lcsa_partial_size", "fvsr_lcsa_select_shard", "fvsr_lcsa_attend_shard",
 ]
 
 
@@ -119,6 +120,9 @@ def lib() -> ctypes.CDLL:
         "fvsr_kv_cache_reserve": ([P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)], ctypes.c_int),
         "fvsr_kv_cache_commit": ([P], ctypes.c_int),
         "fvsr_lcsa_forward_shard": ([PP, P, I32, I32, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_partial_size": ([PP, I32, I32, ctypes.POINTER(SZ)], ctypes.c_int),
+        "fvsr_lcsa_select_shard": ([PP, P, I32, I32, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_attend_shard": ([PP, P, I32, I32, P, P, P, SZ, P, P, P, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -589,6 +593,35 @@ def lcsa_forward_shard(q, shard: QueryShard, pooled_q, cache: KVCache, geom: Geo
     _check(lib().fvsr_lcsa_forward_shard(ctypes.byref(p), _ptr(q2), shard.begin, shard.end, _ptr(pooled_q),
                                          cache.handle, ev, _ptr(_rows(out)), _ptr(kidx), _ptr(kcnt), _ptr(ws),
                                          ws.numel(), _stream(stream)))
+    return out
+
+
+def partial_size(geom: Geometry, shard: QueryShard) -> int:
+    """Bytes of the fp32 partial results lcsa_attend_shard keeps between its two launches."""
+    n = ctypes.c_size_t(0)
+    p = geom.params()
+    _check(lib().fvsr_lcsa_partial_size(ctypes.byref(p), shard.begin, shard.end, ctypes.byref(n)))
+    return int(n.value)
+
+
+def lcsa_select_shard(pooled_q, shard: QueryShard, cache: KVCache, geom: Geometry, workspace, kidx=None, kcnt=None,
+                      stream=None):
+    """The selection of a rank's layer call (fvsr_lcsa_select_shard): over pooled_q and the cache's pooled keys (the
+    current slice committed), with the longest-first order of the rank's items kept in the workspace."""
+    p = geom.params()
+    _check(lib().fvsr_lcsa_select_shard(ctypes.byref(p), _ptr(pooled_q), shard.begin, shard.end, cache.handle,
+                                        _ptr(kidx), _ptr(kcnt), _ptr(workspace), workspace.numel(), _stream(stream)))
+
+
+def lcsa_attend_shard(q, shard: QueryShard, cache: KVCache, geom: Geometry, workspace, out, kv_ready=None,
+                      partial=None, kidx=None, kcnt=None, stream=None):
+    """The attention of a rank's layer call (fvsr_lcsa_attend_shard): with `partial`, the cached slices' blocks
+    first, then — after kv_ready — the current slice's, merged; then the trim."""
+    p = geom.params()
+    ev = None if kv_ready is None else ctypes.c_void_p(kv_ready.cuda_event)
+    _check(lib().fvsr_lcsa_attend_shard(ctypes.byref(p), _ptr(_rows(q)), shard.begin, shard.end, cache.handle, ev,
+                                        _ptr(partial), 0 if partial is None else partial.numel(), _ptr(_rows(out)),
+                                        _ptr(kidx), _ptr(kcnt), _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
 
 

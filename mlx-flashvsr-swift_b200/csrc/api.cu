@@ -179,13 +179,13 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
 fvsr_status run_attention(const fvsr_lcsa_params* p, const Dims& d, const void* q, const void* k, const void* v,
                           int64_t kv_rows, const KvPages& pages, const int32_t* kidx, const int32_t* kcnt, void* out,
                           cudaStream_t st, int item_begin = 0, int item_count = -1, const int32_t* order = nullptr,
-                          OutRows rows = {}) {
+                          OutRows rows = {}, AttnSplit split = {}) {
     fvsr_status s = check_device_sm100();
     if (s != FVSR_OK) return s;
     if (item_count < 0) item_count = d.heads * d.nq;
     if (p->dtype == FVSR_BF16) {
         FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, item_begin, item_count,
-                                 order, st, rows),
+                                 order, st, rows, split),
                 "bf16 attention launch");
     } else {
         FVSR_CU(launch_attn_f32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
@@ -715,10 +715,14 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     return fvsr_kv_cache_trim(cache);
 }
 
-fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, int32_t qb_begin, int32_t qb_end,
-                                    const float* pooled_q, fvsr_kv_cache* cache, fvsr_event_t kv_ready, void* out,
-                                    int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
-                                    fvsr_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Shared checks of the sharded layer entries: geometry against the cache, the committed current slice, the rank's
+// query block range, the workspace. Fills pp (kv_slices from the cache), d and w.
+fvsr_status shard_setup(const fvsr_lcsa_params* p, int32_t qb_begin, int32_t qb_end, const fvsr_kv_cache* cache,
+                        void* workspace, size_t workspace_bytes, fvsr_lcsa_params* pp, Dims* d, Workspace* w) {
     if (!cache) return fail(FVSR_EINVAL, "cache is NULL");
     if (!p) return fail(FVSR_EINVAL, "params is NULL");
     if (p->heads != cache->p.heads || p->bh != cache->p.bh || p->bw != cache->p.bw || p->dtype != cache->p.dtype)
@@ -726,39 +730,121 @@ fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, in
     if (cache->reserved >= 0) return fail(FVSR_EINVAL, "a reserved page is not committed");
     if ((int)cache->pages.size() < p->q_slices)
         return fail(FVSR_EINVAL, "the cache holds %zu slices, fewer than the chunk's %d", cache->pages.size(), p->q_slices);
-    if (!q || !out || !pooled_q) return fail(FVSR_EINVAL, "q, pooled_q and out are required");
-    if (!aligned16(q) || !aligned16(out) || !aligned16(pooled_q))
-        return fail(FVSR_EINVAL, "q, pooled_q and out must be 16-byte aligned");
-    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
-    fvsr_lcsa_params pp = *p;
-    pp.kv_slices = (int32_t)cache->pages.size();
+    *pp = *p;
+    pp->kv_slices = (int32_t)cache->pages.size();
+    fvsr_status s = check_params(pp, d);
+    if (s != FVSR_OK) return s;
+    if (qb_begin < 0 || qb_end < qb_begin || qb_end > d->nq)
+        return fail(FVSR_EINVAL, "query block range [%d, %d) is outside [0, %d)", qb_begin, qb_end, d->nq);
+    *w = layout(*d, workspace);
+    s = check_workspace(*w, workspace, workspace_bytes);
+    if (s != FVSR_OK) return s;
+    return check_device_sm100();
+}
+
+size_t partial_bytes(const Dims& d, int32_t qb_begin, int32_t qb_end) {
+    return (size_t)d.heads * (size_t)(qb_end - qb_begin) * kBlock * (kD + 2) * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" {
+
+fvsr_status fvsr_lcsa_partial_size(const fvsr_lcsa_params* p, int32_t qb_begin, int32_t qb_end, size_t* bytes) {
     Dims d;
-    fvsr_status s = check_params(&pp, &d);
+    fvsr_status s = check_params(p, &d, false);
     if (s != FVSR_OK) return s;
-    if (qb_begin < 0 || qb_end < qb_begin || qb_end > d.nq)
-        return fail(FVSR_EINVAL, "query block range [%d, %d) is outside [0, %d)", qb_begin, qb_end, d.nq);
-    if (qb_end == qb_begin) return fvsr_kv_cache_trim(cache);  // a rank past the end of the chunk: nothing to attend
-    Workspace w = layout(d, workspace);
-    s = check_workspace(w, workspace, workspace_bytes);
+    if (!bytes) return fail(FVSR_EINVAL, "bytes is NULL");
+    if (qb_begin < 0 || qb_end < qb_begin) return fail(FVSR_EINVAL, "bad query block range [%d, %d)", qb_begin, qb_end);
+    *bytes = partial_bytes(d, qb_begin, qb_end);
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_select_shard(const fvsr_lcsa_params* p, const float* pooled_q, int32_t qb_begin, int32_t qb_end,
+                                   fvsr_kv_cache* cache, int32_t* kidx, int32_t* kcnt, void* workspace,
+                                   size_t workspace_bytes, fvsr_stream_t stream) {
+    fvsr_lcsa_params pp;
+    Dims d;
+    Workspace w;
+    fvsr_status s = shard_setup(p, qb_begin, qb_end, cache, workspace, workspace_bytes, &pp, &d, &w);
     if (s != FVSR_OK) return s;
-    s = check_device_sm100();
-    if (s != FVSR_OK) return s;
+    if (!pooled_q) return fail(FVSR_EINVAL, "pooled_q is required");
+    if (!aligned16(pooled_q)) return fail(FVSR_EINVAL, "pooled_q must be 16-byte aligned");
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const KvPages pages = cache->kv_pages();
-    int32_t* li = kidx ? kidx : w.kidx;
-    int32_t* lc = kcnt ? kcnt : w.kcnt;
     FVSR_CU(cudaMemsetAsync(w.hist, 0, select_hist_bytes(d.heads, d.q_slices), st), "histogram clear");
-    FVSR_CU(launch_select(pooled_q, cache->pk_arena, pages, d.heads, d.nq, d.nk, pp.bh, pp.bw, pp.local_range,
-                          pp.q_slices, pp.topk, w.probs, w.hist, li, lc, nullptr, w.order, st, qb_begin, qb_end),
+    FVSR_CU(launch_select(pooled_q, cache->pk_arena, cache->kv_pages(), d.heads, d.nq, d.nk, pp.bh, pp.bw,
+                          pp.local_range, pp.q_slices, pp.topk, w.probs, w.hist, kidx ? kidx : w.kidx,
+                          kcnt ? kcnt : w.kcnt, nullptr, w.order, st, qb_begin, qb_end),
             "selection launch");
-    if (kv_ready) FVSR_CU(cudaStreamWaitEvent(st, reinterpret_cast<cudaEvent_t>(kv_ready), 0), "wait for the K/V gather");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_lcsa_attend_shard(const fvsr_lcsa_params* p, const void* q, int32_t qb_begin, int32_t qb_end,
+                                   fvsr_kv_cache* cache, fvsr_event_t kv_ready, void* partial, size_t partial_size,
+                                   void* out, const int32_t* kidx, const int32_t* kcnt, void* workspace,
+                                   size_t workspace_bytes, fvsr_stream_t stream) {
+    fvsr_lcsa_params pp;
+    Dims d;
+    Workspace w;
+    fvsr_status s = shard_setup(p, qb_begin, qb_end, cache, workspace, workspace_bytes, &pp, &d, &w);
+    if (s != FVSR_OK) return s;
+    if (!q || !out) return fail(FVSR_EINVAL, "q and out are required");
+    if (!aligned16(q) || !aligned16(out) || !aligned16(partial))
+        return fail(FVSR_EINVAL, "q, out and partial must be 16-byte aligned");
+    if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
+    if (partial && partial_size < partial_bytes(d, qb_begin, qb_end))
+        return fail(FVSR_ENOMEM, "partial buffer of %zu bytes is smaller than the %zu required", partial_size,
+                    partial_bytes(d, qb_begin, qb_end));
+    if (qb_end == qb_begin) return fvsr_kv_cache_trim(cache);  // a rank past the end of the chunk: nothing to attend
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaEvent_t ev = reinterpret_cast<cudaEvent_t>(kv_ready);
+    const KvPages pages = cache->kv_pages();
+    const int32_t* li = kidx ? kidx : w.kidx;
+    const int32_t* lc = kcnt ? kcnt : w.kcnt;
     OutRows rows;
     rows.qbase = qb_begin;
     rows.q_blocks = qb_end - qb_begin;
-    s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages,
-                      li, lc, out, st, 0, d.heads * (qb_end - qb_begin), w.order, rows);
+    const int items = d.heads * (qb_end - qb_begin);
+    const int64_t kv_rows = (int64_t)cache->capacity * cache->page_rows();
+    if (partial && pp.dtype == FVSR_BF16) {
+        // the cached slices' blocks first (they are in the cache already), the chunk's own slices' blocks once the
+        // gather has landed, merged in the second launch's epilogue
+        AttnSplit sp;
+        sp.split_nk = (pp.kv_slices - pp.q_slices) * d.s;
+        sp.part_o = static_cast<float*>(partial);
+        sp.part_ml = sp.part_o + (size_t)items * kBlock * kD;
+        sp.part = 1;
+        s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, kv_rows, pages, li, lc, out, st, 0, items, w.order,
+                          rows, sp);
+        if (s != FVSR_OK) return s;
+        if (ev) FVSR_CU(cudaStreamWaitEvent(st, ev, 0), "wait for the K/V gather");
+        sp.part = 2;
+        s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, kv_rows, pages, li, lc, out, st, 0, items, w.order,
+                          rows, sp);
+    } else {
+        if (ev) FVSR_CU(cudaStreamWaitEvent(st, ev, 0), "wait for the K/V gather");
+        s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, kv_rows, pages, li, lc, out, st, 0, items, w.order,
+                          rows);
+    }
     if (s != FVSR_OK) return s;
     return fvsr_kv_cache_trim(cache);
+}
+
+fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, int32_t qb_begin, int32_t qb_end,
+                                    const float* pooled_q, fvsr_kv_cache* cache, fvsr_event_t kv_ready, void* out,
+                                    int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
+                                    fvsr_stream_t stream) {
+    fvsr_lcsa_params pp;
+    Dims d;
+    Workspace w;
+    fvsr_status s = shard_setup(p, qb_begin, qb_end, cache, workspace, workspace_bytes, &pp, &d, &w);
+    if (s != FVSR_OK) return s;
+    if (qb_end == qb_begin) return fvsr_kv_cache_trim(cache);
+    s = fvsr_lcsa_select_shard(p, pooled_q, qb_begin, qb_end, cache, kidx, kcnt, workspace, workspace_bytes, stream);
+    if (s != FVSR_OK) return s;
+    return fvsr_lcsa_attend_shard(p, q, qb_begin, qb_end, cache, kv_ready, nullptr, 0, out, kidx, kcnt, workspace,
+                                  workspace_bytes, stream);
 }
 
 fvsr_status fvsr_lcsa_prepare(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin, const void* v_lin,

@@ -79,6 +79,7 @@ struct AttnArgs {
     float scale_log2;
     KvPages pages;
     OutRows rows;
+    AttnSplit split;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -94,8 +95,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int cnt = a.kcnt[item];
     cnt = cnt < 0 ? 0 : (cnt > a.nk ? a.nk : cnt);
+    int lo = 0;  // first list entry this launch walks
+    const size_t slot = blockIdx.x;
+    if (a.split.part != 0) {
+        // the list is ascending, so its blocks below split_nk are a prefix: count it with the whole CTA
+        const int32_t* gl = a.kidx + (int64_t)item * a.nk;
+        int c1 = 0;
+        for (int j0 = 0; j0 < cnt; j0 += kThreads) {
+            const int j = j0 + (int)threadIdx.x;
+            c1 += __syncthreads_count(j < cnt && gl[j] < a.split.split_nk);
+        }
+        lo = a.split.part == 1 ? 0 : c1;
+        cnt = a.split.part == 1 ? c1 : cnt - c1;
+    }
 
-    if (cnt == 0) {  // SparseAttention.swift:47-53: a query block that selected nothing writes zeros
+    if (cnt == 0) {
+        if (a.split.part == 1) {  // nothing below the split: an empty partial (row sum 0, row maximum −inf)
+            float4* po = reinterpret_cast<float4*>(a.split.part_o + slot * kBlock * kD);
+            for (int idx = threadIdx.x; idx < kBlock * kD / 4; idx += kThreads) po[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = threadIdx.x; r < kBlock; r += kThreads) {
+                a.split.part_ml[(slot * kBlock + r) * 2] = -INFINITY;
+                a.split.part_ml[(slot * kBlock + r) * 2 + 1] = 0.0f;
+            }
+            return;
+        }
+        if (a.split.part == 2) {  // nothing from the split on: the first part's result alone (zeros if it was empty)
+            for (int idx = threadIdx.x; idx < kBlock * 16; idx += kThreads) {
+                const int r = idx >> 4, c = idx & 15;
+                const float l = a.split.part_ml[(slot * kBlock + r) * 2 + 1];
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                const float4* po = reinterpret_cast<const float4*>(a.split.part_o + (slot * kBlock + r) * kD + c * 8);
+                const float4 x0 = po[0], x1 = po[1];
+                *reinterpret_cast<uint4*>(a.out + a.rows.row(qb, r) * ld + h * kD + c * 8) =
+                    make_uint4(pack_bf16x2(x0.x * inv, x0.y * inv), pack_bf16x2(x0.z * inv, x0.w * inv),
+                               pack_bf16x2(x1.x * inv, x1.y * inv), pack_bf16x2(x1.z * inv, x1.w * inv));
+            }
+            return;
+        }
+        // SparseAttention.swift:47-53: a query block that selected nothing writes zeros
         for (int idx = threadIdx.x; idx < kBlock * 16; idx += kThreads) {
             const int r = idx >> 4, c = idx & 15;
             *reinterpret_cast<uint4*>(a.out + a.rows.row(qb, r) * ld + h * kD + c * 8) = make_uint4(0, 0, 0, 0);
@@ -130,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
     }
-    const int32_t* glist = a.kidx + (int64_t)item * a.nk;
+    const int32_t* glist = a.kidx + (int64_t)item * a.nk + lo;
     for (int j = threadIdx.x; j < cnt; j += kThreads) {
         int kb = glist[j];
         kb = kb < 0 ? 0 : (kb >= a.nk ? a.nk - 1 : kb);
@@ -309,20 +346,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float l0 = fin[r], m0 = fin[128 + r], l1 = fin[256 + r], m1 = fin[384 + r];
             const float mf = fmaxf(m0, m1);
             const float l_row = l0 * ex2_approx(m0 - mf) + l1 * ex2_approx(m1 - mf);
-            const float inv = 1.0f / l_row;
-            __nv_bfloat16* orow = a.out + a.rows.row(qb, r) * ld + h * kD + 64 * st;
+            if (a.split.part == 1) {  // unnormalised O (relative to mf), the row maximum and sum: the partial
+                float* po = a.split.part_o + (slot * kBlock + r) * kD + 64 * st;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t ov[32];
-                tmem_ld32(lane_base + kColO + 64u * (uint32_t)st + 32u * c, ov);
-                tmem_ld_wait(ov);
-                uint32_t w[16];
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t ov[32];
+                    tmem_ld32(lane_base + kColO + 64u * (uint32_t)st + 32u * c, ov);
+                    tmem_ld_wait(ov);
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    w[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv, __uint_as_float(ov[2 * i + 1]) * inv);
-                uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+                    for (int i = 0; i < 8; ++i)
+                        reinterpret_cast<float4*>(po + 32 * c)[i] =
+                            make_float4(__uint_as_float(ov[4 * i]), __uint_as_float(ov[4 * i + 1]),
+                                        __uint_as_float(ov[4 * i + 2]), __uint_as_float(ov[4 * i + 3]));
+                }
+                if (st == 0) {
+                    a.split.part_ml[(slot * kBlock + r) * 2] = mf;
+                    a.split.part_ml[(slot * kBlock + r) * 2 + 1] = l_row;
+                }
+            } else {
+                // part 2 merges the first part's partial: O = (O_a·2^(m_a−M) + O_b·2^(m_b−M)) / (l_a·… + l_b·…)
+                float ca = 0.0f, cb = 1.0f, lt = l_row;
+                const float* pa = nullptr;
+                if (a.split.part == 2) {
+                    const float ma = a.split.part_ml[(slot * kBlock + r) * 2];
+                    const float la = a.split.part_ml[(slot * kBlock + r) * 2 + 1];
+                    const float big = fmaxf(ma, mf);
+                    ca = la > 0.0f ? ex2_approx(ma - big) : 0.0f;
+                    cb = ex2_approx(mf - big);
+                    lt = la * ca + l_row * cb;
+                    pa = a.split.part_o + (slot * kBlock + r) * kD + 64 * st;
+                }
+                const float inv = 1.0f / lt;
+                __nv_bfloat16* orow = a.out + a.rows.row(qb, r) * ld + h * kD + 64 * st;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t ov[32];
+                    tmem_ld32(lane_base + kColO + 64u * (uint32_t)st + 32u * c, ov);
+                    tmem_ld_wait(ov);
+                    if (pa) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 x = reinterpret_cast<const float4*>(pa + 32 * c)[i];
+                            ov[4 * i] = __float_as_uint(fmaf(x.x, ca, __uint_as_float(ov[4 * i]) * cb));
+                            ov[4 * i + 1] = __float_as_uint(fmaf(x.y, ca, __uint_as_float(ov[4 * i + 1]) * cb));
+                            ov[4 * i + 2] = __float_as_uint(fmaf(x.z, ca, __uint_as_float(ov[4 * i + 2]) * cb));
+                            ov[4 * i + 3] = __float_as_uint(fmaf(x.w, ca, __uint_as_float(ov[4 * i + 3]) * cb));
+                        }
+                    }
+                    uint32_t w[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        w[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv, __uint_as_float(ov[2 * i + 1]) * inv);
+                    uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+                }
             }
         }
     }
@@ -340,7 +418,8 @@ size_t attn_bf16_smem_bytes(int nk) { return 1024 + kOffList + sizeof(int32_t) *
 
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
-                             int item_begin, int item_count, const int32_t* order, cudaStream_t st, OutRows rows) {
+                             int item_begin, int item_count, const int32_t* order, cudaStream_t st, OutRows rows,
+                             AttnSplit split) {
     if (item_count <= 0) return cudaSuccess;
     CUtensorMap mq, mk, mv;
     const int64_t channels = (int64_t)heads * kD;
@@ -363,6 +442,7 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     a.scale_log2 = (1.0f / sqrtf((float)kD)) * 1.4426950408889634f;
     a.pages = pages;
     a.rows = rows;
+    a.split = split;
     return launch_pdl(attn_bf16_sm100_kernel, dim3(item_count), dim3(kThreads), smem, st, mq, mk, mv, a);
 }
 

@@ -101,10 +101,20 @@ cudaError_t launch_mask_to_lists(const float* mask, int heads, int nq, int nk, i
 cudaError_t launch_attn_f32(const float* q, const float* k, const float* v, const KvPages& pages, int heads, int nq,
                             int nk, const int32_t* kidx, const int32_t* kcnt, float* out, int item_begin,
                             int item_count, const int32_t* order, cudaStream_t st, OutRows rows = {});
+// A key list split at key block split_nk (the lists are ascending): part 0 = the whole list (no split); part 1 = the
+// blocks below split_nk, written unnormalised to fp32 partials — O (slot, 128, 128) and (row maximum in log2 units,
+// row sum) (slot, 128, 2), slot = the CTA's position in the launch; part 2 = the blocks from split_nk on, merged with
+// part 1's partials (same order, same slots) into the output. Lets the cached slices' blocks run while the current
+// slice's keys are still arriving.
+struct AttnSplit {
+    int part = 0, split_nk = 0;
+    float* part_o = nullptr;
+    float* part_ml = nullptr;
+};
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
                              int item_begin, int item_count, const int32_t* order, cudaStream_t st,
-                             OutRows rows = {});
+                             OutRows rows = {}, AttnSplit split = {});
 // The q/k/v side of one layer from the linear outputs (prepare.cu). Token grid (2·q_slices, 8·bh, 8·bw); nq windows.
 struct PrepArgs {
     const void* x[3];        // q, k, v linear outputs, token order (L, C)

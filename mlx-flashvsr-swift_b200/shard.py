@@ -6,10 +6,13 @@ projection leaves them — and, per DiT layer, a replica of that layer's window 
   1. pool the rank's q and k_new shards (fvsr_lcsa_pool: the fp32 block means of DiT.swift:161-162);
   2. all-gather the pooled rows of every rank: the queries into one (Nq, H·128) buffer, the keys straight into the
      cache page reserved for the current slice — on the compute stream (1.7 MB at config 3);
-  3. all-gather the current slice's K and V shards straight into that page, on a communication stream, beside the
-     selection (106 MB at config 3, 189 MB at config 5) — the concat of DiT.swift:508-511 without a copy;
-  4. fvsr_lcsa_forward_shard: the full selection over the gathered pooled rows (every rank computes the same one),
-     a wait for the K/V gather, the attention of the rank's query blocks over every head, and the trim.
+  3. fvsr_lcsa_select_shard: the full selection over the gathered pooled rows (every rank computes the same one);
+  4. all-gather the current slice's K and V shards straight into that page on a communication stream (106 MB at
+     config 3, 189 MB at config 5) — the concat of DiT.swift:508-511 without a copy. It starts after the selection,
+     whose one cooperative launch needs every SM, and runs beside
+  5. fvsr_lcsa_attend_shard: the attention of the rank's query blocks over every head — first the kept blocks in
+     the cached slices (fp32 partials), then, once the gather has landed, the current slice's blocks, merged — and
+     the trim.
 The gathers write equal padded shards of ceil(Nq / N) blocks, so the cache pages are ceil(Nq / N)·N blocks long.
 At N = 1 the same call is fvsr_lcsa_forward (append, select, attend, trim) with no collective.
 """
@@ -21,7 +24,8 @@ import ctypes
 class ShardedChunk:
     """Per-rank state of the partition for `layers` DiT layers of one chunk geometry (q_slices = 1: a steady chunk)."""
 
-    def __init__(self, pkg, geom, kv_len: int, layers: int, rank: int, world: int, comm=None, device=None):
+    def __init__(self, pkg, geom, kv_len: int, layers: int, rank: int, world: int, comm=None, device=None,
+                 split: bool = True):
         import torch
         if geom.q_slices != 1:
             raise pkg.FVSRError(pkg.FVSR_EINVAL, "the sharded chunk takes one temporal slice per chunk")
@@ -40,6 +44,8 @@ class ShardedChunk:
         self.pq_full = torch.zeros((w * world, c), dtype=torch.float32, device=self.device)
         self.full = pkg.Geometry(**{**geom.__dict__, "kv_slices": kv_len + 1})
         self.workspace = pkg.make_workspace(self.full, self.device)
+        self.partial = (torch.empty(pkg.partial_size(geom, self.shard), dtype=torch.uint8, device=self.device)
+                        if split and geom.dtype == pkg.FVSR_BF16 and self.shard.blocks else None)
         self.comm_stream = torch.cuda.Stream(device=self.device)
         self.kv_ready = [torch.cuda.Event() for _ in range(2)]
         self.calls = 0
@@ -77,7 +83,10 @@ class ShardedChunk:
         self.comm.all_gather(self.pq_send, self.pq_full, st)
         self.comm.all_gather(self.pk_send, pk_page, st)
         self.comm.group_end()
-        # the slice's K and V: beside the selection, after every earlier use of this page on the compute stream
+        cache.commit()
+        pkg.lcsa_select_shard(self.pq_full, sh, cache, g, self.workspace, kcnt=kcnt, stream=st)
+        # the slice's K and V, after the selection (and every earlier use of this page) on the compute stream, beside
+        # the attention of the cached slices
         ev = self.kv_ready[self.calls & 1]
         self.calls += 1
         self.comm_stream.wait_stream(st)
@@ -86,9 +95,8 @@ class ShardedChunk:
         self.comm.all_gather(v_new, v_page, self.comm_stream)
         self.comm.group_end()
         ev.record(self.comm_stream)
-        cache.commit()
-        pkg.lcsa_forward_shard(q, sh, self.pq_full, cache, g, out=out, kv_ready=ev, kcnt=kcnt,
-                               workspace=self.workspace, stream=st)
+        pkg.lcsa_attend_shard(q, sh, cache, g, self.workspace, out, kv_ready=ev, partial=self.partial, kcnt=kcnt,
+                              stream=st)
         return out
 
     def close(self) -> None:

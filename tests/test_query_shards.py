@@ -35,17 +35,39 @@ def _slices(cfgs, cfg, g, seed, n):
     return [(0.5 * torch.randn((rows, g.channels), generator=gen, device="cuda")).to(torch.bfloat16) for _ in range(n)]
 
 
+def _rank_cache(fvsr, g, sh, world, k0, v0, k1, v1, kn, vn):
+    """A rank's cache after the gathers: two cached slices, and the current slice's padded shards (what the
+    all-gathers of every rank's shard write) committed as the newest page."""
+    w = sh.width
+    cache = fvsr.KVCache(g, 2, 1, page_blocks=w * world)
+    for k, v in ((k0, v0), (k1, v1)):
+        cache.append(k, v, 1)
+    kp, vp, pkp = cache.reserve()
+    assert kp.shape == (w * world * 128, g.channels) and pkp.shape == (w * world, g.channels)
+    for r2 in range(world):
+        s2 = fvsr.query_shard(g.nq, world, r2)
+        if s2.blocks:
+            kp[r2 * w * 128:r2 * w * 128 + s2.blocks * 128] = kn[s2.begin * 128:s2.end * 128]
+            vp[r2 * w * 128:r2 * w * 128 + s2.blocks * 128] = vn[s2.begin * 128:s2.end * 128]
+            pkp[r2 * w:r2 * w + s2.blocks] = fvsr.pool(kn[s2.begin * 128:s2.end * 128], g)
+    cache.commit()
+    return cache
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("cfg_id,world", [(2, 2), (2, 7), (3, 8)])
-def test_emulated_ranks_reassemble_the_one_gpu_layer(fvsr, cfg_id, world):
+def test_emulated_ranks_reassemble_the_one_gpu_layer(fvsr, orc, cfg_id, world):
+    """Every rank in turn on one GPU. One-launch form (fvsr_lcsa_forward_shard): the selection and the rank's output
+    rows equal fvsr_lcsa_forward's bit for bit. Split form (select, then the cached slices' blocks into fp32
+    partials, then the current slice's merged): the selection is the same and the rows are within the bf16 bar of
+    the fp32 oracle, as the one-launch rows are."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     cfgs = importlib.import_module("fvsr_b200.configs")
     cfg = cfgs.CONFIGS[cfg_id]
     g = cfg.geometry(q_slices=1, kv_slices=3)
-    kv_len, srows = 2, g.s * 128
     k0, v0, k1, v1, q, kn, vn = _slices(cfgs, cfg, g, 40 + world, 7)
-    ref_cache = fvsr.KVCache(g, kv_len, 1)
+    ref_cache = fvsr.KVCache(g, 2, 1)
     for k, v in ((k0, v0), (k1, v1)):
         ref_cache.append(k, v, 1)
     kidx = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device="cuda")
@@ -53,32 +75,43 @@ def test_emulated_ranks_reassemble_the_one_gpu_layer(fvsr, cfg_id, world):
     ref = fvsr.lcsa_forward(q, kn, vn, ref_cache, g, kidx=kidx, kcnt=kcnt)
     ref_k, ref_v = ref_cache.gather()
     pq_full = fvsr.pool(q, g)
+    oracle = orc.attention(q.float().cpu().numpy(), torch.cat([k0, k1, kn]).float().cpu().numpy(),
+                           torch.cat([v0, v1, vn]).float().cpu().numpy(), kidx.cpu().numpy(), kcnt.cpu().numpy(),
+                           g.heads, fast=True)
+    full = fvsr.Geometry(**{**g.__dict__, "kv_slices": 3})
     for r in range(world):
         sh = fvsr.query_shard(g.nq, world, r)
-        w = sh.width
-        cache = fvsr.KVCache(g, kv_len, 1, page_blocks=w * world)
-        for k, v in ((k0, v0), (k1, v1)):
-            cache.append(k, v, 1)
-        kp, vp, pkp = cache.reserve()
-        assert kp.shape == (w * world * 128, g.channels) and pkp.shape == (w * world, g.channels)
-        for r2 in range(world):                     # what the all-gathers of the padded shards write
-            s2 = fvsr.query_shard(g.nq, world, r2)
-            if s2.blocks:
-                kp[r2 * w * 128:r2 * w * 128 + s2.blocks * 128] = kn[s2.begin * 128:s2.end * 128]
-                vp[r2 * w * 128:r2 * w * 128 + s2.blocks * 128] = vn[s2.begin * 128:s2.end * 128]
-                pkp[r2 * w:r2 * w + s2.blocks] = fvsr.pool(kn[s2.begin * 128:s2.end * 128], g)
-        cache.commit()
+        rows = slice(sh.begin * 128, sh.end * 128)
+        cache = _rank_cache(fvsr, g, sh, world, k0, v0, k1, v1, kn, vn)
         rk = torch.full_like(kidx, -7)
         rc = torch.full_like(kcnt, -7)
         out = torch.empty((sh.blocks * 128, g.channels), dtype=torch.bfloat16, device="cuda")
         if sh.blocks:
-            fvsr.lcsa_forward_shard(q[sh.begin * 128:sh.end * 128], sh, pq_full, cache, g, out=out, kidx=rk, kcnt=rc)
+            fvsr.lcsa_forward_shard(q[rows], sh, pq_full, cache, g, out=out, kidx=rk, kcnt=rc)
             torch.cuda.synchronize()
             assert torch.equal(rk, kidx) and torch.equal(rc, kcnt), f"rank {r}: selection differs"
-            assert torch.equal(out.view(torch.int16), ref[sh.begin * 128:sh.end * 128].view(torch.int16)), r
-        assert cache.slices == kv_len
+            assert torch.equal(out.view(torch.int16), ref[rows].view(torch.int16)), r
+        assert cache.slices == 2
         ck, cv = cache.gather()
         assert torch.equal(ck, ref_k) and torch.equal(cv, ref_v)
+        cache.close()
+        if not sh.blocks:
+            continue
+        # the split form, on a fresh copy of the rank's cache
+        cache = _rank_cache(fvsr, g, sh, world, k0, v0, k1, v1, kn, vn)
+        ws = fvsr.make_workspace(full)
+        part = torch.empty(fvsr.partial_size(g, sh), dtype=torch.uint8, device="cuda")
+        rc2 = torch.full_like(kcnt, -7)
+        out2 = torch.empty_like(out)
+        fvsr.lcsa_select_shard(pq_full, sh, cache, g, ws, kcnt=rc2)
+        fvsr.lcsa_attend_shard(q[rows], sh, cache, g, ws, out2, partial=part, kcnt=rc2)
+        torch.cuda.synchronize()
+        assert torch.equal(rc2, kcnt)
+        got = out2.float().cpu().numpy()
+        cmp = orc.compare(got, oracle[rows])
+        assert cmp["rel"] <= 1e-2, (r, cmp)
+        assert orc.compare(got, out.float().cpu().numpy())["rel"] <= 1e-2
+        assert cache.slices == 2
         cache.close()
     ref_cache.close()
     fvsr.device_check()
