@@ -46,7 +46,9 @@ class ShardedChunk:
         self.workspace = pkg.make_workspace(self.full, self.device)
         self.partial = (torch.empty(pkg.partial_size(geom, self.shard), dtype=torch.uint8, device=self.device)
                         if split and geom.dtype == pkg.FVSR_BF16 and self.shard.blocks else None)
-        self.comm_stream = torch.cuda.Stream(device=self.device)
+        # the gathers' stream outranks the compute stream, so NCCL's CTAs take the next SMs the attention frees instead
+        # of queueing behind the whole first-part grid
+        self.comm_stream = torch.cuda.Stream(device=self.device, priority=-1)
         self.kv_ready = [torch.cuda.Event() for _ in range(2)]
         self.calls = 0
 
