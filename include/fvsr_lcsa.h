@@ -246,7 +246,9 @@ fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, in
 /* fvsr_lcsa_forward_shard in two calls, so that the current slice's K/V gather can run beside the attention of the
  * cached slices (cached pairs first, current pairs after the gather):
  *   fvsr_lcsa_select_shard — the selection (same as in fvsr_lcsa_forward_shard) and the order of the rank's items;
- *     needs only the pooled keys of the current slice in the committed page.
+ *     needs only the pooled keys of the current slice in the committed page. Its one launch takes a CTA slot on
+ *     every SM unless spare_sms > 0 leaves that many SMs (at most half) to a collective running beside it, so the
+ *     K/V gather can start before the selection.
  *   fvsr_lcsa_attend_shard — with `partial` (fvsr_lcsa_partial_size bytes, bf16 only): the attention of every item
  *     over its kept blocks in the cached slices, written as fp32 partial results; then a wait for kv_ready; then
  *     the blocks of the chunk's own slices, merged with the partials into out (softmax of the union, so the result
@@ -255,7 +257,7 @@ fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, in
 fvsr_status fvsr_lcsa_partial_size(const fvsr_lcsa_params* p, int32_t qb_begin, int32_t qb_end, size_t* bytes);
 fvsr_status fvsr_lcsa_select_shard(const fvsr_lcsa_params* p, const float* pooled_q, int32_t qb_begin, int32_t qb_end,
                                    fvsr_kv_cache* cache, int32_t* kidx, int32_t* kcnt, void* workspace,
-                                   size_t workspace_bytes, fvsr_stream_t stream);
+                                   size_t workspace_bytes, int32_t spare_sms, fvsr_stream_t stream);
 fvsr_status fvsr_lcsa_attend_shard(const fvsr_lcsa_params* p, const void* q, int32_t qb_begin, int32_t qb_end,
                                    fvsr_kv_cache* cache, fvsr_event_t kv_ready, void* partial, size_t partial_size,
                                    void* out, const int32_t* kidx, const int32_t* kcnt, void* workspace,

@@ -121,7 +121,7 @@ def lib() -> ctypes.CDLL:
         "fvsr_kv_cache_commit": ([P], ctypes.c_int),
         "fvsr_lcsa_forward_shard": ([PP, P, I32, I32, P, P, P, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_lcsa_partial_size": ([PP, I32, I32, ctypes.POINTER(SZ)], ctypes.c_int),
-        "fvsr_lcsa_select_shard": ([PP, P, I32, I32, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_lcsa_select_shard": ([PP, P, I32, I32, P, P, P, P, SZ, I32, P], ctypes.c_int),
         "fvsr_lcsa_attend_shard": ([PP, P, I32, I32, P, P, P, SZ, P, P, P, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
@@ -605,12 +605,14 @@ def partial_size(geom: Geometry, shard: QueryShard) -> int:
 
 
 def lcsa_select_shard(pooled_q, shard: QueryShard, cache: KVCache, geom: Geometry, workspace, kidx=None, kcnt=None,
-                      stream=None):
+                      spare_sms: int = 0, stream=None):
     """The selection of a rank's layer call (fvsr_lcsa_select_shard): over pooled_q and the cache's pooled keys (the
-    current slice committed), with the longest-first order of the rank's items kept in the workspace."""
+    current slice committed), with the longest-first order of the rank's items kept in the workspace. spare_sms:
+    SMs left free for a collective running beside it."""
     p = geom.params()
     _check(lib().fvsr_lcsa_select_shard(ctypes.byref(p), _ptr(pooled_q), shard.begin, shard.end, cache.handle,
-                                        _ptr(kidx), _ptr(kcnt), _ptr(workspace), workspace.numel(), _stream(stream)))
+                                        _ptr(kidx), _ptr(kcnt), _ptr(workspace), workspace.numel(), int(spare_sms),
+                                        _stream(stream)))
 
 
 def lcsa_attend_shard(q, shard: QueryShard, cache: KVCache, geom: Geometry, workspace, out, kv_ready=None,

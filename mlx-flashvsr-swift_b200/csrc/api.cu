@@ -762,7 +762,7 @@ fvsr_status fvsr_lcsa_partial_size(const fvsr_lcsa_params* p, int32_t qb_begin, 
 
 fvsr_status fvsr_lcsa_select_shard(const fvsr_lcsa_params* p, const float* pooled_q, int32_t qb_begin, int32_t qb_end,
                                    fvsr_kv_cache* cache, int32_t* kidx, int32_t* kcnt, void* workspace,
-                                   size_t workspace_bytes, fvsr_stream_t stream) {
+                                   size_t workspace_bytes, int32_t spare_sms, fvsr_stream_t stream) {
     fvsr_lcsa_params pp;
     Dims d;
     Workspace w;
@@ -771,11 +771,12 @@ fvsr_status fvsr_lcsa_select_shard(const fvsr_lcsa_params* p, const float* poole
     if (!pooled_q) return fail(FVSR_EINVAL, "pooled_q is required");
     if (!aligned16(pooled_q)) return fail(FVSR_EINVAL, "pooled_q must be 16-byte aligned");
     if (!aligned4(kidx) || !aligned4(kcnt)) return fail(FVSR_EINVAL, "kidx and kcnt must be 4-byte aligned");
+    if (spare_sms < 0) return fail(FVSR_EINVAL, "spare_sms must be >= 0, got %d", spare_sms);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     FVSR_CU(cudaMemsetAsync(w.hist, 0, select_hist_bytes(d.heads, d.q_slices), st), "histogram clear");
     FVSR_CU(launch_select(pooled_q, cache->pk_arena, cache->kv_pages(), d.heads, d.nq, d.nk, pp.bh, pp.bw,
                           pp.local_range, pp.q_slices, pp.topk, w.probs, w.hist, kidx ? kidx : w.kidx,
-                          kcnt ? kcnt : w.kcnt, nullptr, w.order, st, qb_begin, qb_end),
+                          kcnt ? kcnt : w.kcnt, nullptr, w.order, st, qb_begin, qb_end, spare_sms),
             "selection launch");
     return FVSR_OK;
 }
@@ -841,7 +842,7 @@ fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, in
     fvsr_status s = shard_setup(p, qb_begin, qb_end, cache, workspace, workspace_bytes, &pp, &d, &w);
     if (s != FVSR_OK) return s;
     if (qb_end == qb_begin) return fvsr_kv_cache_trim(cache);
-    s = fvsr_lcsa_select_shard(p, pooled_q, qb_begin, qb_end, cache, kidx, kcnt, workspace, workspace_bytes, stream);
+    s = fvsr_lcsa_select_shard(p, pooled_q, qb_begin, qb_end, cache, kidx, kcnt, workspace, workspace_bytes, 0, stream);
     if (s != FVSR_OK) return s;
     return fvsr_lcsa_attend_shard(p, q, qb_begin, qb_end, cache, kv_ready, nullptr, 0, out, kidx, kcnt, workspace,
                                   workspace_bytes, stream);

@@ -85,10 +85,11 @@ cudaError_t launch_pool2(const void* x1, int64_t n1, float* out1, void* copy_dst
 // longest-first order of all H·nq items. `hist` (select_hist_bytes) must have been cleared by an earlier launch on
 // the stream (the pooling or prepare launch clears it).
 // The order covers the items whose query block lies in [order_q0, order_q1) (all heads); order_q1 <= 0 means all.
+// spare_sms > 0 runs the launch on that many SMs fewer (at most half of them), for a collective running beside it.
 cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk, int bh,
                           int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist, int32_t* kidx,
                           int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st, int order_q0 = 0,
-                          int order_q1 = 0);
+                          int order_q1 = 0, int spare_sms = 0);
 size_t select_smem_bytes();
 size_t select_hist_bytes(int heads, int q_slices);
 // Reads and clears the selection's grid-barrier timeout word of the current device.

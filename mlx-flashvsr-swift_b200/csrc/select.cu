@@ -691,7 +691,7 @@ size_t select_hist_bytes(int heads, int q_slices) { return sizeof(uint32_t) * (s
 cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pages, int heads, int nq, int nk, int bh,
                           int bw, int local_range, int q_slices, int topk, float* probs, uint32_t* hist, int32_t* kidx,
                           int32_t* kcnt, uint8_t* mask, int32_t* order, cudaStream_t st, int order_q0,
-                          int order_q1) {
+                          int order_q1, int spare_sms) {
     SelArgs a;
     a.pq = pq;
     a.pk = pk;
@@ -745,6 +745,9 @@ cudaError_t launch_select(const float* pq, const float* pk, const KvPages& pk_pa
         }
     }
     cudaLaunchConfig_t cfg = {};
+    // SMs left to a collective that runs beside the selection (its kernel's CTAs would otherwise keep the
+    // cooperative launch waiting for a CTA slot on every SM)
+    if (spare_sms > 0) grid = grid - spare_sms > grid / 2 ? grid - spare_sms : grid / 2;
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kSelThreads * kSelGroups);
     cfg.dynamicSmemBytes = (size_t)smem;

@@ -6,10 +6,11 @@ projection leaves them — and, per DiT layer, a replica of that layer's window 
   1. pool the rank's q and k_new shards (fvsr_lcsa_pool: the fp32 block means of DiT.swift:161-162);
   2. all-gather the pooled rows of every rank: the queries into one (Nq, H·128) buffer, the keys straight into the
      cache page reserved for the current slice — on the compute stream (1.7 MB at config 3);
-  3. fvsr_lcsa_select_shard: the full selection over the gathered pooled rows (every rank computes the same one);
-  4. all-gather the current slice's K and V shards straight into that page on a communication stream (106 MB at
-     config 3, 189 MB at config 5) — the concat of DiT.swift:508-511 without a copy. It starts after the selection,
-     whose one cooperative launch needs every SM, and runs beside
+  3. all-gather the current slice's K and V shards straight into that page on a high-priority communication stream
+     (106 MB at config 3, 189 MB at config 5) — the concat of DiT.swift:508-511 without a copy — beside
+  4. fvsr_lcsa_select_shard: the full selection over the gathered pooled rows (every rank computes the same one); its
+     cooperative launch leaves `spare_sms` SMs to the gather's kernel (with spare_sms = 0 it needs every SM, and the
+     gather is issued after it instead), and
   5. fvsr_lcsa_attend_shard: the attention of the rank's query blocks over every head — first the kept blocks in
      the cached slices (fp32 partials), then, once the gather has landed, the current slice's blocks, merged — and
      the trim.
@@ -25,7 +26,7 @@ class ShardedChunk:
     """Per-rank state of the partition for `layers` DiT layers of one chunk geometry (q_slices = 1: a steady chunk)."""
 
     def __init__(self, pkg, geom, kv_len: int, layers: int, rank: int, world: int, comm=None, device=None,
-                 split: bool = True):
+                 split: bool = True, spare_sms: int = 32):
         import torch
         if geom.q_slices != 1:
             raise pkg.FVSRError(pkg.FVSR_EINVAL, "the sharded chunk takes one temporal slice per chunk")
@@ -50,6 +51,7 @@ class ShardedChunk:
         # of queueing behind the whole first-part grid
         self.comm_stream = torch.cuda.Stream(device=self.device, priority=-1)
         self.kv_ready = [torch.cuda.Event() for _ in range(2)]
+        self.spare_sms = spare_sms
         self.calls = 0
 
     def shard_rows(self) -> int:
@@ -86,17 +88,23 @@ class ShardedChunk:
         self.comm.all_gather(self.pk_send, pk_page, st)
         self.comm.group_end()
         cache.commit()
-        pkg.lcsa_select_shard(self.pq_full, sh, cache, g, self.workspace, kcnt=kcnt, stream=st)
-        # the slice's K and V, after the selection (and every earlier use of this page) on the compute stream, beside
-        # the attention of the cached slices
         ev = self.kv_ready[self.calls & 1]
         self.calls += 1
-        self.comm_stream.wait_stream(st)
-        self.comm.group_start()
-        self.comm.all_gather(k_new, k_page, self.comm_stream)
-        self.comm.all_gather(v_new, v_page, self.comm_stream)
-        self.comm.group_end()
-        ev.record(self.comm_stream)
+
+        def kv_gather():  # after every earlier use of this page (and the pooled gather) on the compute stream
+            self.comm_stream.wait_stream(st)
+            self.comm.group_start()
+            self.comm.all_gather(k_new, k_page, self.comm_stream)
+            self.comm.all_gather(v_new, v_page, self.comm_stream)
+            self.comm.group_end()
+            ev.record(self.comm_stream)
+
+        if self.spare_sms > 0:
+            kv_gather()
+        pkg.lcsa_select_shard(self.pq_full, sh, cache, g, self.workspace, kcnt=kcnt, spare_sms=self.spare_sms,
+                              stream=st)
+        if self.spare_sms <= 0:
+            kv_gather()
         pkg.lcsa_attend_shard(q, sh, cache, g, self.workspace, out, kv_ready=ev, partial=self.partial, kcnt=kcnt,
                               stream=st)
         return out
