@@ -537,6 +537,8 @@ def run_chunk(args):
     shard_mod = importlib.import_module("fvsr_b200.shard")
     info = ranks.rank_info()
     world, rank, local = info.world, info.rank, info.local
+    if world > 1:  # NCCL's kernels must fit in the SMs the selection leaves to the gather beside it
+        os.environ.setdefault("NCCL_MAX_CTAS", "32")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     ranks.init(info, "nccl", timeout_s=120, device=dev)
@@ -551,7 +553,7 @@ def run_chunk(args):
     if world > 1:
         nccl = importlib.import_module("fvsr_b200.nccl")
         comm = nccl.Comm(rank, world, dev)
-    sc = shard_mod.ShardedChunk(pkg, g, kv_len, layers, rank, world, comm, dev)
+    sc = shard_mod.ShardedChunk(pkg, g, kv_len, layers, rank, world, comm, dev, spare_sms=32)
     sh = sc.shard
     stream = torch.cuda.current_stream()
     # per layer: the seeded full tensors of the one-GPU problem (q of the chunk, K/V of cache ⊕ current), of which
@@ -642,29 +644,55 @@ def run_chunk(args):
     torch.cuda.synchronize()
     flops = 4.0 * 128 ** 3 * kept
 
-    # the dominant kernel alone: the attention of whole fresh layers (one GPU's problem), CUDA events on its stream
+    # the dominant kernel alone: the attention of whole fresh layers (one GPU's problem), CUDA events on its stream;
+    # then the same launches back to back from a graph (the power-capped rate the step sees)
     L = pkg.lib()
     ws = pkg.make_workspace(g_full, dev)
-    kidx1 = torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device=dev)
-    kcnt1 = torch.empty((g.heads, g.nq), dtype=torch.int32, device=dev)
-    order = torch.empty(g.heads * g.nq, dtype=torch.int32, device=dev)
+    nroof = len(full)
+    kidx1 = [torch.empty((g.heads, g.nq, g.nk), dtype=torch.int32, device=dev) for _ in range(nroof)]
+    kcnt1 = [torch.empty((g.heads, g.nq), dtype=torch.int32, device=dev) for _ in range(nroof)]
+    order = [torch.empty(g.heads * g.nq, dtype=torch.int32, device=dev) for _ in range(nroof)]
     out1 = torch.empty((g.nq * 128, g.channels), dtype=qs[0].dtype, device=dev)
     p1 = g_full.params()
     att_ms, att_kept = [], []
-    for (q, k, v) in full:
-        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p1), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx1),
-                                      pkg._ptr(kcnt1), None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
-        pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p1), pkg._ptr(kcnt1), 0, g.heads * g.nq, pkg._ptr(order),
-                                          pkg._stream()))
+
+    def attention(i):
+        q, k, v = full[i]
+        pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p1), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
+                                               pkg._ptr(kidx1[i]), pkg._ptr(kcnt1[i]), pkg._ptr(out1), 0,
+                                               g.heads * g.nq, pkg._ptr(order[i]), pkg._stream()))
+
+    for i, (q, k, v) in enumerate(full):
+        pkg._check(L.fvsr_lcsa_select(ctypes.byref(p1), pkg._ptr(q), pkg._ptr(k), None, pkg._ptr(kidx1[i]),
+                                      pkg._ptr(kcnt1[i]), None, None, pkg._ptr(ws), ws.numel(), pkg._stream()))
+        pkg._check(L.fvsr_lcsa_item_order(ctypes.byref(p1), pkg._ptr(kcnt1[i]), 0, g.heads * g.nq,
+                                          pkg._ptr(order[i]), pkg._stream()))
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record(stream)
-        pkg._check(L.fvsr_lcsa_attention_range(ctypes.byref(p1), pkg._ptr(q), pkg._ptr(k), pkg._ptr(v),
-                                               pkg._ptr(kidx1), pkg._ptr(kcnt1), pkg._ptr(out1), 0, g.heads * g.nq,
-                                               pkg._ptr(order), pkg._stream()))
+        attention(i)
         a1.record(stream)
         a1.synchronize()
         att_ms.append(a0.elapsed_time(a1))
-        att_kept.append(int(kcnt1.sum().item()))
+        att_kept.append(int(kcnt1[i].sum().item()))
+    att_b2b = None
+    if nroof and not args.no_graph:
+        ag = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ag):
+            for _ in range(max(1, 30 // nroof)):
+                for i in range(nroof):
+                    attention(i)
+        for _ in range(2):
+            ag.replay()
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        for _ in range(3):
+            ag.replay()
+        b1.record(stream)
+        torch.cuda.synchronize()
+        att_b2b = b0.elapsed_time(b1) / (3 * max(1, 30 // nroof) * nroof)
+        ag.reset()
+        del ag
     del full
     att_avg = sum(att_ms) / len(att_ms)
     att_tflops = 4.0 * 128 ** 3 * (sum(att_kept) / len(att_kept)) / (att_avg * 1e-3) / 1e12
@@ -754,6 +782,9 @@ def run_chunk(args):
                              f"{2 * kv_len * srows * g.channels * 2 / 1e6:.0f} MB of cache read (> L2), no flush",
                        "launch": launch, "parallelism": par},
             "ms_per_layer": ms / layers,
+            # the attention of a layer back to back in a graph (as in the step, under the power cap) and the rest
+            "breakdown_ms_per_layer": ({"attention back to back": att_b2b, "rest (append, pooling, selection, "
+                                        "collectives, gaps)": ms / layers - att_b2b} if att_b2b else None),
             "chunk_frac_of_sustained_peak": (value / world / sustained) if sustained and cfg.dtype == "bf16" else None,
             "roofline": (
                 {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
