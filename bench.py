@@ -889,6 +889,64 @@ def run_stream4(args):
                                "30 layers per chunk, R=11, keep 60%", "dtype": "bf16"}}), flush=True)
 
 
+def run_linear(args):
+    """The DiT block's linear layers at the config's chunk (M = the chunk's tokens; FlashVSR dim 1536, FFN 8960) on
+    the tcgen05 GEMM (fvsr_linear / fvsr_linear_qkv): the q/k/v projection, the output projection, the FFN's first
+    layer with GELU(tanh) and its second with the gated residual (DiT.swift:496-499, 539-547). Each shape: 10 calls
+    from a CUDA graph after warm-up, CUDA events; TFLOP/s = 2·M·N·K per call ÷ time, against the measured bf16 burst
+    peak; torch.matmul (cuBLAS) on the same shapes beside it. Prints one JSON line."""
+    import torch
+    pkg, cfgs = load_pkg()
+    cfg = cfgs.CONFIGS[args.config]
+    g = cfg.geometry()
+    m = g.nq * 128
+    d, f = 1536, 8960
+    gen = torch.Generator(device="cuda").manual_seed(9)
+
+    def rnd(*shape, scale=1.0):
+        return (scale * torch.randn(shape, generator=gen, device="cuda")).to(torch.bfloat16)
+
+    x = rnd(m, d)
+    h = rnd(m, f)
+    w_qkv, b_qkv = rnd(3 * d, d, scale=d ** -0.5), rnd(3 * d, scale=0.1)
+    w_o, b_o = rnd(d, d, scale=d ** -0.5), rnd(d, scale=0.1)
+    w_1, b_1 = rnd(f, d, scale=d ** -0.5), rnd(f, scale=0.1)
+    w_2, b_2 = rnd(d, f, scale=f ** -0.5), rnd(d, scale=0.1)
+    gate = rnd(d, scale=0.5)
+    tok = rnd(m, d)
+    outs = [torch.empty((m, d), dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    hid = torch.empty((m, f), dtype=torch.bfloat16, device="cuda")
+    shapes = {
+        "qkv": (3 * d, d, lambda: pkg.linear_qkv(x, w_qkv, b_qkv, outs=outs),
+                lambda: torch.matmul(x, w_qkv.t())),
+        "o": (d, d, lambda: pkg.linear(x, w_o, b_o, out=outs[0]), lambda: torch.matmul(x, w_o.t())),
+        "ffn1_gelu": (f, d, lambda: pkg.linear(x, w_1, b_1, epilogue=pkg.FVSR_LINEAR_GELU, out=hid),
+                      lambda: torch.matmul(x, w_1.t())),
+        "ffn2_gated_residual": (d, f, lambda: pkg.linear(h, w_2, b_2, epilogue=pkg.FVSR_LINEAR_GATED_RESIDUAL,
+                                                         gate=gate, resid=tok, out=outs[1]),
+                                lambda: torch.matmul(h, w_2.t())),
+    }
+    peak, _, kind = peaks()
+    res = {}
+    total_flop, total_ms = 0.0, 0.0
+    for name, (n, k, ours, lib_fn) in shapes.items():
+        flop = 2.0 * m * n * k
+        t_ours = graph_time_us(ours, 10, max(args.warmup, 3)) / 1e3
+        t_lib = graph_time_us(lib_fn, 10, max(args.warmup, 3)) / 1e3
+        res[name] = {"m": m, "n": n, "k": k, "ms": t_ours, "tflops": flop / (t_ours * 1e-3) / 1e12,
+                     "frac_of_peak": flop / (t_ours * 1e-3) / 1e12 / peak,
+                     "torch_matmul_ms": t_lib, "torch_matmul_tflops": flop / (t_lib * 1e-3) / 1e12}
+        total_flop += flop
+        total_ms += t_ours
+    pkg.device_check()
+    print(json.dumps({"metric": f"DiT block linear layers on tcgen05, config {args.config} chunk (M = {m})",
+                      "value": total_flop / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_block": total_ms,
+                      "peak": peak, "peak_kind": f"{kind} bf16 burst", "frac": total_flop / (total_ms * 1e-3) / 1e12 / peak,
+                      "layers": res, "gpu_launches_per_block": 4, "launch": "CUDA graph of 10 calls per shape",
+                      "note": "torch_matmul is cuBLAS on the same shapes without the bias / epilogue, for reference"}),
+          flush=True)
+
+
 def run_kv_append(args):
     """The window cache's in-place append (fvsr_kv_cache_append + trim, DiT.swift:507-511, 532-538) as HBM traffic:
     per chunk the chunk's q_slices new slices of K and V are read and written into their cache pages and the K slices
@@ -1165,6 +1223,8 @@ def main():
                     help="measure the window cache's in-place append (HBM GB/s) instead of the layer step")
     ap.add_argument("--prepare", action="store_true",
                     help="measure the token-order q/k/v pass (HBM GB/s) and the token-order layer")
+    ap.add_argument("--linear", action="store_true",
+                    help="the DiT block's linear layers at the config's chunk on the tcgen05 GEMM (vs cuBLAS)")
     ap.add_argument("--stream4", action="store_true",
                     help="config 4 as a streamed sequence: 10 chunks of 1280x768, chunk 0 of 3 slices, kvLen 2")
     ap.add_argument("--stream", action="store_true",
@@ -1175,6 +1235,9 @@ def main():
         return
     if args.stream4:
         run_stream4(args)
+        return
+    if args.linear:
+        run_linear(args)
         return
     if args.kv_append:
         run_kv_append(args)

@@ -298,6 +298,26 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
                                      void* out, int32_t* kidx, int32_t* kcnt, void* workspace, size_t workspace_bytes,
                                      fvsr_stream_t stream);
 
+/* ---- Linear layers of the DiT block on the tensor cores ----
+ * MLX's Linear (x·Wᵀ + b, DiT.swift:318-381) for the layers around the path: the q/k/v and output projections of
+ * the self-attention (DiT.swift:496-499, 539), the feed-forward pair Linear → GELU(tanh) → Linear (DiT.swift:378,
+ * 546-547) and the gated residual adds tok + gate · f(x) (DiT.swift:540, 547). x (M, K), w (N, K) (the Linear's weight
+ * layout), bias (N) or NULL, all bf16; out (M, N) bf16; M a multiple of 128, N of 256, K of 64 (FVSR_EINVAL else).
+ * fp32 accumulation; the output is rounded to bf16 once (the Linear), and the epilogues keep the reference's
+ * rounding points: GELU → round(gelu(linear)); gated residual → round(resid + round(gate · linear)) with gate (N)
+ * and resid (M, N) bf16 (resid may be out). One persistent tcgen05 kernel. */
+typedef enum fvsr_linear_epilogue {
+    FVSR_LINEAR = 0,
+    FVSR_LINEAR_GELU = 1,
+    FVSR_LINEAR_GATED_RESIDUAL = 2
+} fvsr_linear_epilogue;
+fvsr_status fvsr_linear(int32_t m, int32_t n, int32_t k, const void* x, const void* w, const void* bias,
+                        int32_t epilogue, const void* gate, const void* resid, void* out, fvsr_stream_t stream);
+/* The q, k and v projections in one launch: w = [Wq; Wk; Wv] (3·n, k), bias = [bq; bk; bv] (3·n) or NULL; the three
+ * (m, n) outputs go to q_out, k_out, v_out (n a multiple of 256). Same arithmetic as three fvsr_linear calls. */
+fvsr_status fvsr_linear_qkv(int32_t m, int32_t n, int32_t k, const void* x, const void* w, const void* bias,
+                            void* q_out, void* k_out, void* v_out, fvsr_stream_t stream);
+
 /* ---- Streaming driver: the LCSA side of FlashVSR's chunk loop ----
  * Mirrors FlashVSRPipeline.chunk / FlashVSRDiT.step (Pipeline.swift:95-102, 112-131; DiT.swift:472-485, 554-578) for
  * the self-attention of `layers` DiT blocks at an output size out_h × out_w (multiples of 128; spatial blocks

@@ -25,6 +25,7 @@ LIB_PATH = PKG_DIR / "libfvsr_lcsa.so"
 
 FVSR_OK, FVSR_EINVAL, FVSR_ECUDA, FVSR_ETIMEOUT, FVSR_ENOMEM, FVSR_EUNSUPPORTED = range(6)
 FVSR_F32, FVSR_BF16 = 0, 1
+FVSR_LINEAR, FVSR_LINEAR_GELU, FVSR_LINEAR_GATED_RESIDUAL = 0, 1, 2
 
 EXPORTED = [
     "fvsr_version", "fvsr_status_string", "fvsr_last_error", "fvsr_device_check", "fvsr_wait_probe",
@@ -38,7 +39,7 @@ EXPORTED = [
     "fvsr_stream_chunk_geometry", "fvsr_stream_create", "fvsr_stream_destroy", "fvsr_stream_begin",
     "fvsr_stream_workspace_size", "fvsr_stream_start_chunk", "fvsr_stream_rope", "fvsr_stream_layer",
     "fvsr_kv_cache_create_padded", "fvsr_kv_cache_reserve", "fvsr_kv_cache_commit", "fvsr_lcsa_forward_shard",
-    "fvsr_lcsa_partial_size", "fvsr_lcsa_select_shard", "fvsr_lcsa_attend_shard",
+    "fvsr_lcsa_partial_size", "fvsr_lcsa_select_shard", "fvsr_lcsa_attend_shard", "fvsr_linear", "fvsr_linear_qkv",
 ]
 
 
@@ -123,6 +124,8 @@ def lib() -> ctypes.CDLL:
         "fvsr_lcsa_partial_size": ([PP, I32, I32, ctypes.POINTER(SZ)], ctypes.c_int),
         "fvsr_lcsa_select_shard": ([PP, P, I32, I32, P, P, P, P, SZ, I32, P], ctypes.c_int),
         "fvsr_lcsa_attend_shard": ([PP, P, I32, I32, P, P, P, SZ, P, P, P, P, SZ, P], ctypes.c_int),
+        "fvsr_linear": ([I32, I32, I32, P, P, P, I32, P, P, P, P], ctypes.c_int),
+        "fvsr_linear_qkv": ([I32, I32, I32, P, P, P, P, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -625,6 +628,42 @@ def lcsa_attend_shard(q, shard: QueryShard, cache: KVCache, geom: Geometry, work
                                         _ptr(partial), 0 if partial is None else partial.numel(), _ptr(_rows(out)),
                                         _ptr(kidx), _ptr(kcnt), _ptr(workspace), workspace.numel(), _stream(stream)))
     return out
+
+
+def _bf16_2d(t, name):
+    torch = _torch()
+    if t.dtype != torch.bfloat16 or t.dim() != 2 or not t.is_cuda or not t.is_contiguous():
+        raise FVSRError(FVSR_EINVAL, f"{name} must be a contiguous 2-D bf16 CUDA tensor")
+    return t
+
+
+def linear(x, w, bias=None, epilogue: int = FVSR_LINEAR, gate=None, resid=None, out=None, stream=None):
+    """MLX's Linear on the tensor cores (fvsr_linear): x (M, K) · w (N, K)ᵀ + bias, bf16, with the epilogue
+    FVSR_LINEAR, FVSR_LINEAR_GELU (GELU(tanh) of it) or FVSR_LINEAR_GATED_RESIDUAL (resid + gate · it)."""
+    torch = _torch()
+    x, w = _bf16_2d(_rows(x), "x"), _bf16_2d(w, "w")
+    m, k = x.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise FVSRError(FVSR_EINVAL, f"w must be ({n}, {k})")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _check(lib().fvsr_linear(m, n, k, _ptr(x), _ptr(w), _ptr(bias), int(epilogue), _ptr(gate), _ptr(resid),
+                             _ptr(out), _stream(stream)))
+    return out
+
+
+def linear_qkv(x, w, bias=None, outs=None, stream=None):
+    """The q, k, v projections in one launch (fvsr_linear_qkv): w = [Wq; Wk; Wv] (3n, K) → three (M, n) tensors."""
+    torch = _torch()
+    x, w = _bf16_2d(_rows(x), "x"), _bf16_2d(w, "w")
+    m, k = x.shape
+    n = w.shape[0] // 3
+    if outs is None:
+        outs = tuple(torch.empty((m, n), dtype=torch.bfloat16, device=x.device) for _ in range(3))
+    _check(lib().fvsr_linear_qkv(m, n, k, _ptr(x), _ptr(w), _ptr(bias), _ptr(outs[0]), _ptr(outs[1]),
+                                 _ptr(outs[2]), _stream(stream)))
+    return outs
 
 
 def rope_tables(f: int, h: int, w: int, t0: int = 0, head_dim: int = 128, theta: float = 10000.0, device="cuda"):

@@ -848,6 +848,63 @@ fvsr_status fvsr_lcsa_forward_shard(const fvsr_lcsa_params* p, const void* q, in
                                   workspace_bytes, stream);
 }
 
+fvsr_status fvsr_linear(int32_t m, int32_t n, int32_t k, const void* x, const void* w, const void* bias,
+                        int32_t epilogue, const void* gate, const void* resid, void* out, fvsr_stream_t stream) {
+    if (m <= 0 || n <= 0 || k <= 0 || m % 128 || n % 256 || k % 64)
+        return fail(FVSR_EINVAL, "linear shape (%d, %d, %d): m must be a multiple of 128, n of 256, k of 64", m, n, k);
+    if ((int64_t)m * k > (1ll << 31) || (int64_t)n * k > (1ll << 31) || (int64_t)m * n > (1ll << 31))
+        return fail(FVSR_EUNSUPPORTED, "linear shape (%d, %d, %d) is too large", m, n, k);
+    if (epilogue < FVSR_LINEAR || epilogue > FVSR_LINEAR_GATED_RESIDUAL)
+        return fail(FVSR_EINVAL, "unknown epilogue %d", epilogue);
+    if (!x || !w || !out) return fail(FVSR_EINVAL, "x, w and out are required");
+    if (epilogue == FVSR_LINEAR_GATED_RESIDUAL && (!gate || !resid))
+        return fail(FVSR_EINVAL, "the gated residual needs gate and resid");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(out) || !aligned16(resid) || !aligned4(bias) || !aligned4(gate))
+        return fail(FVSR_EINVAL, "x, w, out and resid must be 16-byte aligned, bias and gate 4-byte aligned");
+    fvsr_status s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    GemmArgs a{};
+    a.M = m;
+    a.N = n;
+    a.K = k;
+    a.bias = static_cast<const __nv_bfloat16*>(bias);
+    a.gate = static_cast<const __nv_bfloat16*>(gate);
+    a.resid = epilogue == FVSR_LINEAR_GATED_RESIDUAL ? static_cast<const __nv_bfloat16*>(resid) : nullptr;
+    a.out[0] = out;
+    a.split = 0;
+    a.ldo = n;
+    a.mode = epilogue;
+    FVSR_CU(launch_gemm_bf16(a, x, w, reinterpret_cast<cudaStream_t>(stream)), "linear launch");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_linear_qkv(int32_t m, int32_t n, int32_t k, const void* x, const void* w, const void* bias,
+                            void* q_out, void* k_out, void* v_out, fvsr_stream_t stream) {
+    if (m <= 0 || n <= 0 || k <= 0 || m % 128 || n % 256 || k % 64)
+        return fail(FVSR_EINVAL, "linear shape (%d, %d, %d): m must be a multiple of 128, n of 256, k of 64", m, n, k);
+    if ((int64_t)m * k > (1ll << 31) || 3ll * n * k > (1ll << 31) || (int64_t)m * n > (1ll << 31))
+        return fail(FVSR_EUNSUPPORTED, "linear shape (%d, %d, %d) is too large", m, n, k);
+    if (!x || !w || !q_out || !k_out || !v_out) return fail(FVSR_EINVAL, "x, w and the three outputs are required");
+    if (!aligned16(x) || !aligned16(w) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(v_out) ||
+        !aligned4(bias))
+        return fail(FVSR_EINVAL, "x, w and the outputs must be 16-byte aligned, bias 4-byte aligned");
+    fvsr_status s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    GemmArgs a{};
+    a.M = m;
+    a.N = 3 * n;
+    a.K = k;
+    a.bias = static_cast<const __nv_bfloat16*>(bias);
+    a.out[0] = q_out;
+    a.out[1] = k_out;
+    a.out[2] = v_out;
+    a.split = n;
+    a.ldo = n;
+    a.mode = kGemmPlain;
+    FVSR_CU(launch_gemm_bf16(a, x, w, reinterpret_cast<cudaStream_t>(stream)), "q/k/v projection launch");
+    return FVSR_OK;
+}
+
 fvsr_status fvsr_lcsa_prepare(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin, const void* v_lin,
                               const void* norm_q, const void* norm_k, float eps, const float* rope_cos,
                               const float* rope_sin, void* q_win, void* k_win, void* v_win, float* pooled_q,

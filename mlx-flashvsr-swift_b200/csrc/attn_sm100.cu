@@ -483,10 +483,11 @@ cudaError_t read_and_clear_device_error(int* flag, cudaStream_t st) {
         e = cudaMemcpyToSymbol(g_fvsr_timeout, &zero, sizeof(int));
         if (e != cudaSuccess) return e;
     }
-    int vp = 0, vs = 0;
+    int vp = 0, vs = 0, vg = 0;
     e = read_and_clear_persist_error(&vp);
     if (e == cudaSuccess) e = read_and_clear_select_error(&vs);
-    *flag = v | vp | vs;
+    if (e == cudaSuccess) e = read_and_clear_gemm_error(&vg);
+    *flag = v | vp | vs | vg;
     return e;
 }
 

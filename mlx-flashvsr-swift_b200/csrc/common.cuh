@@ -160,6 +160,22 @@ cudaError_t launch_attn_bf16_persist(const void* q, const void* k, const void* v
 // by decreasing kcnt (stable by item id), then all empty items of the range by id.
 cudaError_t launch_item_order(const int32_t* kcnt, int nq, int item_begin, int item_count, int32_t* order,
                               cudaStream_t st);
+// The linear layers of the DiT block on tcgen05 (gemm.cu): out = epilogue(A · Bᵀ + bias), A (M, K), B (N, K) bf16,
+// M % 128 = N % 256 = K % 64 = 0. Epilogues (the reference's bf16 rounding points): the Linear (round(acc + bias)),
+// GELU(tanh) of it, or the gated residual round(resid + round(gate · linear)). Outputs: out[j] receives the columns
+// [j·split, (j+1)·split) when split > 0 (the q/k/v projection into three tensors), else out[0] all N; row stride ldo.
+enum GemmMode { kGemmPlain = 0, kGemmGelu = 1, kGemmGatedResidual = 2 };
+struct GemmArgs {
+    int M, N, K;
+    const __nv_bfloat16* bias;   // (N) or NULL
+    const __nv_bfloat16* gate;   // (N), gated residual only
+    const __nv_bfloat16* resid;  // (M, ldo), gated residual only
+    void* out[3];
+    int split, ldo, mode;
+};
+cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B, cudaStream_t st);
+size_t gemm_smem_bytes();
+cudaError_t read_and_clear_gemm_error(int* flag);
 // Reads and clears the persistent kernel's timeout word of the current device.
 cudaError_t read_and_clear_persist_error(int* flag);
 // One bounded wait that runs out (fvsr_wait_probe): sets the device timeout word after limit_ns, faults nothing.

@@ -217,5 +217,18 @@ inline bool make_tile_map(CUtensorMap* map, const void* base, int64_t rows, int6
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over a (rows, cols) bf16 matrix with a box of box_rows rows × 64 columns (128 bytes), 128-byte swizzle.
+inline bool make_tile_map_box(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || box_rows < 1 || box_rows > 256) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace sm100
 }  // namespace fvsr

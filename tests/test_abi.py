@@ -179,3 +179,16 @@ def test_wait_probe_limit_checked_on_host(fvsr):
     L = fvsr.lib()
     assert L.fvsr_wait_probe(0, None) == fvsr.FVSR_EINVAL
     assert L.fvsr_wait_probe(4_000_001, None) == fvsr.FVSR_EINVAL
+
+
+def test_linear_rejects_bad_shapes_before_any_launch(fvsr):
+    """fvsr_linear / fvsr_linear_qkv check the tile multiples and the pointers on the host (no device needed)."""
+    L = fvsr.lib()
+    p = 16  # any non-NULL, aligned address: nothing is launched
+    for m, n, k in ((100, 256, 64), (128, 200, 64), (128, 256, 60), (0, 256, 64)):
+        assert L.fvsr_linear(m, n, k, p, p, None, 0, None, None, p, None) == fvsr.FVSR_EINVAL
+        assert b"multiple" in L.fvsr_last_error()
+    assert L.fvsr_linear(128, 256, 64, None, p, None, 0, None, None, p, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_linear(128, 256, 64, p, p, None, 2, None, None, p, None) == fvsr.FVSR_EINVAL   # gate, resid
+    assert L.fvsr_linear(128, 256, 64, p, p, None, 7, None, None, p, None) == fvsr.FVSR_EINVAL   # epilogue
+    assert L.fvsr_linear_qkv(128, 100, 64, p, p, None, p, p, p, None) == fvsr.FVSR_EINVAL
