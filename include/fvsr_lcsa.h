@@ -318,6 +318,23 @@ fvsr_status fvsr_linear(int32_t m, int32_t n, int32_t k, const void* x, const vo
 fvsr_status fvsr_linear_qkv(int32_t m, int32_t n, int32_t k, const void* x, const void* w, const void* bias,
                             void* q_out, void* k_out, void* v_out, fvsr_stream_t stream);
 
+/* ---- The rest of the DiT block: norms and the cross-attention ----
+ * fvsr_layernorm — LayerNorm over c channels of each of m rows (x, out (m, c) bf16, c a multiple of 256, at most
+ * 2048; eps as the model's): without weight the reference's norm1 / norm2 (affine: false), followed, when shift and
+ * scale (c) are given, by the block's modulation y·(1 + scale) + shift (DiT.swift:489-494, 546); with weight and bias
+ * (c) the affine norm3 (DiT.swift:543). Rounding points: round(n), then round(round(n·round(1 + scale)) + shift);
+ * affine round(n·w + b). fp32 statistics (mean, then the variance about it).
+ * fvsr_rmsnorm — WanRMSNorm (DiT.swift:34-47): round(round(x / √(mean(x²) + eps))·w), the cross-attention's normQ.
+ * fvsr_cross_attention — the cross-attention core (DiT.swift:351-360): softmax(q·kᵀ/√128)·v for every query over all
+ * lk keys of the cached context, per head; q (lq, H·128), k / v (lk, H·128), out (lq, H·128) bf16, lq and lk
+ * multiples of 128 (lk ≤ 327,680). The tcgen05 attention kernel with every key block kept. */
+fvsr_status fvsr_layernorm(int32_t m, int32_t c, const void* x, const void* weight, const void* bias,
+                           const void* shift, const void* scale, float eps, void* out, fvsr_stream_t stream);
+fvsr_status fvsr_rmsnorm(int32_t m, int32_t c, const void* x, const void* weight, float eps, void* out,
+                         fvsr_stream_t stream);
+fvsr_status fvsr_cross_attention(int32_t heads, int32_t lq, int32_t lk, const void* q, const void* k, const void* v,
+                                 void* out, fvsr_stream_t stream);
+
 /* ---- Streaming driver: the LCSA side of FlashVSR's chunk loop ----
  * Mirrors FlashVSRPipeline.chunk / FlashVSRDiT.step (Pipeline.swift:95-102, 112-131; DiT.swift:472-485, 554-578) for
  * the self-attention of `layers` DiT blocks at an output size out_h × out_w (multiples of 128; spatial blocks

@@ -40,6 +40,7 @@ EXPORTED = [
     "fvsr_stream_workspace_size", "fvsr_stream_start_chunk", "fvsr_stream_rope", "fvsr_stream_layer",
     "fvsr_kv_cache_create_padded", "fvsr_kv_cache_reserve", "fvsr_kv_cache_commit", "fvsr_lcsa_forward_shard",
     "fvsr_lcsa_partial_size", "fvsr_lcsa_select_shard", "fvsr_lcsa_attend_shard", "fvsr_linear", "fvsr_linear_qkv",
+    "fvsr_layernorm", "fvsr_rmsnorm", "fvsr_cross_attention",
 ]
 
 
@@ -126,6 +127,9 @@ def lib() -> ctypes.CDLL:
         "fvsr_lcsa_attend_shard": ([PP, P, I32, I32, P, P, P, SZ, P, P, P, P, SZ, P], ctypes.c_int),
         "fvsr_linear": ([I32, I32, I32, P, P, P, I32, P, P, P, P], ctypes.c_int),
         "fvsr_linear_qkv": ([I32, I32, I32, P, P, P, P, P, P, P], ctypes.c_int),
+        "fvsr_layernorm": ([I32, I32, P, P, P, P, P, ctypes.c_float, P, P], ctypes.c_int),
+        "fvsr_rmsnorm": ([I32, I32, P, P, ctypes.c_float, P, P], ctypes.c_int),
+        "fvsr_cross_attention": ([I32, I32, I32, P, P, P, P, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -664,6 +668,39 @@ def linear_qkv(x, w, bias=None, outs=None, stream=None):
     _check(lib().fvsr_linear_qkv(m, n, k, _ptr(x), _ptr(w), _ptr(bias), _ptr(outs[0]), _ptr(outs[1]),
                                  _ptr(outs[2]), _stream(stream)))
     return outs
+
+
+def layernorm(x, weight=None, bias=None, shift=None, scale=None, eps: float = 1e-6, out=None, stream=None):
+    """LayerNorm over the channels (fvsr_layernorm): norm1/norm2 (no affine) with the block's modulation
+    y·(1 + scale) + shift when shift and scale are given (DiT.swift:489-494, 546); norm3 with weight and bias."""
+    torch = _torch()
+    x = _bf16_2d(_rows(x), "x")
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib().fvsr_layernorm(x.shape[0], x.shape[1], _ptr(x), _ptr(weight), _ptr(bias), _ptr(shift), _ptr(scale),
+                                float(eps), _ptr(out), _stream(stream)))
+    return out
+
+
+def rmsnorm(x, weight, eps: float = 1e-6, out=None, stream=None):
+    """WanRMSNorm (DiT.swift:34-47) of each row (fvsr_rmsnorm)."""
+    torch = _torch()
+    x = _bf16_2d(_rows(x), "x")
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib().fvsr_rmsnorm(x.shape[0], x.shape[1], _ptr(x), _ptr(weight), float(eps), _ptr(out), _stream(stream)))
+    return out
+
+
+def cross_attention(q, k, v, heads: int, out=None, stream=None):
+    """The cross-attention core (DiT.swift:351-360, fvsr_cross_attention): every query over all context keys."""
+    torch = _torch()
+    q, k, v = (_bf16_2d(_rows(t), n) for t, n in ((q, "q"), (k, "k"), (v, "v")))
+    if out is None:
+        out = torch.empty_like(q)
+    _check(lib().fvsr_cross_attention(int(heads), q.shape[0], k.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                      _stream(stream)))
+    return out
 
 
 def rope_tables(f: int, h: int, w: int, t0: int = 0, head_dim: int = 128, theta: float = 10000.0, device="cuda"):

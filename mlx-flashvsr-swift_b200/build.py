@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_build"
 LIB = PKG / "libfvsr_lcsa.so"
 SOURCES = ["pool.cu", "prepare.cu", "select.cu", "attn_f32.cu", "attn_sm100.cu", "attn_persist.cu", "schedule.cu",
-           "api.cu", "stream.cu", "select_noalloc.cu", "gemm.cu"]
+           "api.cu", "stream.cu", "select_noalloc.cu", "gemm.cu", "norm.cu"]
 
 
 def nvcc() -> str:

@@ -905,6 +905,53 @@ fvsr_status fvsr_linear_qkv(int32_t m, int32_t n, int32_t k, const void* x, cons
     return FVSR_OK;
 }
 
+fvsr_status fvsr_layernorm(int32_t m, int32_t c, const void* x, const void* weight, const void* bias,
+                           const void* shift, const void* scale, float eps, void* out, fvsr_stream_t stream) {
+    if (m < 0 || c <= 0 || c % 256 || c > 2048)
+        return fail(FVSR_EINVAL, "layernorm: c must be a positive multiple of 256 up to 2048, got %d (m %d)", c, m);
+    if (!x || !out) return fail(FVSR_EINVAL, "x and out are required");
+    if ((shift == nullptr) != (scale == nullptr)) return fail(FVSR_EINVAL, "shift and scale go together");
+    if (bias && !weight) return fail(FVSR_EINVAL, "bias needs weight");
+    if (!(eps >= 0.0f && eps < 1e30f)) return fail(FVSR_EINVAL, "eps must be finite and >= 0");
+    if (!aligned16(x) || !aligned16(out) || !aligned4(weight) || !aligned4(bias) || !aligned4(shift) ||
+        !aligned4(scale))
+        return fail(FVSR_EINVAL, "x and out must be 16-byte aligned, the vectors 4-byte aligned");
+    FVSR_CU(launch_layernorm(m, c, x, weight, bias, shift, scale, eps, out, reinterpret_cast<cudaStream_t>(stream)),
+            "layernorm launch");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_rmsnorm(int32_t m, int32_t c, const void* x, const void* weight, float eps, void* out,
+                         fvsr_stream_t stream) {
+    if (m < 0 || c <= 0 || c % 256 || c > 2048)
+        return fail(FVSR_EINVAL, "rmsnorm: c must be a positive multiple of 256 up to 2048, got %d (m %d)", c, m);
+    if (!x || !out || !weight) return fail(FVSR_EINVAL, "x, weight and out are required");
+    if (!(eps >= 0.0f && eps < 1e30f)) return fail(FVSR_EINVAL, "eps must be finite and >= 0");
+    if (!aligned16(x) || !aligned16(out) || !aligned4(weight))
+        return fail(FVSR_EINVAL, "x and out must be 16-byte aligned, weight 4-byte aligned");
+    FVSR_CU(launch_rmsnorm(m, c, x, weight, eps, out, reinterpret_cast<cudaStream_t>(stream)), "rmsnorm launch");
+    return FVSR_OK;
+}
+
+fvsr_status fvsr_cross_attention(int32_t heads, int32_t lq, int32_t lk, const void* q, const void* k, const void* v,
+                                 void* out, fvsr_stream_t stream) {
+    if (heads < 1 || heads > kMaxHeads) return fail(FVSR_EINVAL, "heads must be in [1, %d], got %d", kMaxHeads, heads);
+    if (lq <= 0 || lk <= 0 || lq % 128 || lk % 128)
+        return fail(FVSR_EINVAL, "lq and lk must be positive multiples of 128, got %d and %d", lq, lk);
+    if (lk / 128 > kMaxNk) return fail(FVSR_EUNSUPPORTED, "lk = %d keys exceeds %d blocks", lk, kMaxNk);
+    if ((int64_t)heads * (lq / 128) > (1ll << 30)) return fail(FVSR_EUNSUPPORTED, "lq = %d is too large", lq);
+    if (!q || !k || !v || !out) return fail(FVSR_EINVAL, "q, k, v and out are required");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+        return fail(FVSR_EINVAL, "q, k, v and out must be 16-byte aligned");
+    fvsr_status s = check_device_sm100();
+    if (s != FVSR_OK) return s;
+    const int nq = lq / 128, nk = lk / 128;
+    FVSR_CU(launch_attn_bf16(q, k, v, (int64_t)lk, identity_pages(nk), heads, nq, nk, nullptr, nullptr, out, 0,
+                             heads * nq, nullptr, reinterpret_cast<cudaStream_t>(stream)),
+            "cross-attention launch");
+    return FVSR_OK;
+}
+
 fvsr_status fvsr_lcsa_prepare(const fvsr_lcsa_params* p, const void* q_lin, const void* k_lin, const void* v_lin,
                               const void* norm_q, const void* norm_k, float eps, const float* rope_cos,
                               const float* rope_sin, void* q_win, void* k_win, void* v_win, float* pooled_q,

@@ -93,11 +93,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int h = item / a.nq, qb = item % a.nq;
     const int64_t ld = (int64_t)a.heads * kD;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int cnt = a.kcnt[item];
+    int cnt = a.kcnt ? a.kcnt[item] : a.nk;  // no lists: dense (every key block, in order)
     cnt = cnt < 0 ? 0 : (cnt > a.nk ? a.nk : cnt);
     int lo = 0;  // first list entry this launch walks
     const size_t slot = blockIdx.x;
-    if (a.split.part != 0) {
+    if (a.split.part != 0 && a.kidx) {
         // the list is ascending, so its blocks below split_nk are a prefix: count it with the whole CTA
         const int32_t* gl = a.kidx + (int64_t)item * a.nk;
         int c1 = 0;
@@ -167,9 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
     }
-    const int32_t* glist = a.kidx + (int64_t)item * a.nk + lo;
+    const int32_t* glist = a.kidx ? a.kidx + (int64_t)item * a.nk + lo : nullptr;
     for (int j = threadIdx.x; j < cnt; j += kThreads) {
-        int kb = glist[j];
+        int kb = glist ? glist[j] : lo + j;
         kb = kb < 0 ? 0 : (kb >= a.nk ? a.nk - 1 : kb);
         s_list[j] = kv_phys_block(a.pages, kb);
     }

@@ -176,6 +176,10 @@ struct GemmArgs {
 cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B, cudaStream_t st);
 size_t gemm_smem_bytes();
 cudaError_t read_and_clear_gemm_error(int* flag);
+// Row normalisations of the DiT block (norm.cu); x / out (m, ch) bf16, ch a multiple of 256 up to 2048.
+cudaError_t launch_layernorm(int m, int ch, const void* x, const void* weight, const void* bias, const void* shift,
+                             const void* scale, float eps, void* out, cudaStream_t st);
+cudaError_t launch_rmsnorm(int m, int ch, const void* x, const void* weight, float eps, void* out, cudaStream_t st);
 // Reads and clears the persistent kernel's timeout word of the current device.
 cudaError_t read_and_clear_persist_error(int* flag);
 // One bounded wait that runs out (fvsr_wait_probe): sets the device timeout word after limit_ns, faults nothing.

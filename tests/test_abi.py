@@ -192,3 +192,15 @@ def test_linear_rejects_bad_shapes_before_any_launch(fvsr):
     assert L.fvsr_linear(128, 256, 64, p, p, None, 2, None, None, p, None) == fvsr.FVSR_EINVAL   # gate, resid
     assert L.fvsr_linear(128, 256, 64, p, p, None, 7, None, None, p, None) == fvsr.FVSR_EINVAL   # epilogue
     assert L.fvsr_linear_qkv(128, 100, 64, p, p, None, p, p, p, None) == fvsr.FVSR_EINVAL
+
+
+def test_block_ops_reject_bad_arguments_before_any_launch(fvsr):
+    L = fvsr.lib()
+    p = 16
+    assert L.fvsr_layernorm(8, 100, p, None, None, None, None, 1e-6, p, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_layernorm(8, 4096, p, None, None, None, None, 1e-6, p, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_layernorm(8, 256, p, None, None, p, None, 1e-6, p, None) == fvsr.FVSR_EINVAL     # shift w/o scale
+    assert L.fvsr_layernorm(8, 256, p, None, p, None, None, 1e-6, p, None) == fvsr.FVSR_EINVAL     # bias w/o weight
+    assert L.fvsr_rmsnorm(8, 256, p, None, 1e-6, p, None) == fvsr.FVSR_EINVAL                      # no weight
+    assert L.fvsr_cross_attention(12, 100, 512, p, p, p, p, None) == fvsr.FVSR_EINVAL
+    assert L.fvsr_cross_attention(0, 128, 128, p, p, p, p, None) == fvsr.FVSR_EINVAL

@@ -4,8 +4,8 @@ Reference (MLX's Linear, DiT.swift:318-381): y = x·Wᵀ + b accumulated in fp32
 keep the reference's rounding points — GELU(tanh) of the rounded Linear, rounded; the gated residual
 round(resid + round(gate · linear)). The GEMM's fp32 summation order differs from torch's, so an element may land
 one bf16 rounding step away: the bar is |Δ| ≤ 2⁻⁷·|ref| + 1e-3·max|ref| per element (two bf16 ulps) and rel ≤ 1e-2.
-Shapes cover one tile, fewer tiles than SMs, several tiles per SM (both TMEM accumulators), and K = 8960 (the FFN's
-second layer)."""
+Shapes cover one half tile (M = 128), a last half tile (M = 384, 17280: rows loaded as zeros past M, not written),
+fewer tiles than SMs, several tiles per SM, and K = 8960 (the FFN's second layer)."""
 from __future__ import annotations
 
 import pytest
@@ -43,8 +43,8 @@ def _close(got, ref):
     assert float(d.max() / r.abs().max()) <= 1e-2
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (1024, 1536, 1536), (2048, 4608, 1536), (256, 1536, 8960),
-                                   (4096, 8960, 1536)])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (384, 512, 128), (1024, 1536, 1536), (2048, 4608, 1536),
+                                   (256, 1536, 8960), (4096, 8960, 1536), (17280, 1536, 1536)])
 def test_linear_matches_fp32_reference(gpu, m, n, k):
     x, w, b = _data(m, n, k, m + n + k)
     got = gpu.linear(x, w, b)
