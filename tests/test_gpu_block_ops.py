@@ -27,7 +27,7 @@ def _bf(x):
 def _one_step(got, ref):
     g, r = got.double(), ref.double()
     d = (g - r).abs()
-    assert (d <= 2.0 ** -7 * r.abs() + 1e-30).all(), float(d.max())
+    assert (d <= 2.0 ** -7 * torch.maximum(g.abs(), r.abs()) + 1e-30).all(), float(d.max())  # one step of the larger
     assert float((d == 0).double().mean()) > 0.99
 
 
