@@ -4,17 +4,14 @@
 // the q/k/v projections of the self-attention, its output projection `sa.o`, the feed-forward pair with GELU(tanh)
 // between, and the gated residual adds `tok + gate · f(x)`.
 //
-// Persistent kernel, one CTA per SM walking 256 × 256 output tiles (consecutive tiles share the A rows, all of B sits
-// in L2). A 256 × 256 tile takes 64 KB of operands per 64-wide K step for 8.4 MFLOP, so an SM needs ≈ 43 B/cycle from
-// L2 at the tensor rate (a 128 × 256 tile would need ≈ 65, the TMA delivery limit measured on this part).
-// Warp roles (320 threads):
-//   warp 0      TMA producer: per K step one A box (256 × 64) and one B box (256 × 64) into a 3-stage ring;
-//   warp 1      TMEM owner + single-thread MMA issuer: per K step 2 halves × 4 × tcgen05.mma (M 128, N 256, K 16)
-//               into the tile's two 256-column TMEM accumulators; the producer keeps prefetching while the epilogue
-//               drains them;
-//   warps 2..9  epilogue: two warps per TMEM lane quarter (one per M half), thread = output row, 32 columns per
-//               tcgen05.ld, the epilogue arithmetic in fp32 with the reference's bf16 rounding points, 64-byte
-//               stores; rows past M (a last half tile, loaded as zeros) are not written.
+// Persistent kernel, one CTA per SM walking 128 × 256 output tiles (consecutive tiles share the A rows, all of B sits
+// in L2). (A 256 × 256 tile, two M-128 MMAs per K step and one accumulator pair, measured slower: its epilogue cannot
+// overlap the next tile.) Warp roles (192 threads):
+//   warp 0      TMA producer: per 64-wide K step one A box (128 × 64) and one B box (256 × 64) into a 4-stage ring;
+//   warp 1      TMEM owner + single-thread MMA issuer: 4 × tcgen05.mma (M 128, N 256, K 16) per K step into one of
+//               two TMEM accumulators (256 columns each), so the next tile's MMAs run while the epilogue drains;
+//   warps 2..5  epilogue: thread = output row = TMEM lane, 32 columns per tcgen05.ld, the epilogue arithmetic in
+//               fp32 with the reference's bf16 rounding points, 64-byte stores.
 // Every wait is bounded (4 s, %globaltimer); on expiry the kernel raises its abort and device timeout words and
 // returns, and fvsr_device_check reports FVSR_ETIMEOUT.
 #include <math.h>
@@ -30,16 +27,16 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 256, kBN = 256, kBK = 64, kStages = 3;
-constexpr uint32_t kABytes = kBM * kBK * 2;   // 32 KB (two 128-row halves of 16 KB)
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr int kThreads = 320;
+constexpr int kThreads = 192;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
-constexpr uint32_t kIdesc = idesc_bf16_f32(128, kBN, 0, 0);
-// barriers: full[s], empty[s], acc_full, acc_empty
-constexpr int kBarFull = 0, kBarEmpty = kStages, kBarAccFull = 2 * kStages, kBarAccEmpty = 2 * kStages + 1,
-              kNumBars = 2 * kStages + 2;
+constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN, 0, 0);
+// barriers: full[s], empty[s], acc_full[2], acc_empty[2]
+constexpr int kBarFull = 0, kBarEmpty = kStages, kBarAccFull = 2 * kStages, kBarAccEmpty = 2 * kStages + 2,
+              kNumBars = 2 * kStages + 4;
 constexpr uint32_t kOffBar = kStages * kStageBytes;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
@@ -65,7 +62,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sbase = smem_u32(smem);
     griddep_wait_then_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = (a.M + kBM - 1) / kBM, nt = a.N / kBN, kt = a.K / kBK;
+    const int mt = a.M / kBM, nt = a.N / kBN, kt = a.K / kBK;
     const int tiles = mt * nt;
     volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(smem + kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
@@ -78,8 +75,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(kBarFull + s), 1);
             mbar_init(bar(kBarEmpty + s), 1);
         }
-        mbar_init(bar(kBarAccFull), 1);
-        mbar_init(bar(kBarAccEmpty), 256);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(kBarAccFull + b), 1);
+            mbar_init(bar(kBarAccEmpty + b), 128);
+        }
         *abort_word = 0;
         fence_mbar_init();
     }
@@ -120,52 +119,49 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             int lt = 0;  // tiles of this CTA so far
             for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++lt) {
-                // the epilogue drained the accumulators of the previous tile
-                if (lt >= 1 && !(ok = wait(kBarAccEmpty, (uint32_t)(lt - 1)))) break;
+                const int acc = lt & 1;
+                // the epilogue drained this accumulator two tiles ago
+                if (lt >= 2 && !(ok = wait(kBarAccEmpty + acc, (uint32_t)((lt >> 1) - 1)))) break;
                 tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)acc * kBN;
                 for (int kb = 0; kb < kt; ++kb, ++it) {
                     const int s = it % kStages;
                     if (!(ok = wait(kBarFull + s, it / kStages))) break;
                     tc_fence_after();
                     const uint32_t sa = sbase + (uint32_t)s * kStageBytes;
+                    const uint64_t ad = smem_desc(sa, 16, 1024);
                     const uint64_t bd = smem_desc(sa + kABytes, 16, 1024);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint64_t ad = smem_desc(sa + (uint32_t)h * (kABytes / 2), 16, 1024);
-#pragma unroll
-                        for (int kk = 0; kk < kBK / 16; ++kk)
-                            mma_ss(tmem + (uint32_t)h * kBN, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), kIdesc,
-                                   (kb > 0 || kk > 0) ? 1u : 0u);
-                    }
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_ss(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
                     mma_commit(bar(kBarEmpty + s));  // the stage is free once these MMAs have read it
                 }
-                if (ok) mma_commit(bar(kBarAccFull));
+                if (ok) mma_commit(bar(kBarAccFull + acc));
             }
         }
     } else {
-        // ---------------- epilogue: warp (half, quarter), thread = row = TMEM lane ----------------
-        const int quarter = warp & 3, half = (warp - 2) >> 2;
-        const int r = half * 128 + quarter * 32 + lane;
-        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)half * kBN;
+        // ---------------- epilogue: thread = row = TMEM lane ----------------
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
         int lt = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++lt) {
-            ok = __all_sync(0xffffffffu, wait(kBarAccFull, (uint32_t)lt));
+            const int acc = lt & 1;
+            ok = __all_sync(0xffffffffu, wait(kBarAccFull + acc, (uint32_t)(lt >> 1)));
             if (!ok) break;
             tc_fence_after();
             const int m0 = (t / nt) * kBM, n0 = (t % nt) * kBN;
             const int j = a.split > 0 ? n0 / a.split : 0;
             const int c0 = a.split > 0 ? n0 - j * a.split : n0;
             const int64_t row = (int64_t)(m0 + r);
-            const bool live = row < a.M;
-            __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out[j]) + (live ? row : 0) * a.ldo + c0;
-            const __nv_bfloat16* rrow = a.resid ? a.resid + (live ? row : 0) * a.ldo + c0 : nullptr;
+            __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a.out[j]) + row * a.ldo + c0;
+            const __nv_bfloat16* rrow = a.resid ? a.resid + row * a.ldo + c0 : nullptr;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t v[32];
-                tmem_ld32(lane_base + 32u * c, v);
+                tmem_ld32(lane_base + (uint32_t)acc * kBN + 32u * c, v);
                 tmem_ld_wait(v);
-                if (!live) continue;
                 const int col = n0 + 32 * c;  // global output column of v[0]
                 uint32_t w[16];
 #pragma unroll
@@ -190,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
             }
             tc_fence_before();
-            mbar_arrive(bar(kBarAccEmpty));  // the MMA thread may now overwrite the accumulators
+            mbar_arrive(bar(kBarAccEmpty + acc));  // the MMA thread may now reuse this accumulator
         }
     }
     tc_fence_before();
@@ -206,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 size_t gemm_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B, cudaStream_t st) {
-    if (args.M % 128 || args.N % kBN || args.K % kBK || args.M <= 0 || args.N <= 0 || args.K <= 0)
+    if (args.M % kBM || args.N % kBN || args.K % kBK || args.M <= 0 || args.N <= 0 || args.K <= 0)
         return cudaErrorInvalidValue;
     CUtensorMap ma, mb;
     if (!make_tile_map_box(&ma, A, args.M, args.K, kBM) || !make_tile_map_box(&mb, B, args.N, args.K, kBN))
@@ -217,7 +213,7 @@ cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B,
     int dev = 0, nsm = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    const int tiles = ((args.M + kBM - 1) / kBM) * (args.N / kBN);
+    const int tiles = (args.M / kBM) * (args.N / kBN);
     const int grid = tiles < nsm ? tiles : nsm;
     return launch_pdl(gemm_bf16_sm100_kernel, dim3(grid), dim3(kThreads), (size_t)kSmemBytes, st, ma, mb, args);
 }
