@@ -947,6 +947,105 @@ def run_linear(args):
           flush=True)
 
 
+def run_block(args):
+    """Whole DiT blocks (blockForward, DiT.swift:486-549) on the library's kernels (dit.block_forward): one steady
+    streamed chunk of config `--config` (default 3: 1920×1152, 17,280 tokens, dim 1536, 12 heads, FFN 8960) through
+    `--layers` blocks chained as in the model (block l's output is block l+1's input), each block with its own
+    random-initialised weights, cached context K/V (512 text tokens) and window K/V cache of kvLen 2 slices (prefilled).
+    A step = the chunk through all blocks; CUDA events; then one more step with an event after each stage for the
+    breakdown. TFLOP/s = the algorithmic FLOPs of every linear layer, the LCSA over its kept triples and the
+    cross-attention ÷ time. Prints one JSON line."""
+    import torch
+    pkg, cfgs = load_pkg()
+    import importlib
+    dit = importlib.import_module("fvsr_b200.dit")
+    cfg = cfgs.CONFIGS[args.config]
+    g = cfg.geometry()
+    if g.q_slices != 1 or cfg.dtype != "bf16":
+        raise SystemExit(f"config {args.config}: the block mode takes a bf16 one-slice chunk")
+    c, ffn, lc, kv_len, layers = g.channels, 8960, 512, g.kv_slices - g.q_slices, args.layers
+    rows, srows = g.nq * 128, g.s * 128
+    gen = torch.Generator(device="cuda").manual_seed(4242)
+    weights, caches, mods = [], [], []
+    for l in range(layers):
+        weights.append(dit.BlockWeights.random(c=c, f=ffn, lc=lc, seed=100 + l))
+        cache = pkg.KVCache(g, kv_len=kv_len, max_new_slices=1)
+        for _ in range(kv_len):
+            ks = torch.randn((srows, c), generator=gen, device="cuda").to(torch.bfloat16)
+            cache.append(ks, torch.randn((srows, c), generator=gen, device="cuda").to(torch.bfloat16), 1)
+        caches.append(cache)
+        mods.append([(s * torch.randn((c,), generator=gen, device="cuda")).to(torch.bfloat16)
+                     for s in (0.2, 0.2, 0.5, 0.2, 0.2, 0.5)])
+    tok0 = torch.randn((rows, c), generator=gen, device="cuda").to(torch.bfloat16)
+    tok = torch.empty_like(tok0)
+    rope = pkg.rope_tables(2, 8 * g.bh, 8 * g.bw, t0=4 + 2 * 3)
+    buf = dit.BlockBuffers(rows, c, ffn)
+    ws = pkg.make_workspace(g)
+    kcnt = torch.zeros((layers, g.heads, g.nq), dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(timeline=None):
+        tok.copy_(tok0)
+        for l in range(layers):
+            dit.block_forward(weights[l], tok, mods[l], caches[l], g, rope, buf, ws, kcnt=kcnt[l], stream=stream,
+                              timeline=timeline)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    kept = [int(x) for x in kcnt.sum(dim=(1, 2)).tolist()]
+    flops = sum(dit.block_flops(rows, c, ffn, lc, k) for k in kept)
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(0).uuid)
+    except Exception:
+        pass
+    clocks = Clocks(uuid)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_begin = time.time()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks.mark(t_begin, time.time())
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    timeline = []
+    step(timeline)
+    torch.cuda.synchronize()
+    pkg.device_check()
+    stages = {}
+    for (_, a), (name, b) in zip(timeline, timeline[1:]):
+        if name != "begin":
+            stages[name] = stages.get(name, 0.0) + a.elapsed_time(b)
+    total = sum(stages.values())
+    lin_flop = 2.0 * rows * c * (6 * c + 2 * ffn) * layers
+    lcsa_flop = sum(4.0 * 128 ** 3 * k for k in kept)
+    peak, _, kind = peaks()
+    for cch in caches:
+        cch.close()
+    value = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": f"DiT block stack effective TFLOP/s, config {args.config} streamed chunk", "value": value,
+        "unit": "TFLOP/s", "ms_per_step": ms, "ms_per_block": ms / layers, "steps": args.steps,
+        "warmup": args.warmup, "layers": layers, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (random-init block weights, seeded tokens, prefilled caches)",
+        "frac_of_peak": value / peak, "peak": peak, "peak_kind": f"{kind} bf16 burst",
+        "flop_per_step": {"linear": lin_flop, "lcsa": lcsa_flop, "cross_attention": 4.0 * rows * lc * c * layers},
+        "kept_triples_per_block": sum(kept) / layers,
+        "breakdown_ms_per_block": {k: v / layers for k, v in stages.items()},
+        "breakdown_share": {k: v / total for k, v in stages.items()},
+        "stage_tflops": {"lcsa": lcsa_flop / (stages["lcsa"] * 1e-3) / 1e12},
+        "clocks": clk,
+        "config": {"workload": f"config {args.config}: {cfg.name}, one steady chunk ({rows} tokens) through "
+                               f"{layers} blocks", "dim": c, "ffn": ffn, "context_tokens": lc, "heads": g.heads,
+                   "kv_len": kv_len, "topk": g.topk, "launch": "host C-ABI calls, no graph", "l2": "inputs > L2"}}),
+        flush=True)
+
+
 def run_kv_append(args):
     """The window cache's in-place append (fvsr_kv_cache_append + trim, DiT.swift:507-511, 532-538) as HBM traffic:
     per chunk the chunk's q_slices new slices of K and V are read and written into their cache pages and the K slices
@@ -1229,7 +1328,12 @@ def main():
                     help="config 4 as a streamed sequence: 10 chunks of 1280x768, chunk 0 of 3 slices, kvLen 2")
     ap.add_argument("--stream", action="store_true",
                     help="run whole chunks through the streaming driver (reference chunk loop and defaults)")
+    ap.add_argument("--block", action="store_true",
+                    help="whole DiT blocks (norms, linear layers, LCSA, cross-attention, FFN) on a streamed chunk")
     args = ap.parse_args()
+    if args.block:
+        run_block(args)
+        return
     if args.stream:
         run_stream(args)
         return
