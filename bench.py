@@ -1024,6 +1024,9 @@ def run_block(args):
     total = sum(stages.values())
     lin_flop = 2.0 * rows * c * (6 * c + 2 * ffn) * layers
     lcsa_flop = sum(4.0 * 128 ** 3 * k for k in kept)
+    stage_flop = {"qkv": 2.0 * rows * c * 3 * c, "lcsa": lcsa_flop / layers, "o": 2.0 * rows * c * c,
+                  "ca.q": 2.0 * rows * c * c, "ca.attention": 4.0 * rows * lc * c, "ca.o": 2.0 * rows * c * c,
+                  "ffn1 (GELU)": 2.0 * rows * c * ffn, "ffn2": 2.0 * rows * ffn * c}
     peak, _, kind = peaks()
     for cch in caches:
         cch.close()
@@ -1038,7 +1041,9 @@ def run_block(args):
         "kept_triples_per_block": sum(kept) / layers,
         "breakdown_ms_per_block": {k: v / layers for k, v in stages.items()},
         "breakdown_share": {k: v / total for k, v in stages.items()},
-        "stage_tflops": {"lcsa": lcsa_flop / (stages["lcsa"] * 1e-3) / 1e12},
+        "stage_tflops": {k: fl * layers / (stages[k] * 1e-3) / 1e12 for k, fl in stage_flop.items()},
+        "norm_gbs": {k: 4.0 * rows * c * layers / (stages[k] * 1e-3) / 1e9 for k in ("norm1", "norm3", "ca.norm_q",
+                                                                                    "norm2")},
         "clocks": clk,
         "config": {"workload": f"config {args.config}: {cfg.name}, one steady chunk ({rows} tokens) through "
                                f"{layers} blocks", "dim": c, "ffn": ffn, "context_tokens": lc, "heads": g.heads,

@@ -97,27 +97,33 @@ def block_forward(w: BlockWeights, tok, mod6, cache, geom, rope, buf: BlockBuffe
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = mod6
     heads = geom.heads
     layernorm(tok, shift=shift_msa, scale=scale_msa, eps=eps, out=buf.inx, stream=stream)
+    mark("norm1")
     linear_qkv(buf.inx, w.w_qkv, w.b_qkv, outs=(buf.q, buf.k, buf.v), stream=stream)
-    mark("norm1 + qkv")
+    mark("qkv")
     lcsa_forward_tokens(buf.q, buf.k, buf.v, cache, geom, norm_q=w.norm_q, norm_k=w.norm_k, eps=eps, rope=rope,
                         q_win=buf.qwin, out=buf.attn, kidx=kidx, kcnt=kcnt, workspace=workspace, stream=stream)
     mark("lcsa")
     linear(buf.attn, w.w_o, w.b_o, epilogue=FVSR_LINEAR_GATED_RESIDUAL, gate=gate_msa, resid=tok, out=tok,
            stream=stream)
-    mark("o + gated residual")
+    mark("o")
     layernorm(tok, weight=w.n3_w, bias=w.n3_b, eps=eps, out=buf.inx, stream=stream)
+    mark("norm3")
     linear(buf.inx, w.ca_wq, w.ca_bq, out=buf.cq_lin, stream=stream)
+    mark("ca.q")
     rmsnorm(buf.cq_lin, w.ca_norm_q, eps=eps, out=buf.cq, stream=stream)
+    mark("ca.norm_q")
     cross_attention(buf.cq, w.ctx_k, w.ctx_v, heads, out=buf.ca, stream=stream)
+    mark("ca.attention")
     linear(buf.ca, w.ca_wo, w.ca_bo, epilogue=FVSR_LINEAR_GATED_RESIDUAL, gate=buf.ones, resid=tok, out=tok,
            stream=stream)
-    mark("cross-attention")
+    mark("ca.o")
     layernorm(tok, shift=shift_mlp, scale=scale_mlp, eps=eps, out=buf.inx, stream=stream)
+    mark("norm2")
     linear(buf.inx, w.w1, w.b1, epilogue=FVSR_LINEAR_GELU, out=buf.h, stream=stream)
-    mark("norm2 + ffn1 (GELU)")
+    mark("ffn1 (GELU)")
     linear(buf.h, w.w2, w.b2, epilogue=FVSR_LINEAR_GATED_RESIDUAL, gate=gate_mlp, resid=tok, out=tok,
            stream=stream)
-    mark("ffn2 + gated residual")
+    mark("ffn2")
     return tok
 
 
