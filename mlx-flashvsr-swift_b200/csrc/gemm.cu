@@ -4,20 +4,28 @@
 // the q/k/v projections of the self-attention, its output projection `sa.o`, the feed-forward pair with GELU(tanh)
 // between, and the gated residual adds `tok + gate · f(x)`.
 //
-// Persistent kernel, one CTA per SM walking 128 × 256 output tiles (consecutive tiles share the A rows, all of B sits
-// in L2). (A 256 × 256 tile, two M-128 MMAs per K step and one accumulator pair, measured slower: its epilogue cannot
-// overlap the next tile.) Warp roles (320 threads):
-//   warp 0      TMA producer: per 64-wide K step one A box (128 × 64) and one B box (256 × 64) into a 4-stage ring;
-//   warp 1      TMEM owner + single-thread MMA issuer: 4 × tcgen05.mma (M 128, N 256, K 16) per K step into one of
-//               two TMEM accumulators (256 columns each), so the next tile's MMAs run while the epilogue drains;
+// Persistent kernel over CTA pairs: a cluster of two CTAs (one TPC) walks 256 × 256 output tiles (consecutive tiles of
+// a pair share the A rows; B sits in L2) with tcgen05 cta_group::2 MMAs (M 256, N 256, K 16). CTA r of the pair loads
+// rows [m0 + 128·r, +128) of A and rows [n0 + 128·r, +128) of B per 64-wide K step (32 KB per stage, 6 stages), the
+// even CTA's single MMA thread drives both tensor cores, and each CTA's TMEM receives its own 128 rows × 256 columns.
+// Against one CTA per 128 × 256 tile this halves B per SM: 8 KB of shared-memory operand reads and 32 KB of L2 → SM
+// traffic per 128 × 256 × 64 of work instead of 12 KB and 48 KB (measured: K = 8960 1209 → 1354 TFLOP/s).
+// Warp roles (320 threads per CTA):
+//   warp 0      TMA producer of this CTA's halves;
+//   warp 1      TMEM owner (pair allocation, 512 columns = two accumulators) and, in the even CTA, the MMA issuer:
+//               the next tile's MMAs run while the epilogue drains the other accumulator;
 //   warps 2..9  epilogue, two warps per TMEM lane quarter (a warp reaches only lanes 32·(warp % 4) + 0..31), each of
 //               the pair taking 128 of the tile's 256 columns: thread = output row = TMEM lane, 32 columns per
 //               tcgen05.ld with the next load in flight while the current chunk is converted, the epilogue arithmetic
 //               in fp32 with the reference's bf16 rounding points, 64-byte loads of the residual row and 64-byte
 //               stores; the tile's bias and gate columns are staged once in shared memory (one column per thread).
-// With K = 1536 a tile's MMAs take ~9 µs, so the epilogue (GELU included) has to fit in that to stay hidden.
-// Every wait is bounded (4 s, %globaltimer); on expiry the kernel raises its abort and device timeout words and
-// returns, and fvsr_device_check reports FVSR_ETIMEOUT.
+// Synchronisation: stage s is full when the even CTA's full[s] has both CTAs' 64 KB (the odd CTA's loads signal it
+// through its cluster address; only the even producer arrives, with the expected byte count); the MMA commits free
+// stage s in both CTAs (empty[s] of each) and announce an accumulator in both (acc_full of each); each epilogue warp of
+// either CTA arrives once on the even CTA's acc_empty (16 arrivals per tile). Both CTAs walk the same tiles and meet at
+// cluster barriers after set-up and before TMEM is freed. No load is multicast: each CTA loads its own operands.
+// Every wait is bounded (4 s, %globaltimer); on expiry the kernel raises its abort and device timeout words and skips
+// the rest of its work, and fvsr_device_check reports FVSR_ETIMEOUT.
 #include <math.h>
 
 #include "common.cuh"
@@ -31,12 +39,11 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;   // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr int kBM = 256, kBN = 256, kBK = 64, kStages = 6;   // pair tile M × N, K step, ring depth
+constexpr uint32_t kHalfBytes = 128 * kBK * 2;                 // 16 KB: one CTA's A rows or B rows per K step
+constexpr uint32_t kStageBytes = 2 * kHalfBytes;               // A then B
 constexpr int kThreads = 320;
-constexpr int kEpiThreads = 256;    // warps 2..9
+constexpr int kEpiWarps = 8, kEpiThreads = 32 * kEpiWarps;     // warps 2..9
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, kBN, 0, 0);
 // barriers: full[s], empty[s], acc_full[2], acc_empty[2]
@@ -45,8 +52,9 @@ constexpr int kBarFull = 0, kBarEmpty = kStages, kBarAccFull = 2 * kStages, kBar
 constexpr uint32_t kOffBar = kStages * kStageBytes;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-constexpr uint32_t kOffCols = kOffAbort + 12;                    // 16-byte aligned: bias[256], gate[256] as fp32
+constexpr uint32_t kOffCols = (kOffAbort + 4 + 15) & ~15u;     // bias[256], gate[256] as fp32
 constexpr uint32_t kSmemBytes = 1024 + kOffCols + 2 * kBN * 4;
+static_assert(kSmemBytes <= 232448, "shared memory");
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -95,15 +103,17 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* v, int mode, cons
     for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           const GemmArgs a) {
+                          const GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     griddep_wait_then_release();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = a.M / kBM, nt = a.N / kBN, kt = a.K / kBK;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int mt = (a.M + kBM - 1) / kBM, nt = a.N / kBN, kt = a.K / kBK;
     const int tiles = mt * nt;
     volatile uint32_t* abort_word = reinterpret_cast<volatile uint32_t*>(smem + kOffAbort);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmemSlot);
@@ -112,13 +122,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         return mbar_wait(bar(b), parity & 1u, abort_word, &g_gemm_timeout, kWaitLimitNs);
     };
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(bar(kBarFull + s), 1);
-            mbar_init(bar(kBarEmpty + s), 1);
+        for (int st = 0; st < kStages; ++st) {
+            mbar_init(bar(kBarFull + st), 1);
+            mbar_init(bar(kBarEmpty + st), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar(kBarAccFull + b), 1);
-            mbar_init(bar(kBarAccEmpty + b), kEpiThreads);
+            mbar_init(bar(kBarAccEmpty + b), 2 * kEpiWarps);
         }
         *abort_word = 0;
         fence_mbar_init();
@@ -128,111 +138,121 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), 512);
-        tmem_relinquish();
+        tmem_alloc_pair(smem_u32(tmem_slot), 512);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised and their TMEM allocated before any remote signal
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer of this CTA's halves ----------------
         if (lane == 0) {
-            uint32_t it = 0;  // K steps issued by this CTA over all its tiles
+            uint32_t it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-                const int m0 = (t / nt) * kBM, n0 = (t % nt) * kBN;
+            for (int t = pair; ok && t < tiles; t += npairs) {
+                int m0 = (t / nt) * kBM + 128 * (int)rank;
+                const int n0 = (t % nt) * kBN + 128 * (int)rank;
+                if (m0 >= a.M) m0 -= 128;  // past M (odd CTA, last tile row): reload the even rows, stored by no one
                 for (int kb = 0; kb < kt; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (it >= kStages && !(ok = wait(kBarEmpty + s, (it / kStages - 1)))) break;
-                    const uint32_t dst = sbase + (uint32_t)s * kStageBytes;
-                    mbar_expect_tx(bar(kBarFull + s), kStageBytes);
-                    tma_load_2d(dst, &tmA, kb * kBK, m0, bar(kBarFull + s));
-                    tma_load_2d(dst + kABytes, &tmB, kb * kBK, n0, bar(kBarFull + s));
+                    const int st = (int)(it % kStages);
+                    if (it >= kStages && !(ok = wait(kBarEmpty + st, it / kStages - 1))) break;
+                    const uint32_t dst = sbase + (uint32_t)st * kStageBytes;
+                    const uint32_t full0 = mapa_shared(bar(kBarFull + st), 0);
+                    if (rank == 0) mbar_expect_tx(bar(kBarFull + st), 2 * kStageBytes);
+                    tma_load_2d_pair(dst, &tmA, kb * kBK, m0, full0);
+                    tma_load_2d_pair(dst + kHalfBytes, &tmB, kb * kBK, n0, full0);
                 }
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (one thread) ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer: one thread of the even CTA ----------------
+        if (lane == 0 && rank == 0) {
             uint32_t it = 0;
             bool ok = true;
-            int lt = 0;  // tiles of this CTA so far
-            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++lt) {
+            int lt = 0;
+            for (int t = pair; ok && t < tiles; t += npairs, ++lt) {
                 const int acc = lt & 1;
-                // the epilogue drained this accumulator two tiles ago
                 if (lt >= 2 && !(ok = wait(kBarAccEmpty + acc, (uint32_t)((lt >> 1) - 1)))) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)acc * kBN;
                 for (int kb = 0; kb < kt; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (!(ok = wait(kBarFull + s, it / kStages))) break;
+                    const int st = (int)(it % kStages);
+                    if (!(ok = wait(kBarFull + st, it / kStages))) break;
                     tc_fence_after();
-                    const uint32_t sa = sbase + (uint32_t)s * kStageBytes;
+                    const uint32_t sa = sbase + (uint32_t)st * kStageBytes;
                     const uint64_t ad = smem_desc(sa, 16, 1024);
-                    const uint64_t bd = smem_desc(sa + kABytes, 16, 1024);
+                    const uint64_t bd = smem_desc(sa + kHalfBytes, 16, 1024);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
-                        mma_ss(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(bar(kBarEmpty + s));  // the stage is free once these MMAs have read it
+                        mma_ss_pair(d, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), kIdesc,
+                                    (kb > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit_pair(bar(kBarEmpty + st));
+                    mma_commit_pair(mapa_shared(bar(kBarEmpty + st), 1));
                 }
-                if (ok) mma_commit(bar(kBarAccFull + acc));
+                if (ok) {
+                    mma_commit_pair(bar(kBarAccFull + acc));
+                    mma_commit_pair(mapa_shared(bar(kBarAccFull + acc), 1));
+                }
             }
         }
     } else {
-        // ---------------- epilogue: thread = row = TMEM lane, half = which 128 columns ----------------
+        // ---------------- epilogue: this CTA's 128 rows; thread = row = TMEM lane, half = which 128 columns ----------------
         const int quarter = warp & 3, half = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;
-        const int et = threadIdx.x - 64;  // 0..255: the tile column this thread stages
+        const int et = threadIdx.x - 64;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * (kBN / 2));
         float* bias_s = reinterpret_cast<float*>(smem + kOffCols);
         float* gate_s = bias_s + kBN;
+        const uint32_t acc_empty0 = mapa_shared(bar(kBarAccEmpty), 0);
         int lt = 0;
         bool ok = true;
-        // Every epilogue warp runs every tile of the CTA, so the two named barriers per tile always meet; after a
-        // timed-out wait (ok false, the abort word raised) a warp only keeps those barriers and skips the tile.
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+        for (int t = pair; t < tiles; t += npairs, ++lt) {
             const int acc = lt & 1;
-            const int m0 = (t / nt) * kBM, n0 = (t % nt) * kBN;
-            named_barrier_sync(1, kEpiThreads);  // every epilogue thread is done with the previous tile's columns
+            const int m0 = (t / nt) * kBM + 128 * (int)rank, n0 = (t % nt) * kBN;
+            named_barrier_sync(1, kEpiThreads);
             bias_s[et] = a.bias ? __bfloat162float(a.bias[n0 + et]) : 0.0f;
             gate_s[et] = a.mode == kGemmGatedResidual ? __bfloat162float(a.gate[n0 + et]) : 0.0f;
             named_barrier_sync(1, kEpiThreads);
             if (ok) ok = __all_sync(0xffffffffu, wait(kBarAccFull + acc, (uint32_t)(lt >> 1)));
             if (!ok) continue;
             tc_fence_after();
-            const int j = a.split > 0 ? n0 / a.split : 0;
-            const int c0 = (a.split > 0 ? n0 - j * a.split : n0) + half * (kBN / 2);
-            const int64_t row = (int64_t)(m0 + r);
-            void* const ob = j == 0 ? a.out[0] : (j == 1 ? a.out[1] : a.out[2]);  // no dynamic index into the params
-            __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(ob) + row * a.ldo + c0;
-            const __nv_bfloat16* rrow = a.resid ? a.resid + row * a.ldo + c0 : nullptr;
-            const float* bcol = bias_s + half * (kBN / 2);
-            const float* gcol = gate_s + half * (kBN / 2);
-            const uint32_t tbase = lane_base + (uint32_t)acc * kBN;
-            uint32_t va[32], vb[32];
-            tmem_ld32(tbase, va);
-            tmem_ld_wait(va);
+            if (m0 < a.M) {  // the odd CTA of the last row of tiles may lie wholly past M
+                const int j = a.split > 0 ? n0 / a.split : 0;
+                const int c0 = (a.split > 0 ? n0 - j * a.split : n0) + half * (kBN / 2);
+                const int64_t row = (int64_t)(m0 + r);
+                void* const ob = j == 0 ? a.out[0] : (j == 1 ? a.out[1] : a.out[2]);
+                __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(ob) + row * a.ldo + c0;
+                const __nv_bfloat16* rrow = a.resid ? a.resid + row * a.ldo + c0 : nullptr;
+                const float* bcol = bias_s + half * (kBN / 2);
+                const float* gcol = gate_s + half * (kBN / 2);
+                const uint32_t tbase = lane_base + (uint32_t)acc * kBN;
+                uint32_t va[32], vb[32];
+                tmem_ld32(tbase, va);
+                tmem_ld_wait(va);
 #pragma unroll
-            for (int c = 0; c < kBN / 64; c += 2) {
-                tmem_ld32(tbase + 32u * (c + 1), vb);
-                epilogue_chunk(va, a.mode, bcol + 32 * c, gcol + 32 * c, rrow ? rrow + 32 * c : nullptr, orow + 32 * c);
-                tmem_ld_wait(vb);
-                if (c + 2 < kBN / 64) tmem_ld32(tbase + 32u * (c + 2), va);
-                epilogue_chunk(vb, a.mode, bcol + 32 * (c + 1), gcol + 32 * (c + 1),
-                               rrow ? rrow + 32 * (c + 1) : nullptr, orow + 32 * (c + 1));
-                if (c + 2 < kBN / 64) tmem_ld_wait(va);
+                for (int c = 0; c < kBN / 64; c += 2) {
+                    tmem_ld32(tbase + 32u * (c + 1), vb);
+                    epilogue_chunk(va, a.mode, bcol + 32 * c, gcol + 32 * c, rrow ? rrow + 32 * c : nullptr,
+                                   orow + 32 * c);
+                    tmem_ld_wait(vb);
+                    if (c + 2 < kBN / 64) tmem_ld32(tbase + 32u * (c + 2), va);
+                    epilogue_chunk(vb, a.mode, bcol + 32 * (c + 1), gcol + 32 * (c + 1),
+                                   rrow ? rrow + 32 * (c + 1) : nullptr, orow + 32 * (c + 1));
+                    if (c + 2 < kBN / 64) tmem_ld_wait(va);
+                }
             }
             tc_fence_before();
-            mbar_arrive(bar(kBarAccEmpty + acc));  // the MMA thread may now reuse this accumulator
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * (uint32_t)acc);  // the even CTA's acc_empty[acc]
         }
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();  // no signal to the other CTA and no MMA on this CTA's shared memory is still in flight
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc_pair(tmem, 512);
     }
 }
 
@@ -241,10 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 size_t gemm_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B, cudaStream_t st) {
-    if (args.M % kBM || args.N % kBN || args.K % kBK || args.M <= 0 || args.N <= 0 || args.K <= 0)
+    if (args.M % 128 || args.N % kBN || args.K % kBK || args.M <= 0 || args.N <= 0 || args.K <= 0)
         return cudaErrorInvalidValue;
     CUtensorMap ma, mb;
-    if (!make_tile_map_box(&ma, A, args.M, args.K, kBM) || !make_tile_map_box(&mb, B, args.N, args.K, kBN))
+    if (!make_tile_map_box(&ma, A, args.M, args.K, 128) || !make_tile_map_box(&mb, B, args.N, args.K, 128))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(gemm_bf16_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kSmemBytes);
@@ -252,9 +272,23 @@ cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B,
     int dev = 0, nsm = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    const int tiles = (args.M / kBM) * (args.N / kBN);
-    const int grid = tiles < nsm ? tiles : nsm;
-    return launch_pdl(gemm_bf16_sm100_kernel, dim3(grid), dim3(kThreads), (size_t)kSmemBytes, st, ma, mb, args);
+    const int tiles = ((args.M + kBM - 1) / kBM) * (args.N / kBN);
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    int resident = 0;  // pairs that fit on the GPU at once (one CTA per SM, both SMs of a pair on one TPC)
+    cfg.gridDim = dim3(nsm & ~1);
+    if (cudaOccupancyMaxActiveClusters(&resident, gemm_bf16_sm100_kernel, &cfg) != cudaSuccess || resident < 1)
+        resident = nsm / 2;
+    const int pairs = tiles < resident ? tiles : resident;
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_bf16_sm100_kernel, ma, mb, args);
 }
 
 cudaError_t read_and_clear_gemm_error(int* flag) {
