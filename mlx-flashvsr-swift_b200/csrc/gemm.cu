@@ -56,24 +56,64 @@ constexpr uint32_t kOffCols = (kOffAbort + 4 + 15) & ~15u;     // bias[256], gat
 constexpr uint32_t kSmemBytes = 1024 + kOffCols + 2 * kBN * 4;
 static_assert(kSmemBytes <= 232448, "shared memory");
 
-__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// Packed fp32 pairs (Blackwell's two-wide FFMA/FADD/FMUL: one instruction for two lanes of arithmetic, same rounding).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void uf2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// The two bf16 halves of a packed pair as fp32 (exact).
+__device__ __forceinline__ void bf2_to_f(uint32_t p, float& lo, float& hi) {
+    lo = __uint_as_float(p << 16);
+    hi = __uint_as_float(p & 0xffff0000u);
+}
 
-// GELU with the tanh approximation, as MLX's GELU(approximation: .tanh): 0.5·x·(1 + tanh(√(2/π)·(x + 0.044715·x³))),
-// with tanh(y) = 1 − 2 / (e^(2y) + 1) from the fast exponential (relative error ~1e-6, far below a bf16 step; e^(2y)
-// overflowing to +inf gives 1, underflowing to 0 gives −1).
-__device__ __forceinline__ float gelu_tanh(float x) {
-    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-    const float y = k0 * (x + k1 * x * x * x);
-    const float t = 1.0f - __fdividef(2.0f, __expf(2.0f * y) + 1.0f);
-    return 0.5f * x * (1.0f + t);
+// GELU with the tanh approximation, as MLX's GELU(approximation: .tanh): 0.5·x·(1 + tanh(y)), y = √(2/π)·(x +
+// 0.044715·x³), evaluated through 0.5·(1 + tanh(y)) = 1 / (1 + e^(−2y)) as x / (1 + 2^z), z = x·(c0 + c1·x²) with
+// c0 = −2·√(2/π)·log2(e), c1 = 0.044715·c0 (relative error ~1e-6, far below a bf16 step; 2^z overflowing to +inf gives
+// 0, underflowing to 0 gives x). Two outputs per call, packed arithmetic except the two exponentials and reciprocals.
+__device__ __forceinline__ void gelu_tanh2(float& x0, float& x1) {
+    constexpr float c0 = -2.0f * 0.7978845608028654f * 1.4426950408889634f, c1 = 0.044715f * c0;
+    const uint64_t x = f2(x0, x1);
+    float z0, z1;
+    uf2(fmul2(x, ffma2(fmul2(x, x), f2(c1, c1), f2(c0, c0))), z0, z1);
+    float d0, d1;
+    uf2(fadd2(f2(ex2_approx(z0), ex2_approx(z1)), f2(1.0f, 1.0f)), d0, d1);
+    uf2(fmul2(x, f2(rcp_approx(d0), rcp_approx(d1))), x0, x1);
 }
 
 // 32 consecutive output columns of one row: v = the fp32 accumulators, bias / gate = the columns' fp32 values in
-// shared memory (broadcast reads), resid / out = the row's bf16 columns in global memory (64 bytes each).
-__device__ __forceinline__ void epilogue_chunk(const uint32_t* v, int mode, const float* bias, const float* gate,
+// shared memory (broadcast reads), resid / out = the row's bf16 columns in global memory (64 bytes each). Rounding
+// points as the reference's ops: Linear = round(acc + bias); GELU = round(gelu(Linear)); gated residual =
+// round(resid + round(gate · Linear)).
+template <int kMode>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t* v, const float* bias, const float* gate,
                                                const __nv_bfloat16* resid, __nv_bfloat16* out) {
     uint32_t rv[16];
-    if (mode == kGemmGatedResidual) {
+    if (kMode == kGemmGatedResidual) {
         const uint4* rp = reinterpret_cast<const uint4*>(resid);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -83,26 +123,38 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t* v, int mode, cons
     }
     uint32_t w[16];
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-        float y[2];
+    for (int i = 0; i < 32; i += 4) {
+        const float4 b = *reinterpret_cast<const float4*>(bias + i);
+        float x[4];
+        uf2(fadd2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), f2(b.x, b.y)), x[0], x[1]);
+        uf2(fadd2(f2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])), f2(b.z, b.w)), x[2], x[3]);
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            float x = bf16_round(__uint_as_float(v[i + u]) + bias[i + u]);  // the Linear's output
-            if (mode == kGemmGelu) x = bf16_round(gelu_tanh(x));
-            if (mode == kGemmGatedResidual) {                                // tok + gate · f(x)
-                const uint32_t rw = rv[(i + u) >> 1];
-                const float rx = __uint_as_float(((i + u) & 1) ? (rw & 0xffff0000u) : (rw << 16));
-                x = bf16_round(rx + bf16_round(gate[i + u] * x));
+        for (int u = 0; u < 4; u += 2) {
+            uint32_t p = pack_bf16x2(x[u], x[u + 1]);  // the Linear's output
+            if (kMode == kGemmGelu) {
+                float y0, y1;
+                bf2_to_f(p, y0, y1);
+                gelu_tanh2(y0, y1);
+                p = pack_bf16x2(y0, y1);
+            } else if (kMode == kGemmGatedResidual) {  // tok + gate · f(x)
+                float y0, y1, r0, r1, g0, g1;
+                bf2_to_f(p, y0, y1);
+                const float2 g = *reinterpret_cast<const float2*>(gate + i + u);
+                uf2(fmul2(f2(g.x, g.y), f2(y0, y1)), g0, g1);
+                bf2_to_f(pack_bf16x2(g0, g1), g0, g1);
+                bf2_to_f(rv[(i + u) >> 1], r0, r1);
+                uf2(fadd2(f2(r0, r1), f2(g0, g1)), y0, y1);
+                p = pack_bf16x2(y0, y1);
             }
-            y[u] = x;
+            w[(i + u) >> 1] = p;
         }
-        w[i >> 1] = pack_bf16x2(y[0], y[1]);
     }
     uint4* dst = reinterpret_cast<uint4*>(out);
 #pragma unroll
     for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
+template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const GemmArgs a) {
@@ -213,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int m0 = (t / nt) * kBM + 128 * (int)rank, n0 = (t % nt) * kBN;
             named_barrier_sync(1, kEpiThreads);
             bias_s[et] = a.bias ? __bfloat162float(a.bias[n0 + et]) : 0.0f;
-            gate_s[et] = a.mode == kGemmGatedResidual ? __bfloat162float(a.gate[n0 + et]) : 0.0f;
+            gate_s[et] = kMode == kGemmGatedResidual ? __bfloat162float(a.gate[n0 + et]) : 0.0f;
             named_barrier_sync(1, kEpiThreads);
             if (ok) ok = __all_sync(0xffffffffu, wait(kBarAccFull + acc, (uint32_t)(lt >> 1)));
             if (!ok) continue;
@@ -234,11 +286,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < kBN / 64; c += 2) {
                     tmem_ld32(tbase + 32u * (c + 1), vb);
-                    epilogue_chunk(va, a.mode, bcol + 32 * c, gcol + 32 * c, rrow ? rrow + 32 * c : nullptr,
+                    epilogue_chunk<kMode>(va, bcol + 32 * c, gcol + 32 * c, rrow ? rrow + 32 * c : nullptr,
                                    orow + 32 * c);
                     tmem_ld_wait(vb);
                     if (c + 2 < kBN / 64) tmem_ld32(tbase + 32u * (c + 2), va);
-                    epilogue_chunk(vb, a.mode, bcol + 32 * (c + 1), gcol + 32 * (c + 1),
+                    epilogue_chunk<kMode>(vb, bcol + 32 * (c + 1), gcol + 32 * (c + 1),
                                    rrow ? rrow + 32 * (c + 1) : nullptr, orow + 32 * (c + 1));
                     if (c + 2 < kBN / 64) tmem_ld_wait(va);
                 }
@@ -256,18 +308,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
-}  // namespace
-
-size_t gemm_smem_bytes() { return kSmemBytes; }
-
-cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B, cudaStream_t st) {
-    if (args.M % 128 || args.N % kBN || args.K % kBK || args.M <= 0 || args.N <= 0 || args.K <= 0)
-        return cudaErrorInvalidValue;
-    CUtensorMap ma, mb;
-    if (!make_tile_map_box(&ma, A, args.M, args.K, 128) || !make_tile_map_box(&mb, B, args.N, args.K, 128))
-        return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBytes);
+template <int kMode>
+cudaError_t launch_gemm_mode(const GemmArgs& args, const CUtensorMap& ma, const CUtensorMap& mb, cudaStream_t st) {
+    auto kernel = gemm_bf16_sm100_kernel<kMode>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess) return e;
     int dev = 0, nsm = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
@@ -278,8 +322,7 @@ cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B,
     cfg.dynamicSmemBytes = kSmemBytes;
     int resident = 0;  // pairs that fit on the GPU at once (one CTA per SM, both SMs of a pair on one TPC)
     cfg.gridDim = dim3(nsm & ~1);
-    if (cudaOccupancyMaxActiveClusters(&resident, gemm_bf16_sm100_kernel, &cfg) != cudaSuccess || resident < 1)
-        resident = nsm / 2;
+    if (cudaOccupancyMaxActiveClusters(&resident, kernel, &cfg) != cudaSuccess || resident < 1) resident = nsm / 2;
     const int pairs = tiles < resident ? tiles : resident;
     cfg.gridDim = dim3(2 * pairs);
     cfg.stream = st;
@@ -288,7 +331,25 @@ cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_bf16_sm100_kernel, ma, mb, args);
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, args);
+}
+
+}  // namespace
+
+size_t gemm_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_gemm_bf16(const GemmArgs& args, const void* A, const void* B, cudaStream_t st) {
+    if (args.M % 128 || args.N % kBN || args.K % kBK || args.M <= 0 || args.N <= 0 || args.K <= 0)
+        return cudaErrorInvalidValue;
+    CUtensorMap ma, mb;
+    if (!make_tile_map_box(&ma, A, args.M, args.K, 128) || !make_tile_map_box(&mb, B, args.N, args.K, 128))
+        return cudaErrorInvalidValue;
+    switch (args.mode) {
+        case kGemmPlain: return launch_gemm_mode<kGemmPlain>(args, ma, mb, st);
+        case kGemmGelu: return launch_gemm_mode<kGemmGelu>(args, ma, mb, st);
+        case kGemmGatedResidual: return launch_gemm_mode<kGemmGatedResidual>(args, ma, mb, st);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t read_and_clear_gemm_error(int* flag) {
