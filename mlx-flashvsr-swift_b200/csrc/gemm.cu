@@ -56,41 +56,6 @@ constexpr uint32_t kOffCols = (kOffAbort + 4 + 15) & ~15u;     // bias[256], gat
 constexpr uint32_t kSmemBytes = 1024 + kOffCols + 2 * kBN * 4;
 static_assert(kSmemBytes <= 232448, "shared memory");
 
-// Packed fp32 pairs (Blackwell's two-wide FFMA/FADD/FMUL: one instruction for two lanes of arithmetic, same rounding).
-__device__ __forceinline__ uint64_t f2(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void uf2(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-// The two bf16 halves of a packed pair as fp32 (exact).
-__device__ __forceinline__ void bf2_to_f(uint32_t p, float& lo, float& hi) {
-    lo = __uint_as_float(p << 16);
-    hi = __uint_as_float(p & 0xffff0000u);
-}
-
 // GELU with the tanh approximation, as MLX's GELU(approximation: .tanh): 0.5·x·(1 + tanh(y)), y = √(2/π)·(x +
 // 0.044715·x³), evaluated through 0.5·(1 + tanh(y)) = 1 / (1 + e^(−2y)) as x / (1 + 2^z), z = x·(c0 + c1·x²) with
 // c0 = −2·√(2/π)·log2(e), c1 = 0.044715·c0 (relative error ~1e-6, far below a bf16 step; 2^z overflowing to +inf gives
@@ -106,21 +71,23 @@ __device__ __forceinline__ void gelu_tanh2(float& x0, float& x1) {
 }
 
 // 32 consecutive output columns of one row: v = the fp32 accumulators, bias / gate = the columns' fp32 values in
-// shared memory (broadcast reads), resid / out = the row's bf16 columns in global memory (64 bytes each). Rounding
+// shared memory (broadcast reads), rv = the residual's bf16 pairs (gated residual only), out = the row's bf16 columns
+// in global memory (64 bytes). Rounding
 // points as the reference's ops: Linear = round(acc + bias); GELU = round(gelu(Linear)); gated residual =
 // round(resid + round(gate · Linear)).
+// The 32 bf16 residual values of a chunk (64 bytes of one row), loaded ahead of their use.
+__device__ __forceinline__ void load_resid(const __nv_bfloat16* resid, uint32_t* rv) {
+    const uint4* rp = reinterpret_cast<const uint4*>(resid);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 q = rp[i];
+        rv[4 * i] = q.x, rv[4 * i + 1] = q.y, rv[4 * i + 2] = q.z, rv[4 * i + 3] = q.w;
+    }
+}
+
 template <int kMode>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t* v, const float* bias, const float* gate,
-                                               const __nv_bfloat16* resid, __nv_bfloat16* out) {
-    uint32_t rv[16];
-    if (kMode == kGemmGatedResidual) {
-        const uint4* rp = reinterpret_cast<const uint4*>(resid);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 q = rp[i];
-            rv[4 * i] = q.x, rv[4 * i + 1] = q.y, rv[4 * i + 2] = q.z, rv[4 * i + 3] = q.w;
-        }
-    }
+                                               const uint32_t* rv, __nv_bfloat16* out) {
     uint32_t w[16];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
@@ -267,16 +234,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             bias_s[et] = a.bias ? __bfloat162float(a.bias[n0 + et]) : 0.0f;
             gate_s[et] = kMode == kGemmGatedResidual ? __bfloat162float(a.gate[n0 + et]) : 0.0f;
             named_barrier_sync(1, kEpiThreads);
+            const bool live = m0 < a.M;  // the odd CTA of the last row of tiles may lie wholly past M
+            const int j = a.split > 0 ? n0 / a.split : 0;
+            const int c0 = (a.split > 0 ? n0 - j * a.split : n0) + half * (kBN / 2);
+            const int64_t row = (int64_t)(m0 + r);
+            const __nv_bfloat16* rrow = a.resid ? a.resid + row * a.ldo + c0 : nullptr;
+            uint32_t ra[16], rb[16];
+            if (kMode == kGemmGatedResidual && ok && live) load_resid(rrow, ra);  // in flight during the wait
             if (ok) ok = __all_sync(0xffffffffu, wait(kBarAccFull + acc, (uint32_t)(lt >> 1)));
             if (!ok) continue;
             tc_fence_after();
-            if (m0 < a.M) {  // the odd CTA of the last row of tiles may lie wholly past M
-                const int j = a.split > 0 ? n0 / a.split : 0;
-                const int c0 = (a.split > 0 ? n0 - j * a.split : n0) + half * (kBN / 2);
-                const int64_t row = (int64_t)(m0 + r);
+            if (live) {
                 void* const ob = j == 0 ? a.out[0] : (j == 1 ? a.out[1] : a.out[2]);
                 __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(ob) + row * a.ldo + c0;
-                const __nv_bfloat16* rrow = a.resid ? a.resid + row * a.ldo + c0 : nullptr;
                 const float* bcol = bias_s + half * (kBN / 2);
                 const float* gcol = gate_s + half * (kBN / 2);
                 const uint32_t tbase = lane_base + (uint32_t)acc * kBN;
@@ -286,12 +256,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c = 0; c < kBN / 64; c += 2) {
                     tmem_ld32(tbase + 32u * (c + 1), vb);
-                    epilogue_chunk<kMode>(va, bcol + 32 * c, gcol + 32 * c, rrow ? rrow + 32 * c : nullptr,
-                                   orow + 32 * c);
+                    if (kMode == kGemmGatedResidual) load_resid(rrow + 32 * (c + 1), rb);
+                    epilogue_chunk<kMode>(va, bcol + 32 * c, gcol + 32 * c, ra, orow + 32 * c);
                     tmem_ld_wait(vb);
-                    if (c + 2 < kBN / 64) tmem_ld32(tbase + 32u * (c + 2), va);
-                    epilogue_chunk<kMode>(vb, bcol + 32 * (c + 1), gcol + 32 * (c + 1),
-                                   rrow ? rrow + 32 * (c + 1) : nullptr, orow + 32 * (c + 1));
+                    if (c + 2 < kBN / 64) {
+                        tmem_ld32(tbase + 32u * (c + 2), va);
+                        if (kMode == kGemmGatedResidual) load_resid(rrow + 32 * (c + 2), ra);
+                    }
+                    epilogue_chunk<kMode>(vb, bcol + 32 * (c + 1), gcol + 32 * (c + 1), rb, orow + 32 * (c + 1));
                     if (c + 2 < kBN / 64) tmem_ld_wait(va);
                 }
             }

@@ -11,10 +11,13 @@
 //   RMSNorm:   inv = 1 / √(Σx² / C + eps), round(round(x·inv)·w).
 // Sums run as lane partials in channel order, then a xor butterfly (MLX's order is unspecified).
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace fvsr {
 
 namespace {
+
+using namespace sm100;
 
 constexpr int kMaxChunks = 8;  // 8 × 256 = 2048 channels
 
@@ -40,15 +43,22 @@ __device__ __forceinline__ void load_row(const __nv_bfloat16* row, int nch, int 
     }
 }
 
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t*>(&v);
-}
-
 __device__ __forceinline__ float ldb(const __nv_bfloat16* p, int i) { return __bfloat162float(p[i]); }
 
-// Shared-memory vectors of a CTA: [kVecs][ch] fp32.
+// Shared-memory vectors of a CTA: [kVecs][ch] fp32, each stored so that the eight columns a lane owns in a 256-column
+// chunk (256c + 8·lane + 0..7) are two float4 at ((2c + h)·32 + lane)·4, h = 0, 1: a warp's float4 reads are
+// consecutive 16-byte words (no bank conflicts; the natural layout gives 8-way conflicts on scalar reads).
 enum { kVW = 0, kVB = 1, kVShift = 2, kVScale1 = 3, kVecs = 4 };
+__device__ __forceinline__ int vec_pos(int col) {
+    const int c = col >> 8, lane = (col >> 3) & 31, i = col & 7;
+    return (((c << 1) + (i >> 2)) * 32 + lane) * 4 + (i & 3);
+}
+// The eight vector values of a lane's columns in chunk c.
+__device__ __forceinline__ void vec8(const float* v, int c, int lane, float (&out)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(v + ((2 * c) * 32 + lane) * 4);
+    const float4 b = *reinterpret_cast<const float4*>(v + ((2 * c + 1) * 32 + lane) * 4);
+    out[0] = a.x, out[1] = a.y, out[2] = a.z, out[3] = a.w, out[4] = b.x, out[5] = b.y, out[6] = b.z, out[7] = b.w;
+}
 
 template <int NCH>
 __global__ void __launch_bounds__(256, 2) layernorm_kernel(int m, int ch, const __nv_bfloat16* __restrict__ x,
@@ -60,10 +70,11 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(int m, int ch, const 
     extern __shared__ float vec[];
     griddep_wait_then_release();
     for (int i = threadIdx.x; i < ch; i += blockDim.x) {
-        vec[kVW * ch + i] = weight ? ldb(weight, i) : 1.0f;
-        vec[kVB * ch + i] = bias ? ldb(bias, i) : 0.0f;
-        vec[kVShift * ch + i] = shift ? ldb(shift, i) : 0.0f;
-        vec[kVScale1 * ch + i] = scale ? bf(__fadd_rn(1.0f, ldb(scale, i))) : 1.0f;
+        const int pos = vec_pos(i);
+        vec[kVW * ch + pos] = weight ? ldb(weight, i) : 1.0f;
+        vec[kVB * ch + pos] = bias ? ldb(bias, i) : 0.0f;
+        vec[kVShift * ch + pos] = shift ? ldb(shift, i) : 0.0f;
+        vec[kVScale1 * ch + pos] = scale ? bf(__fadd_rn(1.0f, ldb(scale, i))) : 1.0f;
     }
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -88,24 +99,37 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(int m, int ch, const 
         const float var = __fdiv_rn(warp_sum(q), (float)ch);
         const float rstd = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
         __nv_bfloat16* orow = out + (int64_t)rowi * ch;
+        const uint64_t negmean2 = f2(-mean, -mean), rstd2 = f2(rstd, rstd);
 #pragma unroll
         for (int c = 0; c < kMaxChunks; ++c) {
             if (c >= nch) continue;
             const int col0 = 256 * c + 8 * lane;
+            float wv[8], bv[8], s1[8], sh[8];
+            if (affine) {
+                vec8(vec + kVW * ch, c, lane, wv);
+                vec8(vec + kVB * ch, c, lane, bv);
+            }
+            if (modulate) {
+                vec8(vec + kVScale1 * ch, c, lane, s1);
+                vec8(vec + kVShift * ch, c, lane, sh);
+            }
             uint32_t w[4];
 #pragma unroll
             for (int i = 0; i < 8; i += 2) {
-                float y[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int col = col0 + i + u;
-                    float n = __fmul_rn(__fsub_rn(v[8 * c + i + u], mean), rstd);
-                    if (affine) n = __fmaf_rn(n, vec[kVW * ch + col], vec[kVB * ch + col]);
-                    n = bf(n);
-                    if (modulate) n = bf(__fadd_rn(bf(__fmul_rn(n, vec[kVScale1 * ch + col])), vec[kVShift * ch + col]));
-                    y[u] = n;
+                // n = (x − mean)·rstd, two columns per packed op, each rounded as the scalar ops would be
+                uint64_t n2 = fmul2(fadd2(f2(v[8 * c + i], v[8 * c + i + 1]), negmean2), rstd2);
+                if (affine) n2 = ffma2(n2, f2(wv[i], wv[i + 1]), f2(bv[i], bv[i + 1]));
+                float n0, n1;
+                uf2(n2, n0, n1);
+                uint32_t p = pack_bf16x2(n0, n1);
+                if (modulate) {  // round(round(n·round(1 + scale)) + shift)
+                    bf2_to_f(p, n0, n1);
+                    uf2(fmul2(f2(n0, n1), f2(s1[i], s1[i + 1])), n0, n1);
+                    bf2_to_f(pack_bf16x2(n0, n1), n0, n1);
+                    uf2(fadd2(f2(n0, n1), f2(sh[i], sh[i + 1])), n0, n1);
+                    p = pack_bf16x2(n0, n1);
                 }
-                w[i >> 1] = pack2(y[0], y[1]);
+                w[i >> 1] = p;
             }
             *reinterpret_cast<uint4*>(orow + col0) = make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -118,7 +142,7 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_kernel(int m, int ch, const __
                                                       __nv_bfloat16* __restrict__ out) {
     extern __shared__ float vec[];
     griddep_wait_then_release();
-    for (int i = threadIdx.x; i < ch; i += blockDim.x) vec[i] = ldb(weight, i);
+    for (int i = threadIdx.x; i < ch; i += blockDim.x) vec[vec_pos(i)] = ldb(weight, i);
     __syncthreads();
     const int lane = threadIdx.x & 31;
     constexpr int nch = NCH;
@@ -130,17 +154,22 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_kernel(int m, int ch, const __
         for (int i = 0; i < kMaxChunks * 8; ++i)
             if (i < nch * 8) s = __fmaf_rn(v[i], v[i], s);
         const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(s), (float)ch), eps)));
+        const uint64_t inv2 = f2(inv, inv);
         __nv_bfloat16* orow = out + (int64_t)rowi * ch;
 #pragma unroll
         for (int c = 0; c < kMaxChunks; ++c) {
             if (c >= nch) continue;
             const int col0 = 256 * c + 8 * lane;
+            float wv[8];
+            vec8(vec, c, lane, wv);
             uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const float y0 = bf(__fmul_rn(bf(__fmul_rn(v[8 * c + i], inv)), vec[col0 + i]));
-                const float y1 = bf(__fmul_rn(bf(__fmul_rn(v[8 * c + i + 1], inv)), vec[col0 + i + 1]));
-                w[i >> 1] = pack2(y0, y1);
+            for (int i = 0; i < 8; i += 2) {  // round(round(x·inv)·w), two columns per packed op
+                float y0, y1;
+                uf2(fmul2(f2(v[8 * c + i], v[8 * c + i + 1]), inv2), y0, y1);
+                bf2_to_f(pack_bf16x2(y0, y1), y0, y1);
+                uf2(fmul2(f2(y0, y1), f2(wv[i], wv[i + 1])), y0, y1);
+                w[i >> 1] = pack_bf16x2(y0, y1);
             }
             *reinterpret_cast<uint4*>(orow + col0) = make_uint4(w[0], w[1], w[2], w[3]);
         }
