@@ -938,11 +938,22 @@ def run_linear(args):
                      "torch_matmul_ms": t_lib, "torch_matmul_tflops": flop / (t_lib * 1e-3) / 1e12}
         total_flop += flop
         total_ms += t_ours
+    # the block's row normalisations at the same M (bytes moved = read + write of (M, d) bf16)
+    vecs = [rnd(d, scale=0.3) for _ in range(4)]
+    nout = torch.empty_like(x)
+    norm_calls = {"layernorm_modulated": lambda: pkg.layernorm(x, shift=vecs[0], scale=vecs[1], out=nout),
+                  "layernorm_affine": lambda: pkg.layernorm(x, weight=vecs[2], bias=vecs[3], out=nout),
+                  "rmsnorm": lambda: pkg.rmsnorm(x, vecs[2], out=nout),
+                  "copy_same_bytes": lambda: nout.copy_(x)}
+    norms = {}
+    for name, fn in norm_calls.items():
+        us = graph_time_us(fn, 20, max(args.warmup, 3))
+        norms[name] = {"us": us, "gbs": 2 * m * d * 2 / (us * 1e-6) / 1e9}
     pkg.device_check()
     print(json.dumps({"metric": f"DiT block linear layers on tcgen05, config {args.config} chunk (M = {m})",
                       "value": total_flop / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_block": total_ms,
                       "peak": peak, "peak_kind": f"{kind} bf16 burst", "frac": total_flop / (total_ms * 1e-3) / 1e12 / peak,
-                      "layers": res, "gpu_launches_per_block": 4, "launch": "CUDA graph of 10 calls per shape",
+                      "layers": res, "norms": norms, "gpu_launches_per_block": 4, "launch": "CUDA graph of 10 calls per shape",
                       "note": "torch_matmul is cuBLAS on the same shapes without the bias / epilogue, for reference"}),
           flush=True)
 

@@ -305,7 +305,8 @@ fvsr_status fvsr_lcsa_forward_tokens(const fvsr_lcsa_params* p, const void* q_li
  * layout), bias (N) or NULL, all bf16; out (M, N) bf16; M a multiple of 128, N of 256, K of 64 (FVSR_EINVAL else).
  * fp32 accumulation; the output is rounded to bf16 once (the Linear), and the epilogues keep the reference's
  * rounding points: GELU → round(gelu(linear)); gated residual → round(resid + round(gate · linear)) with gate (N)
- * and resid (M, N) bf16 (resid may be out). One persistent tcgen05 kernel. */
+ * and resid (M, N) bf16 (resid may be out). One persistent tcgen05 kernel over CTA pairs (clusters of two CTAs,
+ * 256 × 256 output tiles). */
 typedef enum fvsr_linear_epilogue {
     FVSR_LINEAR = 0,
     FVSR_LINEAR_GELU = 1,
