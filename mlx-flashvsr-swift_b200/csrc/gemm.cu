@@ -23,7 +23,7 @@
 // through its cluster address; only the even producer arrives, with the expected byte count); the MMA commits free
 // stage s in both CTAs (empty[s] of each) and announce an accumulator in both (acc_full of each); each epilogue warp of
 // either CTA arrives once on the even CTA's acc_empty (16 arrivals per tile). Both CTAs walk the same tiles and meet at
-// cluster barriers after set-up and before TMEM is freed. No load is multicast: each CTA loads its own operands.
+// cluster barriers after set-up and before TMEM is freed. Each CTA loads only its own operands, with plain tile loads.
 // Every wait is bounded (4 s, %globaltimer); on expiry the kernel raises its abort and device timeout words and skips
 // the rest of its work, and fvsr_device_check reports FVSR_ETIMEOUT.
 #include <math.h>
