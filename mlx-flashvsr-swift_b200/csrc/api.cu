@@ -179,13 +179,13 @@ fvsr_status run_select(const fvsr_lcsa_params* p, const Dims& d, const float* po
 fvsr_status run_attention(const fvsr_lcsa_params* p, const Dims& d, const void* q, const void* k, const void* v,
                           int64_t kv_rows, const KvPages& pages, const int32_t* kidx, const int32_t* kcnt, void* out,
                           cudaStream_t st, int item_begin = 0, int item_count = -1, const int32_t* order = nullptr,
-                          OutRows rows = {}, AttnSplit split = {}) {
+                          OutRows rows = {}, AttnSplit split = {}, FreshKv fresh = {}) {
     fvsr_status s = check_device_sm100();
     if (s != FVSR_OK) return s;
     if (item_count < 0) item_count = d.heads * d.nq;
     if (p->dtype == FVSR_BF16) {
         FVSR_CU(launch_attn_bf16(q, k, v, kv_rows, pages, d.heads, d.nq, d.nk, kidx, kcnt, out, item_begin, item_count,
-                                 order, st, rows, split),
+                                 order, st, rows, split, fresh),
                 "bf16 attention launch");
     } else {
         FVSR_CU(launch_attn_f32(static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
@@ -209,6 +209,10 @@ struct fvsr_kv_cache {
     void* v_arena = nullptr;
     float* pk_arena = nullptr;   // pooled keys, (capacity·page_blocks, H·128) fp32
     int device = 0;
+    // fvsr_lcsa_forward's copy of the appended slices into the arena runs on this stream beside the selection and the
+    // attention (which read the new slices from the caller's buffers); fork / join events order it (bf16 caches)
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
     int64_t page_rows() const { return (int64_t)page_blocks * 128; }
     int64_t page_bytes() const { return page_rows() * d.channels * d.elt; }
     int64_t slice_bytes() const { return (int64_t)d.s * 128 * d.channels * d.elt; }
@@ -579,12 +583,23 @@ fvsr_status fvsr_kv_cache_create_padded(const fvsr_lcsa_params* p, int32_t kv_le
         delete c;
         return fail(FVSR_ENOMEM, "cache arena allocation of %zu bytes failed", 2 * bytes + pbytes);
     }
+    if (c->p.dtype == FVSR_BF16 &&
+        (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming) != cudaSuccess ||
+         cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming) != cudaSuccess)) {
+        cudaGetLastError();
+        fvsr_kv_cache_destroy(c);
+        return fail(FVSR_ECUDA, "cache side stream creation failed");
+    }
     *cache = c;
     return FVSR_OK;
 }
 
 fvsr_status fvsr_kv_cache_destroy(fvsr_kv_cache* c) {
     if (!c) return FVSR_OK;
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->fork) cudaEventDestroy(c->fork);
+    if (c->join) cudaEventDestroy(c->join);
     cudaFree(c->k_arena);
     cudaFree(c->v_arena);
     cudaFree(c->pk_arena);
@@ -699,18 +714,71 @@ fvsr_status fvsr_lcsa_forward(const fvsr_lcsa_params* p, const void* q, const vo
     s = check_workspace(w, workspace, workspace_bytes);
     if (s != FVSR_OK) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    s = fvsr_kv_cache_append(cache, k_new, v_new, p->q_slices, stream);
-    if (s != FVSR_OK) return s;
-    const KvPages pages = cache->kv_pages();
     int32_t* li = kidx ? kidx : w.kidx;
     int32_t* lc = kcnt ? kcnt : w.kcnt;
+    if (pp.dtype != FVSR_BF16) {  // the fp32 lane reads the arena: append first
+        s = fvsr_kv_cache_append(cache, k_new, v_new, p->q_slices, stream);
+        if (s != FVSR_OK) return s;
+        const KvPages pages = cache->kv_pages();
+        FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, nullptr, 0, nullptr, pp.dtype, (int)d.channels, st, w.hist,
+                             select_hist_bytes(d.heads, d.q_slices) / 4),
+                "pool q launch");
+        s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, w.order, st);
+        if (s != FVSR_OK) return s;
+        s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(),
+                          pages, li, lc, out, st, 0, d.heads * d.nq, w.order);
+        if (s != FVSR_OK) return s;
+        return fvsr_kv_cache_trim(cache);
+    }
+    // bf16: the new slices' keys are pooled into their arena pages (the selection reads every slice's pooled keys
+    // there); their K/V rows are copied into the pages on the cache's side stream while the selection and the
+    // attention run, the attention reading those blocks from k_new / v_new themselves; the call's stream waits for
+    // the copy at the end, so the cache is whole when the call's work is.
+    if (!k_new || !v_new) return fail(FVSR_EINVAL, "k_new and v_new are required");
+    if (!aligned16(k_new) || !aligned16(v_new)) return fail(FVSR_EINVAL, "k_new and v_new must be 16-byte aligned");
+    if (p->q_slices < 1 || (int)cache->pages.size() + p->q_slices > cache->capacity)
+        return fail(FVSR_EINVAL, "appending %d slices to %zu exceeds the capacity %d", p->q_slices, cache->pages.size(),
+                    cache->capacity);
+    if (!cache->side) return fail(FVSR_ECUDA, "the cache has no side stream");
+    KvPages dst{};
+    std::vector<int32_t> after;
+    choose_pages(cache, p->q_slices, &dst, &after);
+    const int64_t slice = cache->slice_bytes();
+    for (int t = 0; t < p->q_slices; ++t)
+        FVSR_CU(launch_pool(static_cast<const uint8_t*>(k_new) + t * slice, pp.dtype, d.s, (int)d.channels,
+                            cache->pk_arena + (int64_t)dst.page_block[t] * d.channels, nullptr, st),
+                "pool k_new launch");
+    FVSR_CU(cudaEventRecord(cache->fork, st), "fork record");
+    FVSR_CU(cudaStreamWaitEvent(cache->side, cache->fork, 0), "fork wait");
+    for (int t = 0; t < p->q_slices; ++t) {
+        const int64_t off = (int64_t)dst.page_block[t] * 128 * d.channels * d.elt;
+        FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(cache->k_arena) + off,
+                                static_cast<const uint8_t*>(k_new) + t * slice, slice, cudaMemcpyDeviceToDevice,
+                                cache->side),
+                "append copy (keys)");
+        FVSR_CU(cudaMemcpyAsync(static_cast<uint8_t*>(cache->v_arena) + off,
+                                static_cast<const uint8_t*>(v_new) + t * slice, slice, cudaMemcpyDeviceToDevice,
+                                cache->side),
+                "append copy (values)");
+    }
+    FVSR_CU(cudaEventRecord(cache->join, cache->side), "join record");
+    const size_t old_slices = cache->pages.size();
+    cache->pages = after;
+    const KvPages pages = cache->kv_pages();
+    KvPages attn_pages = pages;  // the appended slices marked fresh: block t·s + b of k_new / v_new
+    for (int t = 0; t < p->q_slices; ++t) attn_pages.page_block[old_slices + t] = kFreshPage | (t * d.s);
+    FreshKv fresh;
+    fresh.k = k_new;
+    fresh.v = v_new;
+    fresh.rows = (int64_t)p->q_slices * d.s * 128;
     FVSR_CU(launch_pool2(q, d.nq, w.pooled_q, nullptr, nullptr, 0, nullptr, pp.dtype, (int)d.channels, st, w.hist,
                          select_hist_bytes(d.heads, d.q_slices) / 4),
             "pool q launch");
     s = run_select(&pp, d, w.pooled_q, cache->pk_arena, pages, li, lc, nullptr, w.probs, w.hist, w.order, st);
-    if (s != FVSR_OK) return s;
-    s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(), pages, li, lc,
-                      out, st, 0, d.heads * d.nq, w.order);
+    if (s == FVSR_OK)
+        s = run_attention(&pp, d, q, cache->k_arena, cache->v_arena, (int64_t)cache->capacity * cache->page_rows(),
+                          attn_pages, li, lc, out, st, 0, d.heads * d.nq, w.order, OutRows{}, AttnSplit{}, fresh);
+    FVSR_CU(cudaStreamWaitEvent(st, cache->join, 0), "join wait");  // also on failure: the side work stays ordered
     if (s != FVSR_OK) return s;
     return fvsr_kv_cache_trim(cache);
 }

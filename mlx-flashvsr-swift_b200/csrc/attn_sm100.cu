@@ -84,7 +84,8 @@ struct AttnArgs {
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                           const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmKn,
+                           const __grid_constant__ CUtensorMap tmVn, const AttnArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
@@ -166,6 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tmQ);
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
+        prefetch_tmap(&tmKn);
+        prefetch_tmap(&tmVn);
     }
     const int32_t* glist = a.kidx ? a.kidx + (int64_t)item * a.nk + lo : nullptr;
     for (int j = threadIdx.x; j < cnt; j += kThreads) {
@@ -195,8 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j >= kKSlots && !wait(kBarSF + ks, (uint32_t)(j / kKSlots - 1))) return false;  // S_{j−3} done
                 const uint32_t dk = sbase + kOffK + (uint32_t)ks * kTileBytes;
                 mbar_expect_tx(bar(kBarKF + ks), kTileBytes);
-                tma_load_2d(dk, &tmK, x0, s_list[j] * kBlock, bar(kBarKF + ks));
-                tma_load_2d(dk + kBoxBytes, &tmK, x0 + 64, s_list[j] * kBlock, bar(kBarKF + ks));
+                const bool fresh = (s_list[j] & kFreshPage) != 0;  // a block of the slice being appended
+                const CUtensorMap* mk = fresh ? &tmKn : &tmK;
+                const int ky = (s_list[j] & ~kFreshPage) * kBlock;
+                tma_load_2d(dk, mk, x0, ky, bar(kBarKF + ks));
+                tma_load_2d(dk + kBoxBytes, mk, x0 + 64, ky, bar(kBarKF + ks));
                 return true;
             };
             auto load_v = [&](int j) -> bool {
@@ -204,8 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (j >= kVSlots && !wait(kBarPV + vs, (uint32_t)(j / kVSlots - 1))) return false;  // PV_{j−2} done
                 const uint32_t dv = sbase + kOffV + (uint32_t)vs * kTileBytes;
                 mbar_expect_tx(bar(kBarVF + vs), kTileBytes);
-                tma_load_2d(dv, &tmV, x0, s_list[j] * kBlock, bar(kBarVF + vs));
-                tma_load_2d(dv + kBoxBytes, &tmV, x0 + 64, s_list[j] * kBlock, bar(kBarVF + vs));
+                const bool fresh = (s_list[j] & kFreshPage) != 0;
+                const CUtensorMap* mv = fresh ? &tmVn : &tmV;
+                const int vy = (s_list[j] & ~kFreshPage) * kBlock;
+                tma_load_2d(dv, mv, x0, vy, bar(kBarVF + vs));
+                tma_load_2d(dv + kBoxBytes, mv, x0 + 64, vy, bar(kBarVF + vs));
                 return true;
             };
             bool ok = load_k(0) && (cnt < 2 || load_k(1));
@@ -419,14 +428,21 @@ size_t attn_bf16_smem_bytes(int nk) { return 1024 + kOffList + sizeof(int32_t) *
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
                              int item_begin, int item_count, const int32_t* order, cudaStream_t st, OutRows rows,
-                             AttnSplit split) {
+                             AttnSplit split, FreshKv fresh) {
     if (item_count <= 0) return cudaSuccess;
-    CUtensorMap mq, mk, mv;
+    CUtensorMap mq, mk, mv, mkn, mvn;
     const int64_t channels = (int64_t)heads * kD;
     const int64_t q_rows = (int64_t)(rows.q_blocks > 0 ? rows.q_blocks : nq) * kBlock;
     if (!make_tile_map(&mq, q, q_rows, channels) || !make_tile_map(&mk, k, kv_rows, channels) ||
         !make_tile_map(&mv, v, kv_rows, channels))
         return cudaErrorInvalidValue;
+    if (fresh.k) {
+        if (!make_tile_map(&mkn, fresh.k, fresh.rows, channels) || !make_tile_map(&mvn, fresh.v, fresh.rows, channels))
+            return cudaErrorInvalidValue;
+    } else {  // no page is marked fresh: the maps are never read
+        mkn = mk;
+        mvn = mv;
+    }
     const size_t smem = attn_bf16_smem_bytes(nk);
     cudaError_t e = cudaFuncSetAttribute(attn_bf16_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -443,7 +459,7 @@ cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_
     a.pages = pages;
     a.rows = rows;
     a.split = split;
-    return launch_pdl(attn_bf16_sm100_kernel, dim3(item_count), dim3(kThreads), smem, st, mq, mk, mv, a);
+    return launch_pdl(attn_bf16_sm100_kernel, dim3(item_count), dim3(kThreads), smem, st, mq, mk, mv, mkn, mvn, a);
 }
 
 namespace {

@@ -21,6 +21,15 @@ struct KvPages {
 __host__ __device__ inline int32_t kv_phys_block(const KvPages& pg, int32_t j) {
     return pg.page_block[j / pg.s] + j % pg.s;
 }
+// A page entry with this bit set names a slice being appended by the same call: the bf16 attention reads its key and
+// value blocks (the entry without the bit, plus the block's index in the slice) from the caller's k_new / v_new
+// (FreshKv) instead of the arena, so the copy into the arena can run beside it.
+constexpr int32_t kFreshPage = 1 << 30;
+struct FreshKv {
+    const void* k = nullptr;  // (rows, channels) window order, or NULL: no fresh pages
+    const void* v = nullptr;
+    int64_t rows = 0;
+};
 
 // Token r of window (query block) w on the (F, 8·bh, 8·bw) patch grid (windowPartition, DiT.swift:113-118): windows
 // ordered (nf, nh, nw), tokens inside a window (wf, wh, ww). token_row gives the token-order row (the layout
@@ -115,7 +124,7 @@ struct AttnSplit {
 cudaError_t launch_attn_bf16(const void* q, const void* k, const void* v, int64_t kv_rows, const KvPages& pages,
                              int heads, int nq, int nk, const int32_t* kidx, const int32_t* kcnt, void* out,
                              int item_begin, int item_count, const int32_t* order, cudaStream_t st,
-                             OutRows rows = {}, AttnSplit split = {});
+                             OutRows rows = {}, AttnSplit split = {}, FreshKv fresh = {});
 // The q/k/v side of one layer from the linear outputs (prepare.cu). Token grid (2·q_slices, 8·bh, 8·bw); nq windows.
 struct PrepArgs {
     const void* x[3];        // q, k, v linear outputs, token order (L, C)
