@@ -2,11 +2,13 @@
 
 Metric: block-sparse attention effective TFLOP/s — 4·128³ FLOP per kept (query block, key block,
 head) triple, over the whole path's device time (pooling + selection + attention) — plus ms per 30-layer chunk.
-Workload at N=1: config 3 (1920×1152 chunk: 12 heads, 135 × 405 blocks, R = 11, keep 30 %), a step = one chunk =
-30 layer calls, each on fresh seeded Q/K/V resident in HBM (371 MB per layer, larger than L2, so no flush is needed).
-N > 1 (torchrun, one process per GPU): independent config-3 streams, one per GPU (config 5's throughput variant);
-no data-path collective, weak scaling, time = max over ranks. --config 5 (or --shard) instead splits one config's
-(head, query block) items across the ranks: strong scaling, still no data-path collective (heads are independent).
+Workload (default, every N): config 3 (1920×1152 chunk: 12 heads, 135 × 405 blocks, R = 11, keep 30 %) as one
+steady-state streamed chunk: a step = 30 DiT layers, each with its window cache of 2 earlier slices and fresh seeded
+q / k_new / v_new resident in HBM (per layer 159 MB of chunk data + 212 MB of cache read, larger than L2, so no flush
+is needed). N > 1 (torchrun, one process per GPU): the same chunk split by query blocks, each rank pooling its shard,
+NCCL all-gathers of the pooled rows and of the current slice's K/V inside the timed region; strong scaling, time =
+max over ranks. --fresh: 30 independent layer calls on fresh full Q/K/V. --shard: one config's (head, query block)
+items split across the ranks with no data-path collective; --replicas: one independent chunk per GPU (weak scaling).
 
 --impl reference: the CPU baseline arm — the reference's Swift/MLX path cannot run off Apple hardware, so this times
 the CPU oracle (a C/OpenMP restatement of the reference's selection and block-masked attention) on all host threads,
@@ -644,6 +646,33 @@ def run_chunk(args):
     torch.cuda.synchronize()
     flops = 4.0 * 128 ** 3 * kept
 
+    # the collective this partition adds, alone: the two K/V all-gathers of one layer (the slice's shards into a
+    # page-sized buffer) on the communication stream, back to back, CUDA events on that stream, max over ranks
+    gather_ms = None
+    if comm is not None:
+        kdst = torch.empty((world * ks[0].shape[0], g.channels), dtype=ks[0].dtype, device=dev)
+        vdst = torch.empty_like(kdst)
+        cs = sc.comm_stream
+
+        def kv_gather_once():
+            comm.group_start()
+            comm.all_gather(ks[0], kdst, cs)
+            comm.all_gather(vs[0], vdst, cs)
+            comm.group_end()
+
+        for _ in range(3):
+            kv_gather_once()
+        torch.cuda.synchronize()
+        ranks.barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(cs)
+        for _ in range(20):
+            kv_gather_once()
+        c1.record(cs)
+        torch.cuda.synchronize()
+        gather_ms = ranks.max_over_ranks(c0.elapsed_time(c1) / 20, dev)
+        del kdst, vdst
+
     # the dominant kernel alone: the attention of whole fresh layers (one GPU's problem), CUDA events on its stream;
     # then the same launches back to back from a graph (the power-capped rate the step sees)
     L = pkg.lib()
@@ -782,9 +811,17 @@ def run_chunk(args):
                              f"{2 * kv_len * srows * g.channels * 2 / 1e6:.0f} MB of cache read (> L2), no flush",
                        "launch": launch, "parallelism": par},
             "ms_per_layer": ms / layers,
-            # the attention of a layer back to back in a graph (as in the step, under the power cap) and the rest
-            "breakdown_ms_per_layer": ({"attention back to back": att_b2b, "rest (append, pooling, selection, "
-                                        "collectives, gaps)": ms / layers - att_b2b} if att_b2b else None),
+            # N = 1: the attention of a layer back to back in a graph (as in the step, under the power cap) and the
+            # rest. N > 1: the rank's layer (max over ranks), the K/V all-gather alone, and the one-GPU references
+            "breakdown_ms_per_layer": (
+                ({"attention back to back": att_b2b, "rest (append, pooling, selection, gaps)": ms / layers - att_b2b}
+                 if world == 1 else
+                 {"layer (max over ranks)": ms / layers,
+                  "kv_all_gather_alone": gather_ms,
+                  "kv_all_gather_bytes_received_per_rank": 2 * (world - 1) * ks[0].numel() * ks[0].element_size(),
+                  "one_gpu_attention_of_the_whole_layer_back_to_back": att_b2b,
+                  "ideal_layer (one-GPU attention / N)": att_b2b / world})
+                if att_b2b else None),
             "chunk_frac_of_sustained_peak": (value / world / sustained) if sustained and cfg.dtype == "bf16" else None,
             "roofline": (
                 {"kernel": "attn_bf16_sm100_kernel", "bound": "tensor", "achieved": att_tflops, "peak": peak,
@@ -800,9 +837,9 @@ def run_chunk(args):
                  "ms_alone_per_layer": att_avg, "traffic": None,
                  "timed": f"the attention of {len(att_ms)} whole fresh layers alone, CUDA events"}),
             "clocks": clk,
-            # per layer: N = 1 append (+ key pooling), query pooling, selection, attention; N > 1 two pooling
-            # launches, selection, attention (the collectives are NCCL's kernels, not counted)
-            "gpu_launches": 4 * layers * args.steps,
+            # per layer: N = 1 key pooling (the append), query pooling, selection, attention; N > 1 two pooling
+            # launches, selection, attention (two launches when split around the gather; NCCL's kernels not counted)
+            "gpu_launches": (4 if world == 1 or sc.partial is None else 5) * layers * args.steps,
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:
@@ -1330,6 +1367,8 @@ def main():
                     help="split the config's (head, query block) items across the ranks (default for config 5)")
     ap.add_argument("--replicas", dest="shard", action="store_false",
                     help="one independent copy of the config per rank (default except for config 5)")
+    ap.add_argument("--chunk", action="store_true",
+                    help="the streamed-chunk step (query blocks split across ranks at N > 1) for any config, 5 included")
     ap.add_argument("--fresh", action="store_true",
                     help="30 independent layer calls on fresh full Q/K/V (no cache) instead of a streamed chunk")
     ap.add_argument("--roofline-layers", type=int, default=8,
@@ -1369,7 +1408,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.fresh or args.shard is not None or args.as_rank or args.config == 5:
+    elif not args.chunk and (args.fresh or args.shard is not None or args.as_rank or args.config == 5):
         run_ours(args)
     else:
         run_chunk(args)

@@ -546,8 +546,9 @@ __device__ __forceinline__ void finish_rows(const SelArgs& a, int64_t r0, int64_
 // the segment with a longer key list, or an equal one and a smaller id; empty items rank after all non-empty ones, by
 // id. All threads of the group call it; sc (4096 words) and cnt (4 words) are shared scratch of the group.
 __device__ void order_segment(const int32_t* __restrict__ kcnt, int nq, int item_begin, int item_count, int q0, int q1,
-                              int32_t* __restrict__ order, int seg, int32_t* __restrict__ sc, int* __restrict__ cnt,
-                              const Grp& g) {
+                              int32_t* __restrict__ order, int seg, int32_t* sc, int* cnt, const Grp& g) {
+    // sc and cnt are shared memory that several threads write and read across g.sync(): not __restrict__, so the
+    // compiler keeps their accesses on their side of the inline-asm barrier
     const int h = item_begin / nq + seg;
     const int s0 = max(item_begin, h * nq + q0), s1 = min(item_begin + item_count, h * nq + q1);
     const int n = s1 - s0;
