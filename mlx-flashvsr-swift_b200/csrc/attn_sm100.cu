@@ -62,7 +62,8 @@ constexpr uint32_t kOffBar = kOffV + kVSlots * kTileBytes;      // barriers
 // because the next completion on it needs the tile the producer has not loaded yet.
 static_assert(kKSlots == kSBufs && kVSlots == 2, "ring slots are released through the S and PV barriers");
 constexpr int kBarQ = 0, kBarKF = 1, kBarVF = kBarKF + kKSlots, kBarSF = kBarVF + kVSlots, kBarPF = kBarSF + kSBufs,
-              kBarPV = kBarPF + kSBufs, kBarM = kBarPV + 2, kBarFin = kBarM + 2, kNumBars = kBarFin + 1;
+              kBarPV = kBarPF + kSBufs, kBarM = kBarPV + 2, kBarFin = kBarM + 2, kBarDone = kBarFin + 1,
+              kNumBars = kBarDone + 1;
 constexpr uint32_t kOffTmemSlot = kOffBar + 8 * kNumBars;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kOffM = (kOffAbort + 4 + 15) & ~15u;         // running max handoff: [2 parities][128] f32
@@ -160,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar(kBarM + b), 128);
         }
         mbar_init(bar(kBarFin), 256);
+        mbar_init(bar(kBarDone), 1);
         *abort_word = 0;
         fence_mbar_init();
     }
@@ -256,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_ts(tmem + kColO, pa + 8u * (uint32_t)kk, vd + (uint64_t)(kk * (2048 >> 4)), kIdescPV,
                            (j > 0 || kk > 0) ? 1u : 0u);
                 mma_commit(bar(kBarPV + (j & 1)));
+                if (j == cnt - 1) mma_commit(bar(kBarDone));  // every MMA done: a single-phase barrier
             }
         }
     } else {
@@ -350,7 +353,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         fin[(st * 2 + 1) * 128 + r] = mref;
         mbar_arrive(bar(kBarFin));
         if (ok) ok = wait_warp(kBarFin, 0);
-        if (ok && wait_warp(kBarPV + ((cnt - 1) & 1), (uint32_t)((cnt - 1) >> 1))) {
+        // the last PV on a single-phase barrier: a parity wait for PV_{cnt−1} on the alternating PV barriers would pass
+        // early if PV_{cnt−3} had not completed yet
+        if (ok && wait_warp(kBarDone, 0)) {
             tc_fence_after();
             const float l0 = fin[r], m0 = fin[128 + r], l1 = fin[256 + r], m1 = fin[384 + r];
             const float mf = fmaxf(m0, m1);
