@@ -539,8 +539,8 @@ def run_chunk(args):
     shard_mod = importlib.import_module("fvsr_b200.shard")
     info = ranks.rank_info()
     world, rank, local = info.world, info.rank, info.local
-    if world > 1:  # NCCL's kernels must fit in the SMs the selection leaves to the gather beside it
-        os.environ.setdefault("NCCL_MAX_CTAS", "32")
+    if world > 1 and args.spare_sms > 0:  # NCCL's kernels must fit in the SMs the selection leaves to the gather
+        os.environ.setdefault("NCCL_MAX_CTAS", str(args.spare_sms))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     ranks.init(info, "nccl", timeout_s=120, device=dev)
@@ -555,7 +555,7 @@ def run_chunk(args):
     if world > 1:
         nccl = importlib.import_module("fvsr_b200.nccl")
         comm = nccl.Comm(rank, world, dev)
-    sc = shard_mod.ShardedChunk(pkg, g, kv_len, layers, rank, world, comm, dev, spare_sms=32)
+    sc = shard_mod.ShardedChunk(pkg, g, kv_len, layers, rank, world, comm, dev, spare_sms=args.spare_sms)
     sh = sc.shard
     stream = torch.cuda.current_stream()
     # per layer: the seeded full tensors of the one-GPU problem (q of the chunk, K/V of cache ⊕ current), of which
@@ -1369,6 +1369,9 @@ def main():
                     help="one independent copy of the config per rank (default except for config 5)")
     ap.add_argument("--chunk", action="store_true",
                     help="the streamed-chunk step (query blocks split across ranks at N > 1) for any config, 5 included")
+    ap.add_argument("--spare-sms", type=int, default=32,
+                    help="chunk mode, N > 1: SMs the selection leaves to the K/V gather started before it (0: the gather "
+                         "starts after the selection)")
     ap.add_argument("--fresh", action="store_true",
                     help="30 independent layer calls on fresh full Q/K/V (no cache) instead of a streamed chunk")
     ap.add_argument("--roofline-layers", type=int, default=8,
